@@ -1,0 +1,222 @@
+/*
+ * jdgpu.h — C ABI of the B200 decode engine for janus.DoE.
+ *
+ * Two groups of entry points:
+ *   jd_*   host-side model code: the reference's structs, weight generation and GGUF
+ *          formats (no CUDA).  These replace the reference's Config / ModelW / GGUFHost
+ *          handling (janusdoe.c:136-185, 703-776, 1781-1961, 2745-3048).
+ *   jdg_*  the GPU engine: upload a model, then run decode steps on sm_100a kernels.
+ *          These replace the reference's token loop (forward_token janusdoe.c:879,
+ *          parliament_elect janusdoe.c:779, sample janusdoe.c:3637, gguf_host_forward
+ *          janusdoe.c:3160, host_parliament_elect janusdoe.c:3054, jd_qmatvec
+ *          janusdoe.c:2685).
+ *
+ * Conventions: every call returns an int status (JD_OK = 0, negative on error) and
+ * never aborts; jdg_last_error() describes the last failure on a context.  All pointer
+ * arguments are host pointers unless the name ends in _dev.  One host thread drives a
+ * context; each engine owns its device buffers and runs on its own CUDA stream.
+ */
+#ifndef JDGPU_H
+#define JDGPU_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define JD_MAX_EXPERTS 16 /* janusdoe.c:116 */
+#define JD_MAX_LAYERS 32  /* janusdoe.c:117, 2533 */
+
+enum {
+    JD_OK = 0,
+    JD_EINVAL = -1,       /* bad argument or shape */
+    JD_ENOMEM = -2,       /* host or device allocation failed */
+    JD_ECUDA = -3,        /* a CUDA call failed */
+    JD_EFORMAT = -4,      /* malformed or truncated file */
+    JD_EUNSUPPORTED = -5, /* packed dtype without a kernel (janusdoe.c:2739 aborts here) */
+    JD_EIO = -6,          /* open/read/write failed */
+    JD_ESTATE = -7,       /* call out of order, or device-side check failed */
+    JD_ECOMM = -8         /* NCCL failure */
+};
+
+/* GGUF tensor dtypes used by the host path (janusdoe.c:2543) */
+enum { JD_F32 = 0, JD_F16 = 1, JD_Q4_0 = 2, JD_Q5_0 = 6, JD_Q8_0 = 8, JD_Q4_K = 12, JD_Q6_K = 14 };
+
+/* ------------------------------------------------------------------------------------
+ * Own model ("organism").  Layout mirrors Config (janusdoe.c:136-149), LayerW +
+ * Parliament (janusdoe.c:625-634, 708-713) and ModelW (janusdoe.c:715-719).  Weights are
+ * row-major f32 [out][in] as in the reference; dead expert slots have NULL pointers
+ * and alive = 0.
+ * ---------------------------------------------------------------------------------- */
+typedef struct {
+    int depth, dim, n_heads, n_kv_heads, head_dim, hidden_dim, vocab_size, seq_len;
+    float norm_eps, rope_theta, attn_clamp;
+    int active_depth, initial_experts;
+} jd_config;
+
+typedef struct {
+    float *attn_norm, *ffn_norm, *wq, *wk, *wv, *wo, *w_vote; /* w_vote: [16][dim] */
+    float *w_gate[JD_MAX_EXPERTS], *w_up[JD_MAX_EXPERTS], *w_down[JD_MAX_EXPERTS];
+    int alive[JD_MAX_EXPERTS];
+    float consensus;   /* Parliament.consensus: the EMA a fresh sequence starts from */
+    float temperature; /* Parliament.temperature (<= 0.05 means 1) */
+} jd_layer;
+
+typedef struct {
+    jd_config c;
+    float *tok_emb, *output, *output_norm;
+    jd_layer layers[JD_MAX_LAYERS];
+} jd_model;
+
+/* config_from_depth (janusdoe.c:151-185); vocab_size is set to 258 + merges */
+int jd_config_from_depth(int depth, jd_config *c);
+/* allocate a model of config c the way init_weights shapes it (janusdoe.c:744-776) */
+int jd_model_alloc(jd_model *m, const jd_config *c);
+void jd_model_free(jd_model *m);
+/* Synthetic weights: xorshift state = splitmix64(seed); every tensor is overwritten with
+ * rand_normal()*std (janusdoe.c:190-193) in the order tok_emb, output, then per layer wq,
+ * wk, wv, wo, w_vote, experts 0..initial-1 (gate, up, down); norms stay 1.  draw_masks:
+ * per layer, a target alive count in [max(2, n-3), n] is drawn and slots are killed. */
+int jd_model_fill_seeded(jd_model *m, uint64_t seed, float std, int draw_masks);
+/* export_gguf (janusdoe.c:1781-1826): f32, alive experts only */
+int jd_model_export_gguf(const jd_model *m, const char *path);
+/* load_own_gguf (janusdoe.c:1832-1961): m must be allocated with the file's config;
+ * experts present in the file are revived, absent ones are killed. */
+int jd_model_load_gguf(jd_model *m, const char *path);
+
+/* ------------------------------------------------------------------------------------
+ * Host GGUF model.  Mirrors GGUFHost (janusdoe.c:2764-2800): packed weights point into
+ * a read-only mmap, tok_emb and norms are dequantised to f32 at load (janusdoe.c:2817),
+ * and the LoRA parliament has per-layer experts A [dim][rank], B [rank][dim].
+ * ---------------------------------------------------------------------------------- */
+typedef struct {
+    const void *wq, *wk, *wv, *wo, *gate, *up, *down;
+    int wq_dt, wk_dt, wv_dt, wo_dt, gate_dt, up_dt, down_dt;
+    const float *attn_norm, *ffn_norm; /* NULL = all ones */
+} jd_host_layer;
+
+typedef struct {
+    int n_layers, dim, hidden, n_heads, n_kv_heads, head_dim, vocab;
+    float rope_theta, rms_eps;
+    int rope_norm; /* 1 NORM (2i,2i+1), 0 NEOX (i,i+hd/2): janusdoe.c:3148-3156 */
+    char arch[64];
+    int bos, eos;
+    const float *tok_emb; /* [vocab][dim] f32 */
+    const void *output;
+    int output_dt;
+    const float *output_norm;
+    jd_host_layer layers[JD_MAX_LAYERS];
+    int lora_rank;
+    float lora_alpha;                                    /* 0.1 (janusdoe.c:2841) */
+    float *w_vote[JD_MAX_LAYERS];                        /* [16][dim] */
+    float *A[JD_MAX_LAYERS][JD_MAX_EXPERTS];             /* [dim][rank] */
+    float *B[JD_MAX_LAYERS][JD_MAX_EXPERTS];             /* [rank][dim] */
+    int alive[JD_MAX_LAYERS][JD_MAX_EXPERTS];
+    float consensus0[JD_MAX_LAYERS];                     /* 0.5 (janusdoe.c:3026) */
+    float attention_bias[JD_MAX_LAYERS], layer_focus[JD_MAX_LAYERS]; /* 0 and 1 */
+    char **vocab_tokens; /* tokenizer.ggml.tokens, NULL if absent */
+    int n_vocab_tokens;
+    void *priv;          /* loader bookkeeping (mmap, dequant buffers) */
+} jd_host_model;
+
+/* gguf_host_load (janusdoe.c:2837-3048). rope_override: -1 arch heuristic, 0 NEOX, 1 NORM.
+ * The LoRA parliament is allocated with lora_rank and 4 alive zero experts, consensus 0.5. */
+int jd_host_load_gguf(jd_host_model *h, const char *path, int rope_override, int lora_rank);
+void jd_host_free(jd_host_model *h); /* gguf_host_free (janusdoe.c:3449-3467) */
+/* Synthetic LoRA parliament: state = splitmix64(seed); per layer 16 vote rows uniform
+ * (2u-1)*vote_amp, then experts e < n_alive draw A then B as rand_normal()*ab_std. */
+int jd_host_lora_seed(jd_host_model *h, uint64_t seed, int n_alive, float ab_std, float vote_amp);
+/* LoRA sidecar "JDLORA01": L, D, rank, alive mask, w_vote, A, B (f32 little-endian).
+ * The reference re-draws its LoRA at every load; the sidecar lets runs share one. */
+int jd_host_lora_save(const jd_host_model *h, const char *path);
+int jd_host_lora_load(jd_host_model *h, const char *path);
+/* Write a synthetic llama-family GGUF v3 (the format gguf_host_load reads): weights
+ * N(0, std) quantised per block to dtype (JD_Q8_0 or JD_Q4_K; norms f32 = 1), metadata
+ * keys as the loader matches them.  Tensors are generated in parallel blocks from
+ * splitmix64(seed ^ tensor index ^ block index); threads <= 0 uses all cores. */
+int jd_gguf_write_synthetic(const char *path, const char *arch, int n_layers, int dim, int hidden,
+                            int n_heads, int n_kv_heads, int vocab, float rope_theta, float rms_eps,
+                            int dtype, uint64_t seed, float std, int threads);
+
+/* ------------------------------------------------------------------------------------
+ * GPU engine.
+ * ---------------------------------------------------------------------------------- */
+typedef struct jdg_ctx jdg_ctx;
+typedef struct jdg_engine jdg_engine;
+
+/* Per-step election trace, written for every (sequence, layer): k, elected slots in
+ * election order, their softmax weights and the consensus EMA after the update.
+ * Arrays are [B][n_layers] (k, ema) and [B][n_layers][16] (sel, w). */
+typedef struct {
+    int *k;
+    int *sel;
+    float *w;
+    float *ema;
+} jdg_trace;
+
+int jdg_open(int device, jdg_ctx **out);
+void jdg_close(jdg_ctx *ctx);
+const char *jdg_last_error(jdg_ctx *ctx);
+int jdg_device_count(int *n);
+
+/* Upload an own model (alive experts, alive mask, per-layer consensus and temperature).
+ * The host model stays the source of truth; max_batch sequence slots are allocated, each
+ * with KV [n_layers][seq_len][kv_dim] f32 and its own consensus EMA per layer. */
+int jdg_own_upload(jdg_ctx *ctx, const jd_model *m, int max_batch, jdg_engine **out);
+/* Upload a host GGUF model: packed bytes copied as they are, LoRA parliament in f32.
+ * KV holds max_seq positions per slot. */
+int jdg_host_upload(jdg_ctx *ctx, const jd_host_model *h, int max_batch, int max_seq, jdg_engine **out);
+/* Tensor-parallel host upload: this process holds rank `rank` of `world`; nccl_id is the
+ * 128-byte ncclUniqueId created by rank 0 (jdg_comm_unique_id) and shared by the caller. */
+int jdg_comm_unique_id(void *nccl_id_128);
+int jdg_host_upload_tp(jdg_ctx *ctx, const jd_host_model *h, int max_batch, int max_seq, int rank, int world,
+                       const void *nccl_id_128, jdg_engine **out);
+void jdg_engine_free(jdg_engine *e);
+
+/* Sampling: temperature <= 0 is greedy argmax (janusdoe.c:3637, 3374); otherwise
+ * sample() with temperature and top_k and each sequence's own xorshift state. */
+int jdg_set_sampling(jdg_engine *e, float temperature, int top_k);
+/* Fresh sequence in slot `slot` (-1: all): zero its KV, restart its EMAs (chat(),
+ * janusdoe.c:3656-3657), clear its prompt. */
+int jdg_reset(jdg_engine *e, int slot);
+/* Give slots 0..B-1 a prompt: tokens[b*P + i], i < len[b] <= P.  The next run feeds the
+ * prompt token by token (sequential prefill, janusdoe.c:3660) and then generates. */
+int jdg_set_prompt(jdg_engine *e, int B, const int *tokens, int P, const int *len, const uint64_t *rng);
+/* Run n decode steps for slots 0..B-1 entirely on the device: each step forwards the
+ * current token at the current position, then picks the next one (the prompt's while
+ * it lasts, else sampled/greedy).  Generated tokens land in the history buffer. */
+int jdg_run(jdg_engine *e, int B, int n_steps);
+/* Read back: current token and position per slot, and the last n history entries. */
+int jdg_get_state(jdg_engine *e, int B, int *tok, int *pos);
+int jdg_get_history(jdg_engine *e, int B, int n, int *tokens);
+/* One decode step through host buffers: upload tok/pos (and rng if given), forward,
+ * pick, download next_tok (and rng).  logits [B][vocab] and trace are optional. */
+int jdg_step(jdg_engine *e, int B, const int *tok, const int *pos, uint64_t *rng, int *next_tok,
+             float *logits, jdg_trace *trace);
+/* Logits and trace of the last step for slots 0..B-1. */
+int jdg_get_logits(jdg_engine *e, int B, float *logits);
+int jdg_get_trace(jdg_engine *e, int B, jdg_trace *trace);
+/* Timing: device time of the last jdg_run in milliseconds (CUDA events on the engine's stream). */
+int jdg_last_run_ms(jdg_engine *e, float *ms);
+/* Per-kernel device time of one more step (events around each launch of a step). */
+int jdg_profile_step(jdg_engine *e, int B, float *ms_by_kernel, int max_kernels, int *n_kernels,
+                     const char **names);
+/* Counts of this library's kernel launches since the engine was created. */
+int jdg_launch_count(jdg_engine *e, long long *n);
+
+/* Packed GEMV/GEMM on the device through host buffers: out[b][r] = W[r][:] . x[b][:],
+ * W packed as dtype dt (JD_F32, JD_Q8_0, JD_Q4_K), B rows of x.  Mirrors jd_qmatvec
+ * (janusdoe.c:2685): JD_EUNSUPPORTED where the reference returns -1. */
+int jdg_qmatvec(jdg_ctx *ctx, float *out, const void *W, int dt, const float *x, int r, int c, int B);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,774 @@
+// jdg_engine.cu — the C ABI of the B200 decode engine (include/jdgpu.h): contexts, weight
+// upload, per-sequence state, the decode step as a sequence of sm_100a kernels captured in
+// a CUDA graph per batch size, and the device-resident decode loop.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/jdgpu.h"
+#include "jdg_engine.h"
+#include "jdg_kernels.cuh"
+
+using namespace jdg;
+
+struct jdg_ctx {
+    int device;
+    char err[1024];
+};
+
+static thread_local char g_tls_err[1024];
+
+void jdg_set_err(jdg_ctx *c, const char *fmt, ...) {
+    char *dst = c ? c->err : g_tls_err;
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(dst, 1024, fmt, ap);
+    va_end(ap);
+}
+
+#define CK(call)                                                                                          \
+    do {                                                                                                  \
+        cudaError_t _e = (call);                                                                          \
+        if (_e != cudaSuccess) {                                                                          \
+            jdg_set_err(E_CTX, "%s failed: %s (%s:%d)", #call, cudaGetErrorString(_e), __FILE__, __LINE__); \
+            return JD_ECUDA;                                                                              \
+        }                                                                                                 \
+    } while (0)
+
+// ------------------------------------------------------------------------------------
+extern "C" int jdg_device_count(int *n) {
+    if (!n) return JD_EINVAL;
+    cudaError_t e = cudaGetDeviceCount(n);
+    if (e != cudaSuccess) {
+        *n = 0;
+        return JD_ECUDA;
+    }
+    return JD_OK;
+}
+
+extern "C" int jdg_open(int device, jdg_ctx **out) {
+    if (!out) return JD_EINVAL;
+    *out = nullptr;
+    jdg_ctx *c = (jdg_ctx *)calloc(1, sizeof(jdg_ctx));
+    if (!c) return JD_ENOMEM;
+    c->device = device;
+#define E_CTX c
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+        snprintf(g_tls_err, sizeof(g_tls_err), "no CUDA device %d (count %d)", device, n);
+        free(c);
+        return JD_ECUDA;
+    }
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) {
+        snprintf(g_tls_err, sizeof(g_tls_err), "cudaSetDevice(%d): %s", device, cudaGetErrorString(e));
+        free(c);
+        return JD_ECUDA;
+    }
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) == cudaSuccess && prop.major < 10) {
+        snprintf(g_tls_err, sizeof(g_tls_err), "device %d is sm_%d%d; this library is built for sm_100a", device,
+                 prop.major, prop.minor);
+        free(c);
+        return JD_EUNSUPPORTED;
+    }
+#undef E_CTX
+    *out = c;
+    return JD_OK;
+}
+
+extern "C" void jdg_close(jdg_ctx *c) { free(c); }
+
+extern "C" const char *jdg_last_error(jdg_ctx *c) { return c ? c->err : g_tls_err; }
+
+int jdg_ctx_device(jdg_ctx *c) { return c->device; }
+
+// ------------------------------------------------------------------------------------
+// Device arena: one allocation, 256-byte aligned sub-buffers.
+struct Arena {
+    std::vector<std::pair<size_t *, size_t>> req;
+};
+
+static size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+#define E_CTX (e->ctx)
+
+static int dev_alloc(jdg_engine *e, void **p, size_t bytes) {
+    cudaError_t r = cudaMalloc(p, bytes ? bytes : 256);
+    if (r != cudaSuccess) {
+        jdg_set_err(e->ctx, "cudaMalloc(%zu) failed: %s", bytes, cudaGetErrorString(r));
+        return JD_ENOMEM;
+    }
+    e->allocs.push_back(*p);
+    return JD_OK;
+}
+#define DALLOC(ptr, bytes)                                              \
+    do {                                                                \
+        int _r = dev_alloc(e, (void **)&(ptr), (size_t)(bytes));        \
+        if (_r != JD_OK) return _r;                                     \
+    } while (0)
+
+static int h2d(jdg_engine *e, void *dst, const void *src, size_t bytes) {
+    CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, e->st));
+    return JD_OK;
+}
+
+// common state buffers: tokens, positions, prompts, history, RNG, EMA, trace, election
+int jdg_alloc_state(jdg_engine *e) {
+    const int B = e->B_max, L = e->L;
+    DALLOC(e->tok, B * 4);
+    DALLOC(e->pos, B * 4);
+    DALLOC(e->plen, B * 4);
+    DALLOC(e->next_out, B * 4);
+    DALLOC(e->hist_n, B * 4);
+    DALLOC(e->rng, B * 8);
+    e->Pmax = e->max_seq;
+    e->Hmax = e->max_seq;
+    DALLOC(e->prompt, (size_t)B * e->Pmax * 4);
+    DALLOC(e->hist, (size_t)B * e->Hmax * 4);
+    DALLOC(e->consensus, (size_t)B * L * 4);
+    DALLOC(e->kcnt, B * 4);
+    DALLOC(e->sel, (size_t)B * kMaxE * 4);
+    DALLOC(e->selw, (size_t)B * kMaxE * 4);
+    DALLOC(e->rcnt, kMaxE * 4);
+    DALLOC(e->ridx, (size_t)kMaxE * B * 4);
+    DALLOC(e->pairrow, (size_t)B * kMaxE * 4);
+    DALLOC(e->tr_k, (size_t)B * L * 4);
+    DALLOC(e->tr_ema, (size_t)B * L * 4);
+    DALLOC(e->tr_sel, (size_t)B * L * kMaxE * 4);
+    DALLOC(e->tr_w, (size_t)B * L * kMaxE * 4);
+    DALLOC(e->err, 4);
+    CK(cudaMemsetAsync(e->err, 0, 4, e->st));
+    CK(cudaMemsetAsync(e->tok, 0, B * 4, e->st));
+    CK(cudaMemsetAsync(e->pos, 0, B * 4, e->st));
+    CK(cudaMemsetAsync(e->plen, 0, B * 4, e->st));
+    CK(cudaMemsetAsync(e->hist_n, 0, B * 4, e->st));
+    CK(cudaMemsetAsync(e->rng, 0, B * 8, e->st));
+    CK(cudaMemsetAsync(e->tr_k, 0, (size_t)B * L * 4, e->st));
+    return JD_OK;
+}
+
+static int engine_new(jdg_ctx *ctx, int kind, jdg_engine **out) {
+    jdg_engine *e = new (std::nothrow) jdg_engine();
+    if (!e) return JD_ENOMEM;
+    e->ctx = ctx;
+    e->kind = kind;
+    e->temp = 0.f;
+    e->top_k = 0;
+    cudaError_t r = cudaSetDevice(ctx->device);
+    if (r == cudaSuccess) r = cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking);
+    if (r == cudaSuccess) r = cudaEventCreate(&e->ev0);
+    if (r == cudaSuccess) r = cudaEventCreate(&e->ev1);
+    if (r != cudaSuccess) {
+        jdg_set_err(ctx, "stream/event create: %s", cudaGetErrorString(r));
+        delete e;
+        return JD_ECUDA;
+    }
+    *out = e;
+    return JD_OK;
+}
+
+// ------------------------------------------------------------------------------------
+// Own-model upload.  Device layout per layer: wqkv = [wq; wk; wv] (rows), wo, w_vote,
+// and per alive expert gu = interleaved rows (gate_i, up_i) [2H][D] and down [D][H].
+extern "C" int jdg_own_upload(jdg_ctx *ctx, const jd_model *m, int max_batch, jdg_engine **out) {
+    if (!ctx || !m || !out || !m->tok_emb || max_batch < 1 || max_batch > 4096) {
+        if (ctx) jdg_set_err(ctx, "jdg_own_upload: bad arguments");
+        return JD_EINVAL;
+    }
+    const jd_config &c = m->c;
+    if (c.depth < 1 || c.depth > JD_MAX_LAYERS || c.n_kv_heads < 1 || c.n_heads % c.n_kv_heads ||
+        (c.head_dim != 64 && c.head_dim != 128) || c.n_heads / c.n_kv_heads > kMaxHG || c.dim % 16 ||
+        c.hidden_dim % 16 || (c.n_heads * c.head_dim) % 16 || c.seq_len < 1) {
+        jdg_set_err(ctx, "jdg_own_upload: unsupported config (dim %d heads %d/%d hd %d hidden %d)", c.dim, c.n_heads,
+                    c.n_kv_heads, c.head_dim, c.hidden_dim);
+        return JD_EUNSUPPORTED;
+    }
+    jdg_engine *e = nullptr;
+    int rc = engine_new(ctx, 0, &e);
+    if (rc != JD_OK) return rc;
+    rc = jdg_own_upload_impl(e, m, max_batch);
+    if (rc != JD_OK) {
+        jdg_engine_free(e);
+        return rc;
+    }
+    *out = e;
+    return JD_OK;
+}
+
+int jdg_own_upload_impl(jdg_engine *e, const jd_model *m, int max_batch) {
+    const jd_config &c = m->c;
+    e->B_max = max_batch;
+    e->L = (c.active_depth > 0 && c.active_depth <= c.depth) ? c.active_depth : c.depth;
+    e->D = c.dim;
+    e->Hh = c.n_heads;
+    e->KVH = c.n_kv_heads;
+    e->HD = c.head_dim;
+    e->hidden = c.hidden_dim;
+    e->V = c.vocab_size;
+    e->max_seq = c.seq_len;
+    e->qd = c.n_heads * c.head_dim;
+    e->kd = c.n_kv_heads * c.head_dim;
+    e->qkvd = e->qd + 2 * e->kd;
+    e->eps = c.norm_eps;
+    e->clamp = c.attn_clamp;
+    e->nchunk = (e->max_seq + kAttnChunk - 1) / kAttnChunk;
+    const int D = e->D, H = e->hidden, L = e->L, V = e->V;
+    // weight arena
+    size_t bytes = al256((size_t)V * D * 4) * 2 + al256(D * 4);
+    int kmax = 0;
+    for (int l = 0; l < L; l++) {
+        const jd_layer &ly = m->layers[l];
+        bytes += al256(D * 4) * 2 + al256((size_t)e->qkvd * D * 4) + al256((size_t)D * e->qd * 4) +
+                 al256((size_t)kMaxE * D * 4);
+        int na = 0;
+        for (int x = 0; x < kMaxE; x++)
+            if (ly.alive[x]) {
+                if (!ly.w_gate[x] || !ly.w_up[x] || !ly.w_down[x]) {
+                    jdg_set_err(e->ctx, "layer %d expert %d alive without weights", l, x);
+                    return JD_EINVAL;
+                }
+                bytes += al256((size_t)2 * H * D * 4) + al256((size_t)D * H * 4);
+                na++;
+            }
+        if (na > kmax) kmax = na;
+        e->n_alive[l] = na;
+    }
+    e->kmax = kmax < 1 ? 1 : kmax;
+    DALLOC(e->arena, bytes);
+    char *p = (char *)e->arena;
+    auto take = [&](size_t b) {
+        char *r = p;
+        p += al256(b);
+        return r;
+    };
+    std::vector<float> tmp;
+    e->tok_emb = (float *)take((size_t)V * D * 4);
+    e->output = (float *)take((size_t)V * D * 4);
+    e->output_norm = (float *)take(D * 4);
+    CK(cudaMemcpy(e->tok_emb, m->tok_emb, (size_t)V * D * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(e->output, m->output, (size_t)V * D * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(e->output_norm, m->output_norm, D * 4, cudaMemcpyHostToDevice));
+    std::vector<float *> gu((size_t)L * kMaxE, nullptr), dn((size_t)L * kMaxE, nullptr);
+    std::vector<int> alive((size_t)L * kMaxE, 0);
+    for (int l = 0; l < L; l++) {
+        const jd_layer &ly = m->layers[l];
+        LayerDev &ld = e->layers[l];
+        ld.attn_norm = (float *)take(D * 4);
+        ld.ffn_norm = (float *)take(D * 4);
+        ld.wqkv = (float *)take((size_t)e->qkvd * D * 4);
+        ld.wo = (float *)take((size_t)D * e->qd * 4);
+        ld.w_vote = (float *)take((size_t)kMaxE * D * 4);
+        ld.temperature = ly.temperature;
+        CK(cudaMemcpy(ld.attn_norm, ly.attn_norm, D * 4, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(ld.ffn_norm, ly.ffn_norm, D * 4, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(ld.wqkv, ly.wq, (size_t)e->qd * D * 4, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(ld.wqkv + (size_t)e->qd * D, ly.wk, (size_t)e->kd * D * 4, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(ld.wqkv + (size_t)(e->qd + e->kd) * D, ly.wv, (size_t)e->kd * D * 4, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(ld.wo, ly.wo, (size_t)D * e->qd * 4, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(ld.w_vote, ly.w_vote, (size_t)kMaxE * D * 4, cudaMemcpyHostToDevice));
+        for (int x = 0; x < kMaxE; x++) {
+            if (!ly.alive[x]) continue;
+            float *g = (float *)take((size_t)2 * H * D * 4);
+            float *d = (float *)take((size_t)D * H * 4);
+            tmp.resize((size_t)2 * H * D);
+            for (int i = 0; i < H; i++) {
+                memcpy(&tmp[(size_t)(2 * i) * D], ly.w_gate[x] + (size_t)i * D, D * 4);
+                memcpy(&tmp[(size_t)(2 * i + 1) * D], ly.w_up[x] + (size_t)i * D, D * 4);
+            }
+            CK(cudaMemcpy(g, tmp.data(), (size_t)2 * H * D * 4, cudaMemcpyHostToDevice));
+            CK(cudaMemcpy(d, ly.w_down[x], (size_t)D * H * 4, cudaMemcpyHostToDevice));
+            gu[(size_t)l * kMaxE + x] = g;
+            dn[(size_t)l * kMaxE + x] = d;
+            alive[(size_t)l * kMaxE + x] = 1;
+        }
+        e->layer_consensus[l] = ly.consensus;
+    }
+    DALLOC(e->gu_tab, (size_t)L * kMaxE * sizeof(float *));
+    DALLOC(e->dn_tab, (size_t)L * kMaxE * sizeof(float *));
+    DALLOC(e->alive_dev, (size_t)L * kMaxE * 4);
+    CK(cudaMemcpy(e->gu_tab, gu.data(), gu.size() * sizeof(float *), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(e->dn_tab, dn.data(), dn.size() * sizeof(float *), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(e->alive_dev, alive.data(), alive.size() * 4, cudaMemcpyHostToDevice));
+    // RoPE cache as alloc_run builds it (janusdoe.c:866-873)
+    const int half = e->HD / 2;
+    std::vector<float> cs((size_t)e->max_seq * half), sn((size_t)e->max_seq * half);
+    for (int pp = 0; pp < e->max_seq; pp++)
+        for (int i = 0; i < half; i++) {
+            float freq = 1.0f / powf(c.rope_theta, (float)(2 * i) / (float)c.head_dim);
+            float ang = (float)pp * freq;
+            cs[(size_t)pp * half + i] = cosf(ang);
+            sn[(size_t)pp * half + i] = sinf(ang);
+        }
+    DALLOC(e->rope_cos, cs.size() * 4);
+    DALLOC(e->rope_sin, sn.size() * 4);
+    CK(cudaMemcpy(e->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(e->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+    e->rope_norm = 0;
+    // activations
+    const int B = max_batch;
+    DALLOC(e->x, (size_t)B * D * 4);
+    DALLOC(e->xb, (size_t)B * D * 4);
+    DALLOC(e->qkv, (size_t)B * e->qkvd * 4);
+    DALLOC(e->att, (size_t)B * e->qd * 4);
+    DALLOC(e->part, (size_t)B * e->Hh * e->nchunk * (e->HD + 2) * 4);
+    DALLOC(e->hbuf, (size_t)B * kMaxE * H * 4);
+    DALLOC(e->ybuf, (size_t)B * kMaxE * D * 4);
+    DALLOC(e->logits, (size_t)B * V * 4);
+    // KV cache [B][L][S][kd]
+    e->kv_bstride = (long)L * e->max_seq * e->kd;
+    DALLOC(e->kc, (size_t)B * e->kv_bstride * 4);
+    DALLOC(e->vc, (size_t)B * e->kv_bstride * 4);
+    int rc = jdg_alloc_state(e);
+    if (rc != JD_OK) return rc;
+    rc = jdg_reset(e, -1);
+    if (rc != JD_OK) return rc;
+    CK(cudaStreamSynchronize(e->st));
+    return JD_OK;
+}
+
+// ------------------------------------------------------------------------------------
+static int pick_bm(int B) { return B <= 16 ? 16 : B <= 32 ? 32 : 64; }
+
+template <int EPI>
+static void launch_sgemm(jdg_engine *e, const SgemmArgs &a, int B, int nseg) {
+    dim3 grid((a.N + 127) / 128, (B + pick_bm(B) - 1) / pick_bm(B), nseg);
+    switch (pick_bm(B)) {
+    case 16: k_sgemm<16, EPI><<<grid, 256, 0, e->st>>>(a); break;
+    case 32: k_sgemm<32, EPI><<<grid, 256, 0, e->st>>>(a); break;
+    default: k_sgemm<64, EPI><<<grid, 256, 0, e->st>>>(a); break;
+    }
+    e->launches++;
+}
+
+static void launch_gemv1(jdg_engine *e, int epi, const float *W, int N, int K, const float *X, const float *norm_w,
+                         int prenorm, float *Y) {
+    GemvArgs a;
+    a.W = W;
+    a.N = N;
+    a.K = K;
+    a.X = X;
+    a.ldx = K;
+    a.norm_w = norm_w;
+    a.eps = e->eps;
+    a.prenorm = prenorm;
+    a.Y = Y;
+    a.ldy = N;
+    int grid = (N + 3) / 4;
+    size_t sm = (size_t)K * 4;
+    if (epi == EPI_ADD) k_gemv_f32<1, 1, EPI_ADD><<<grid, 128, sm, e->st>>>(a);
+    else k_gemv_f32<1, 1, EPI_STORE><<<grid, 128, sm, e->st>>>(a);
+    e->launches++;
+}
+
+static void launch_attention(jdg_engine *e, int l, int B, float scale, float bias) {
+    AttnArgs a;
+    a.qkv = e->qkv;
+    a.ld = e->qkvd;
+    a.kc = e->kc + (size_t)l * e->max_seq * e->kd;
+    a.vc = e->vc + (size_t)l * e->max_seq * e->kd;
+    a.bstride = e->kv_bstride;
+    a.pos = e->pos;
+    a.H = e->Hh;
+    a.KVH = e->KVH;
+    a.HD = e->HD;
+    a.hg = e->Hh / e->KVH;
+    a.nchunk = e->nchunk;
+    a.scale = scale;
+    a.bias = bias;
+    a.clamp = e->clamp;
+    a.inv_clamp = e->clamp > 0 ? 1.0f / e->clamp : 0.f;
+    a.part = e->part;
+    dim3 grid(e->nchunk, e->KVH, B);
+    if (e->HD == 64) k_attn_partial<64><<<grid, 128, 0, e->st>>>(a);
+    else k_attn_partial<128><<<grid, 128, 0, e->st>>>(a);
+    k_attn_combine<<<dim3(e->Hh, B), e->HD, 0, e->st>>>(e->part, e->pos, e->Hh, e->HD, e->nchunk, e->att, e->qd);
+    e->launches += 2;
+}
+
+void jdg_launch_rope(jdg_engine *e, int l, int B) {
+    RopeArgs r;
+    r.qkv = e->qkv;
+    r.ld = e->qkvd;
+    r.H = e->Hh;
+    r.KVH = e->KVH;
+    r.HD = e->HD;
+    r.cos_t = e->rope_cos;
+    r.sin_t = e->rope_sin;
+    r.pair_norm = e->rope_norm;
+    r.pos = e->pos;
+    r.max_seq = e->max_seq;
+    r.kc = e->kc + (size_t)l * e->max_seq * e->kd;
+    r.vc = e->vc + (size_t)l * e->max_seq * e->kd;
+    r.bstride = e->kv_bstride;
+    r.err = e->err;
+    k_rope_kv<<<B, 256, 0, e->st>>>(r);
+    e->launches++;
+}
+
+void jdg_launch_attention(jdg_engine *e, int l, int B, float scale, float bias) { launch_attention(e, l, B, scale, bias); }
+
+void jdg_launch_pick(jdg_engine *e, int B) {
+    PickArgs pa;
+    pa.logits = e->logits;
+    pa.V = e->V;
+    pa.ldl = e->V;
+    pa.temp = e->temp;
+    pa.top_k = e->top_k;
+    pa.tok = e->tok;
+    pa.pos = e->pos;
+    pa.rng = e->rng;
+    pa.plen = e->plen;
+    pa.prompt = e->prompt;
+    pa.Pmax = e->Pmax;
+    pa.hist = e->hist;
+    pa.hist_n = e->hist_n;
+    pa.Hmax = e->Hmax;
+    pa.next_out = e->next_out;
+    k_pick<<<B, 1024, 0, e->st>>>(pa);
+    e->launches++;
+}
+
+void jdg_launch_elect(jdg_engine *e, int l, int B, const float *xin, const float *norm_w, const float *w_vote,
+                      const int *alive, float temperature, int host) {
+    ElectArgs a;
+    a.x = xin;
+    a.norm_w = norm_w;
+    a.eps = e->eps;
+    a.D = e->D;
+    a.host = host;
+    a.w_vote = w_vote;
+    a.alive = alive;
+    a.temperature = temperature;
+    a.consensus = e->consensus;
+    a.L = e->L;
+    a.l = l;
+    a.xb = e->xb;
+    a.kcnt = e->kcnt;
+    a.sel = e->sel;
+    a.selw = e->selw;
+    a.tr_k = e->tr_k;
+    a.tr_sel = e->tr_sel;
+    a.tr_w = e->tr_w;
+    a.tr_ema = e->tr_ema;
+    k_elect<<<B, 256, (size_t)e->D * 4, e->st>>>(a);
+    e->launches++;
+}
+
+// One own-model decode step for slots 0..B-1 (forward_token, janusdoe.c:879-934, then
+// the next-token pick).
+static void enqueue_own_step(jdg_engine *e, int B) {
+    const int D = e->D, H = e->hidden, L = e->L, V = e->V, qd = e->qd;
+    const float scale = 1.0f / sqrtf((float)e->HD);
+    k_embed<<<B, 256, 0, e->st>>>(e->tok_emb, V, D, e->tok, e->x, e->err);
+    e->launches++;
+    for (int l = 0; l < L; l++) {
+        LayerDev &ly = e->layers[l];
+        if (B == 1) {
+            launch_gemv1(e, EPI_STORE, ly.wqkv, e->qkvd, D, e->x, ly.attn_norm, 1, e->qkv);
+        } else {
+            k_rmsnorm<<<B, 256, 0, e->st>>>(e->x, ly.attn_norm, e->xb, D, e->eps);
+            e->launches++;
+            SgemmArgs a = {};
+            a.A = e->xb; a.lda = D; a.M = B; a.W = ly.wqkv; a.N = e->qkvd; a.K = D; a.C = e->qkv; a.ldc = e->qkvd;
+            launch_sgemm<EPI_STORE>(e, a, B, 1);
+        }
+        jdg_launch_rope(e, l, B);
+        launch_attention(e, l, B, scale, 1.0f);
+        if (B == 1) {
+            launch_gemv1(e, EPI_ADD, ly.wo, D, qd, e->att, nullptr, 0, e->x);
+        } else {
+            SgemmArgs a = {};
+            a.A = e->att; a.lda = qd; a.M = B; a.W = ly.wo; a.N = D; a.K = qd; a.C = e->x; a.ldc = D;
+            launch_sgemm<EPI_ADD>(e, a, B, 1);
+        }
+        jdg_launch_elect(e, l, B, e->x, ly.ffn_norm, ly.w_vote, e->alive_dev + (size_t)l * kMaxE, ly.temperature, 0);
+        const float *const *gu = e->gu_tab + (size_t)l * kMaxE;
+        const float *const *dn = e->dn_tab + (size_t)l * kMaxE;
+        if (e->n_alive[l] < 2) continue;  // parliament_elect returns 0 below MIN_EXPERTS
+        if (B == 1) {
+            dim3 g1((H + 3) / 4, e->n_alive[l]);
+            k_expert_gu_b1<<<g1, 128, (size_t)D * 4, e->st>>>(gu, e->kcnt, e->sel, H, D, e->xb, e->hbuf, e->err);
+            k_expert_down_b1<<<(D + 3) / 4, 128, (size_t)e->n_alive[l] * H * 4, e->st>>>(dn, e->kcnt, e->sel, e->selw, D,
+                                                                                         H, e->hbuf, e->x);
+            e->launches += 2;
+        } else {
+            k_route<<<1, 512, 0, e->st>>>(e->kcnt, e->sel, B, e->rcnt, e->ridx, e->pairrow, e->err);
+            SgemmArgs a = {};
+            a.A = e->xb; a.lda = D; a.idx = e->ridx; a.ldi = B; a.cnt = e->rcnt; a.Wtab = gu; a.N = 2 * H; a.K = D;
+            a.C = e->hbuf; a.ldc = H; a.c_seg_rows = B;
+            launch_sgemm<EPI_SWIGLU>(e, a, B, kMaxE);
+            SgemmArgs d = {};
+            d.A = e->hbuf; d.lda = H; d.a_seg_rows = B; d.cnt = e->rcnt; d.Wtab = dn; d.N = D; d.K = H;
+            d.C = e->ybuf; d.ldc = D; d.c_seg_rows = B;
+            launch_sgemm<EPI_STORE>(e, d, B, kMaxE);
+            k_combine<<<B, 256, 0, e->st>>>(e->kcnt, e->selw, e->pairrow, e->ybuf, D, e->x);
+            e->launches += 2;
+        }
+    }
+    if (B == 1) {
+        launch_gemv1(e, EPI_STORE, e->output, V, D, e->x, e->output_norm, 1, e->logits);
+    } else {
+        k_rmsnorm<<<B, 256, 0, e->st>>>(e->x, e->output_norm, e->xb, D, e->eps);
+        e->launches++;
+        SgemmArgs a = {};
+        a.A = e->xb; a.lda = D; a.M = B; a.W = e->output; a.N = V; a.K = D; a.C = e->logits; a.ldc = V;
+        launch_sgemm<EPI_STORE>(e, a, B, 1);
+    }
+    jdg_launch_pick(e, B);
+}
+
+static int enqueue_step(jdg_engine *e, int B) {
+    if (e->kind == 0) enqueue_own_step(e, B);
+    else return jdg_enqueue_host_step(e, B);
+    return JD_OK;
+}
+
+// Capture one step for batch B into a CUDA graph (built once per B and sampling setting).
+static int get_graph(jdg_engine *e, int B, cudaGraphExec_t *out) {
+    auto it = e->graphs.find(B);
+    if (it != e->graphs.end()) {
+        *out = it->second;
+        return JD_OK;
+    }
+    static bool attr_done = false;
+    if (!attr_done) {
+        CK(cudaFuncSetAttribute(k_gemv_f32<1, 1, EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        CK(cudaFuncSetAttribute(k_gemv_f32<1, 1, EPI_ADD>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        CK(cudaFuncSetAttribute(k_expert_down_b1, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        CK(cudaFuncSetAttribute(k_expert_gu_b1, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        CK(cudaFuncSetAttribute(k_elect, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        int rc = jdg_host_set_attrs(e);
+        if (rc != JD_OK) return rc;
+        attr_done = true;
+    }
+    cudaGraph_t g;
+    CK(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+    long long before = e->launches;
+    int rc = enqueue_step(e, B);
+    cudaError_t r = cudaStreamEndCapture(e->st, &g);
+    if (rc != JD_OK) return rc;
+    if (r != cudaSuccess) {
+        jdg_set_err(e->ctx, "graph capture failed: %s", cudaGetErrorString(r));
+        return JD_ECUDA;
+    }
+    cudaGraphExec_t ge;
+    r = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    if (r != cudaSuccess) {
+        jdg_set_err(e->ctx, "graph instantiate failed: %s", cudaGetErrorString(r));
+        return JD_ECUDA;
+    }
+    e->launches_per_step[B] = e->launches - before;
+    e->launches = before;
+    e->graphs[B] = ge;
+    *out = ge;
+    return JD_OK;
+}
+
+static void drop_graphs(jdg_engine *e) {
+    for (auto &kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
+}
+
+static int check_err(jdg_engine *e) {
+    int h = 0;
+    CK(cudaMemcpyAsync(&h, e->err, 4, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    if (h) {
+        CK(cudaMemsetAsync(e->err, 0, 4, e->st));
+        jdg_set_err(e->ctx, "device-side check failed (flags 0x%x: %s%s%s%s)", h, (h & JDG_ERR_TOKEN) ? "token " : "",
+                    (h & JDG_ERR_POS) ? "position " : "", (h & JDG_ERR_ROUTE) ? "route " : "",
+                    (h & JDG_ERR_SHAPE) ? "shape" : "");
+        return JD_ESTATE;
+    }
+    return JD_OK;
+}
+
+// ------------------------------------------------------------------------------------
+extern "C" void jdg_engine_free(jdg_engine *e) {
+    if (!e) return;
+    cudaSetDevice(e->ctx->device);
+    if (e->st) cudaStreamSynchronize(e->st);
+    drop_graphs(e);
+    jdg_host_release(e);
+    for (void *p : e->allocs) cudaFree(p);
+    if (e->ev0) cudaEventDestroy(e->ev0);
+    if (e->ev1) cudaEventDestroy(e->ev1);
+    if (e->st) cudaStreamDestroy(e->st);
+    delete e;
+}
+
+extern "C" int jdg_set_sampling(jdg_engine *e, float temperature, int top_k) {
+    if (!e || top_k < 0) return JD_EINVAL;
+    if (temperature != e->temp || top_k != e->top_k) drop_graphs(e);
+    e->temp = temperature;
+    e->top_k = top_k;
+    return JD_OK;
+}
+
+extern "C" int jdg_reset(jdg_engine *e, int slot) {
+    if (!e || slot >= e->B_max || slot < -1) return JD_EINVAL;
+    cudaSetDevice(e->ctx->device);
+    int s0 = slot < 0 ? 0 : slot, s1 = slot < 0 ? e->B_max : slot + 1, n = s1 - s0;
+    CK(cudaMemsetAsync(e->kc + (size_t)s0 * e->kv_bstride, 0, (size_t)n * e->kv_bstride * 4, e->st));
+    CK(cudaMemsetAsync(e->vc + (size_t)s0 * e->kv_bstride, 0, (size_t)n * e->kv_bstride * 4, e->st));
+    std::vector<float> cons((size_t)n * e->L);
+    for (int b = 0; b < n; b++)
+        for (int l = 0; l < e->L; l++) cons[(size_t)b * e->L + l] = e->layer_consensus[l];
+    CK(cudaMemcpyAsync(e->consensus + (size_t)s0 * e->L, cons.data(), cons.size() * 4, cudaMemcpyHostToDevice, e->st));
+    CK(cudaMemsetAsync(e->plen + s0, 0, n * 4, e->st));
+    CK(cudaMemsetAsync(e->hist_n + s0, 0, n * 4, e->st));
+    CK(cudaMemsetAsync(e->pos + s0, 0, n * 4, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    return JD_OK;
+}
+
+extern "C" int jdg_set_prompt(jdg_engine *e, int B, const int *tokens, int P, const int *len, const uint64_t *rng) {
+    if (!e || B < 1 || B > e->B_max || !tokens || !len || P < 1 || P > e->Pmax) return JD_EINVAL;
+    cudaSetDevice(e->ctx->device);
+    for (int b = 0; b < B; b++)
+        if (len[b] < 1 || len[b] > P) {
+            jdg_set_err(e->ctx, "prompt length %d of slot %d outside [1, %d]", len[b], b, P);
+            return JD_EINVAL;
+        }
+    std::vector<int> pr((size_t)B * e->Pmax, 0), t0(B), p0(B, 0);
+    for (int b = 0; b < B; b++) {
+        memcpy(&pr[(size_t)b * e->Pmax], tokens + (size_t)b * P, (size_t)len[b] * 4);
+        t0[b] = tokens[(size_t)b * P];
+    }
+    CK(cudaMemcpyAsync(e->prompt, pr.data(), pr.size() * 4, cudaMemcpyHostToDevice, e->st));
+    CK(cudaMemcpyAsync(e->plen, len, B * 4, cudaMemcpyHostToDevice, e->st));
+    CK(cudaMemcpyAsync(e->tok, t0.data(), B * 4, cudaMemcpyHostToDevice, e->st));
+    CK(cudaMemcpyAsync(e->pos, p0.data(), B * 4, cudaMemcpyHostToDevice, e->st));
+    if (rng) CK(cudaMemcpyAsync(e->rng, rng, B * 8, cudaMemcpyHostToDevice, e->st));
+    CK(cudaMemsetAsync(e->hist_n, 0, B * 4, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    return JD_OK;
+}
+
+extern "C" int jdg_run(jdg_engine *e, int B, int n_steps) {
+    if (!e || B < 1 || B > e->B_max || n_steps < 0) return JD_EINVAL;
+    cudaSetDevice(e->ctx->device);
+    cudaGraphExec_t ge;
+    int rc = get_graph(e, B, &ge);
+    if (rc != JD_OK) return rc;
+    CK(cudaEventRecord(e->ev0, e->st));
+    for (int i = 0; i < n_steps; i++) CK(cudaGraphLaunch(ge, e->st));
+    CK(cudaEventRecord(e->ev1, e->st));
+    CK(cudaEventSynchronize(e->ev1));
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, e->ev0, e->ev1));
+    e->last_ms = ms;
+    e->launches += (long long)n_steps * e->launches_per_step[B];
+    return check_err(e);
+}
+
+extern "C" int jdg_last_run_ms(jdg_engine *e, float *ms) {
+    if (!e || !ms) return JD_EINVAL;
+    *ms = e->last_ms;
+    return JD_OK;
+}
+
+extern "C" int jdg_launch_count(jdg_engine *e, long long *n) {
+    if (!e || !n) return JD_EINVAL;
+    *n = e->launches;
+    return JD_OK;
+}
+
+extern "C" int jdg_get_state(jdg_engine *e, int B, int *tok, int *pos) {
+    if (!e || B < 1 || B > e->B_max) return JD_EINVAL;
+    cudaSetDevice(e->ctx->device);
+    if (tok) CK(cudaMemcpyAsync(tok, e->tok, B * 4, cudaMemcpyDeviceToHost, e->st));
+    if (pos) CK(cudaMemcpyAsync(pos, e->pos, B * 4, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    return JD_OK;
+}
+
+extern "C" int jdg_get_history(jdg_engine *e, int B, int n, int *tokens) {
+    if (!e || B < 1 || B > e->B_max || n < 0 || n > e->Hmax || !tokens) return JD_EINVAL;
+    cudaSetDevice(e->ctx->device);
+    std::vector<int> h((size_t)B * e->Hmax), hn(B);
+    CK(cudaMemcpyAsync(h.data(), e->hist, h.size() * 4, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaMemcpyAsync(hn.data(), e->hist_n, B * 4, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    for (int b = 0; b < B; b++) {
+        int cnt = hn[b] < e->Hmax ? hn[b] : e->Hmax;
+        for (int i = 0; i < n; i++) {
+            int src = cnt - n + i;
+            tokens[(size_t)b * n + i] = src >= 0 ? h[(size_t)b * e->Hmax + src] : -1;
+        }
+    }
+    return JD_OK;
+}
+
+extern "C" int jdg_get_logits(jdg_engine *e, int B, float *logits) {
+    if (!e || B < 1 || B > e->B_max || !logits) return JD_EINVAL;
+    cudaSetDevice(e->ctx->device);
+    CK(cudaMemcpyAsync(logits, e->logits, (size_t)B * e->V * 4, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    return JD_OK;
+}
+
+extern "C" int jdg_get_trace(jdg_engine *e, int B, jdg_trace *t) {
+    if (!e || B < 1 || B > e->B_max || !t) return JD_EINVAL;
+    cudaSetDevice(e->ctx->device);
+    const size_t n = (size_t)B * e->L;
+    if (t->k) CK(cudaMemcpyAsync(t->k, e->tr_k, n * 4, cudaMemcpyDeviceToHost, e->st));
+    if (t->ema) CK(cudaMemcpyAsync(t->ema, e->tr_ema, n * 4, cudaMemcpyDeviceToHost, e->st));
+    if (t->sel) CK(cudaMemcpyAsync(t->sel, e->tr_sel, n * kMaxE * 4, cudaMemcpyDeviceToHost, e->st));
+    if (t->w) CK(cudaMemcpyAsync(t->w, e->tr_w, n * kMaxE * 4, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    return JD_OK;
+}
+
+extern "C" int jdg_step(jdg_engine *e, int B, const int *tok, const int *pos, uint64_t *rng, int *next_tok, float *logits,
+                        jdg_trace *trace) {
+    if (!e || B < 1 || B > e->B_max || !tok || !pos) return JD_EINVAL;
+    for (int b = 0; b < B; b++) {
+        if (pos[b] < 0 || pos[b] >= e->max_seq) {
+            jdg_set_err(e->ctx, "position %d of slot %d outside [0, %d)", pos[b], b, e->max_seq);
+            return JD_EINVAL;
+        }
+        if (tok[b] < 0 || (e->kind == 0 && tok[b] >= e->V)) {
+            jdg_set_err(e->ctx, "token %d of slot %d outside [0, %d)", tok[b], b, e->V);
+            return JD_EINVAL;
+        }
+    }
+    cudaSetDevice(e->ctx->device);
+    cudaGraphExec_t ge;
+    int rc = get_graph(e, B, &ge);
+    if (rc != JD_OK) return rc;
+    CK(cudaMemcpyAsync(e->tok, tok, B * 4, cudaMemcpyHostToDevice, e->st));
+    CK(cudaMemcpyAsync(e->pos, pos, B * 4, cudaMemcpyHostToDevice, e->st));
+    CK(cudaMemsetAsync(e->plen, 0, B * 4, e->st));
+    if (rng) CK(cudaMemcpyAsync(e->rng, rng, B * 8, cudaMemcpyHostToDevice, e->st));
+    CK(cudaEventRecord(e->ev0, e->st));
+    CK(cudaGraphLaunch(ge, e->st));
+    CK(cudaEventRecord(e->ev1, e->st));
+    e->launches += e->launches_per_step[B];
+    if (next_tok) CK(cudaMemcpyAsync(next_tok, e->next_out, B * 4, cudaMemcpyDeviceToHost, e->st));
+    if (rng) CK(cudaMemcpyAsync(rng, e->rng, B * 8, cudaMemcpyDeviceToHost, e->st));
+    if (logits) CK(cudaMemcpyAsync(logits, e->logits, (size_t)B * e->V * 4, cudaMemcpyDeviceToHost, e->st));
+    rc = check_err(e);
+    if (rc != JD_OK) return rc;
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, e->ev0, e->ev1));
+    e->last_ms = ms;
+    if (trace) return jdg_get_trace(e, B, trace);
+    return JD_OK;
+}
+
+extern "C" int jdg_profile_step(jdg_engine *e, int B, float *ms_by_kernel, int max_kernels, int *n_kernels,
+                                const char **names) {
+    (void)e; (void)B; (void)ms_by_kernel; (void)max_kernels; (void)names;
+    if (n_kernels) *n_kernels = 0;
+    return JD_EUNSUPPORTED;
+}

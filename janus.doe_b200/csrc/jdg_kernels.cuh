@@ -1,0 +1,888 @@
+// jdg_kernels.cuh — decode-step kernels for the own model and the shared pieces of the
+// host path: embedding, RMSNorm, f32 GEMV (batch <= 8), f32 SIMT GEMM (grouped by expert),
+// RoPE + KV append, split-K decode attention, the parliament election, routing, expert
+// combine, and next-token selection.  Every kernel cites the reference lines it replaces.
+#pragma once
+#include "jdg_common.cuh"
+
+namespace jdg {
+
+constexpr int kMaxE = 16;
+constexpr int kAttnChunk = 64;  // positions per attention CTA
+constexpr int kMaxHG = 8;       // query heads per KV head supported by the attention kernel
+
+// ------------------------------------------------------------------------------------
+// x[b] = tok_emb[tok[b]] (janusdoe.c:882; host janusdoe.c:3177 zero row for token >= V)
+__global__ void k_embed(const float *__restrict__ emb, int V, int D, const int *__restrict__ tok, float *__restrict__ x,
+                        int *err) {
+    int b = blockIdx.x, t = tok[b];
+    float *xr = x + (size_t)b * D;
+    if (t < 0 || t >= V) {
+        if (threadIdx.x == 0) atomicOr(err, JDG_ERR_TOKEN);
+        for (int i = threadIdx.x; i < D; i += blockDim.x) xr[i] = 0.f;
+        return;
+    }
+    const float *er = emb + (size_t)t * D;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) xr[i] = er[i];
+}
+
+// out[b] = x[b] * (1/sqrtf(sum(x^2)/D + eps)) * w   (janusdoe.c:504, 3181-3186); w may be null
+__global__ void k_rmsnorm(const float *__restrict__ x, const float *__restrict__ w, float *__restrict__ out, int D,
+                          float eps) {
+    __shared__ float red[32];
+    int b = blockIdx.x;
+    const float *xr = x + (size_t)b * D;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+    ss = block_sum(ss, red);
+    float inv = 1.0f / sqrtf(ss / (float)D + eps);
+    float *o = out + (size_t)b * D;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) {
+        float v = __fmul_rn(xr[i], inv);
+        o[i] = w ? __fmul_rn(v, w[i]) : v;
+    }
+}
+
+// ------------------------------------------------------------------------------------
+// f32 GEMV for NB <= 8 tokens: Y[b][row] (epi) W[row][:] . X[b][:]  (matvec, janusdoe.c:505-519)
+// One warp per RPW rows, X staged in shared memory, optionally RMS-normalised on the way in.
+enum { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2 };
+
+struct GemvArgs {
+    const float *W;
+    int N, K;
+    const float *X;
+    int ldx;
+    const float *norm_w;  // prenorm weights (nullptr with prenorm = ones)
+    float eps;
+    int prenorm;
+    float *Y;
+    int ldy;
+};
+
+template <int NB, int RPW, int EPI>
+__global__ __launch_bounds__(128) void k_gemv_f32(GemvArgs a) {
+    extern __shared__ float xs[];  // [NB][K]
+    __shared__ float red[32];
+    const int K = a.K, K4 = K >> 2;
+    for (int b = 0; b < NB; b++) {
+        const float4 *src = reinterpret_cast<const float4 *>(a.X + (size_t)b * a.ldx);
+        float4 *dst = reinterpret_cast<float4 *>(xs + (size_t)b * K);
+        float ss = 0.f;
+        for (int i = threadIdx.x; i < K4; i += blockDim.x) {
+            float4 v = src[i];
+            dst[i] = v;
+            ss = dot4(v, v, ss);
+        }
+        if (a.prenorm) {
+            ss = block_sum(ss, red);
+            float inv = 1.0f / sqrtf(ss / (float)K + a.eps);
+            for (int i = threadIdx.x; i < K; i += blockDim.x) {
+                float v = __fmul_rn(xs[b * K + i], inv);
+                xs[b * K + i] = a.norm_w ? __fmul_rn(v, a.norm_w[i]) : v;
+            }
+        }
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int row0 = (blockIdx.x * (blockDim.x >> 5) + warp) * RPW;
+    if (row0 >= a.N) return;
+    float acc[RPW][NB];
+#pragma unroll
+    for (int r = 0; r < RPW; r++)
+#pragma unroll
+        for (int b = 0; b < NB; b++) acc[r][b] = 0.f;
+    const float *wr[RPW];
+#pragma unroll
+    for (int r = 0; r < RPW; r++) wr[r] = a.W + (size_t)min(row0 + r, a.N - 1) * K;
+    const float4 *xs4 = reinterpret_cast<const float4 *>(xs);
+#pragma unroll 4
+    for (int k4 = lane; k4 < K4; k4 += 32) {
+        float4 w[RPW];
+#pragma unroll
+        for (int r = 0; r < RPW; r++) w[r] = ld_stream4(wr[r] + 4 * k4);
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            float4 xv = xs4[b * K4 + k4];
+#pragma unroll
+            for (int r = 0; r < RPW; r++) acc[r][b] = dot4(w[r], xv, acc[r][b]);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < RPW; r++)
+#pragma unroll
+        for (int b = 0; b < NB; b++) acc[r][b] = warp_sum(acc[r][b]);
+    if (lane != 0) return;
+#pragma unroll
+    for (int b = 0; b < NB; b++) {
+        float *y = a.Y + (size_t)b * a.ldy;
+        if (EPI == EPI_SWIGLU) {
+            // rows (2i, 2i+1) = (gate_i, up_i): h_i = silu(g)*u  (janusdoe.c:925)
+            y[row0 >> 1] = __fmul_rn(silu_ref(acc[0][b]), acc[RPW - 1][b]);
+        } else {
+#pragma unroll
+            for (int r = 0; r < RPW; r++) {
+                int row = row0 + r;
+                if (row < a.N) {
+                    if (EPI == EPI_ADD) y[row] = __fadd_rn(y[row], acc[r][b]);
+                    else y[row] = acc[r][b];
+                }
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------
+// Expert FFN for one token (janusdoe.c:921-929): gate/up of each elected expert.
+// grid (ceil(2H / (4 warps * 2 rows)), 16): y = election slot ki; rows 2i/2i+1 = gate_i/up_i.
+__global__ __launch_bounds__(128) void k_expert_gu_b1(const float *const *__restrict__ gu_tab, const int *__restrict__ kcnt,
+                                                      const int *__restrict__ sel, int H, int D,
+                                                      const float *__restrict__ xb, float *__restrict__ hbuf, int *err) {
+    extern __shared__ float xs[];
+    const int ki = blockIdx.y;
+    if (ki >= kcnt[0]) return;
+    const int e = sel[ki];
+    if (e < 0 || e >= kMaxE || gu_tab[e] == nullptr) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(err, JDG_ERR_ROUTE);
+        return;
+    }
+    const float *W = gu_tab[e];
+    const int K4 = D >> 2;
+    for (int i = threadIdx.x; i < K4; i += blockDim.x) reinterpret_cast<float4 *>(xs)[i] = reinterpret_cast<const float4 *>(xb)[i];
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int i = blockIdx.x * (blockDim.x >> 5) + warp;  // hidden unit
+    if (i >= H) return;
+    const float *wg = W + (size_t)(2 * i) * D, *wu = wg + D;
+    float ag = 0.f, au = 0.f;
+    const float4 *xs4 = reinterpret_cast<const float4 *>(xs);
+#pragma unroll 4
+    for (int k4 = lane; k4 < K4; k4 += 32) {
+        float4 g = ld_stream4(wg + 4 * k4), u = ld_stream4(wu + 4 * k4), xv = xs4[k4];
+        ag = dot4(g, xv, ag);
+        au = dot4(u, xv, au);
+    }
+    ag = warp_sum(ag);
+    au = warp_sum(au);
+    if (lane == 0) hbuf[(size_t)ki * H + i] = __fmul_rn(silu_ref(ag), au);
+}
+
+// Down projection of every elected expert for one token, then the weighted sum in election
+// order and the residual add: expert_out += w_ki * (Wd_e . h_ki); x += expert_out
+// (janusdoe.c:926-929).  grid ceil(D / 4 warps).
+__global__ __launch_bounds__(128) void k_expert_down_b1(const float *const *__restrict__ dn_tab, const int *__restrict__ kcnt,
+                                                        const int *__restrict__ sel, const float *__restrict__ selw, int D, int H,
+                                                        const float *__restrict__ hbuf, float *__restrict__ x) {
+    extern __shared__ float hs[];  // [k][H]
+    const int k = kcnt[0];
+    const int H4 = H >> 2;
+    for (int i = threadIdx.x; i < k * H4; i += blockDim.x) reinterpret_cast<float4 *>(hs)[i] = reinterpret_cast<const float4 *>(hbuf)[i];
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int r = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (r >= D) return;
+    float eo = 0.f;
+    for (int ki = 0; ki < k; ki++) {
+        const float *W = dn_tab[sel[ki]];
+        if (W == nullptr) continue;
+        const float *wr = W + (size_t)r * H;
+        const float4 *h4 = reinterpret_cast<const float4 *>(hs + (size_t)ki * H);
+        float acc = 0.f;
+#pragma unroll 4
+        for (int k4 = lane; k4 < H4; k4 += 32) acc = dot4(ld_stream4(wr + 4 * k4), h4[k4], acc);
+        acc = warp_sum(acc);
+        eo = __fadd_rn(eo, __fmul_rn(selw[ki], acc));
+    }
+    if (lane == 0) x[r] = __fadd_rn(x[r], eo);
+}
+
+// ------------------------------------------------------------------------------------
+// f32 SIMT GEMM, optionally grouped by expert: C[row(m)][n] (epi) sum_k A[arow(m)][k] * W[n][k]
+// Tile BM x 128 x 16, 256 threads, thread tile (BM/16) x 8, register double buffering.
+struct SgemmArgs {
+    const float *A;
+    int lda;
+    const int *idx;   // grouped + gathered: A row of (segment s, m) = idx[s*ldi + m]
+    int ldi;
+    int a_seg_rows;   // grouped, not gathered: A row = s*a_seg_rows + m
+    const int *cnt;   // grouped: rows of segment s = cnt[s]; nullptr = dense with M rows
+    int M;
+    const float *const *Wtab;  // grouped: weights of segment s
+    const float *W;
+    int N, K;
+    float *C;
+    int ldc;
+    int c_seg_rows;   // grouped: C row = s*c_seg_rows + m
+};
+
+template <int BM, int EPI>
+__global__ __launch_bounds__(256) void k_sgemm(SgemmArgs a) {
+    constexpr int BN = 128, BK = 16, TM = BM / 16;
+    const int seg = blockIdx.z;
+    const int M = a.cnt ? a.cnt[seg] : a.M;
+    const int m0 = blockIdx.y * BM;
+    if (m0 >= M) return;
+    const float *W = a.Wtab ? a.Wtab[seg] : a.W;
+    if (W == nullptr) return;
+    const int n0 = blockIdx.x * BN;
+    const int tid = threadIdx.x;
+    __shared__ __align__(16) float As[2][BK][BM + 4];
+    __shared__ __align__(16) float Ws[2][BK][BN + 4];
+
+    // loader mapping
+    const int la_row = tid >> 2, la_k4 = tid & 3;  // A: BM rows x 4 float4
+    const bool la_on = la_row < BM;
+    const float *a_src = nullptr;
+    if (la_on && m0 + la_row < M) {
+        int m = m0 + la_row, ar;
+        if (a.cnt && a.idx) ar = a.idx[seg * a.ldi + m];
+        else if (a.cnt) ar = seg * a.a_seg_rows + m;
+        else ar = m;
+        a_src = a.A + (size_t)ar * a.lda;
+    }
+    const float *w_src[2];
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        int n = n0 + la_row + 64 * j;
+        w_src[j] = n < a.N ? W + (size_t)n * a.K : nullptr;
+    }
+    float4 ra, rw[2];
+    auto gload = [&](int k0) {
+        ra = a_src ? *reinterpret_cast<const float4 *>(a_src + k0 + 4 * la_k4) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 2; j++)
+            rw[j] = w_src[j] ? ld_stream4(w_src[j] + k0 + 4 * la_k4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    };
+    auto sstore = [&](int buf) {
+        if (la_on) {
+            As[buf][4 * la_k4 + 0][la_row] = ra.x;
+            As[buf][4 * la_k4 + 1][la_row] = ra.y;
+            As[buf][4 * la_k4 + 2][la_row] = ra.z;
+            As[buf][4 * la_k4 + 3][la_row] = ra.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            int n = la_row + 64 * j;
+            Ws[buf][4 * la_k4 + 0][n] = rw[j].x;
+            Ws[buf][4 * la_k4 + 1][n] = rw[j].y;
+            Ws[buf][4 * la_k4 + 2][n] = rw[j].z;
+            Ws[buf][4 * la_k4 + 3][n] = rw[j].w;
+        }
+    };
+    const int ty = tid >> 4, tx = tid & 15;
+    float acc[TM][8];
+#pragma unroll
+    for (int i = 0; i < TM; i++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[i][j] = 0.f;
+
+    const int nk = a.K / BK;
+    gload(0);
+    sstore(0);
+    __syncthreads();
+    for (int kt = 0; kt < nk; kt++) {
+        const int buf = kt & 1;
+        if (kt + 1 < nk) gload((kt + 1) * BK);
+#pragma unroll
+        for (int kk = 0; kk < BK; kk++) {
+            float av[TM];
+#pragma unroll
+            for (int i = 0; i < TM; i++) av[i] = As[buf][kk][ty * TM + i];
+            float4 w0 = *reinterpret_cast<const float4 *>(&Ws[buf][kk][tx * 4]);
+            float4 w1 = *reinterpret_cast<const float4 *>(&Ws[buf][kk][64 + tx * 4]);
+            float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int i = 0; i < TM; i++)
+#pragma unroll
+                for (int j = 0; j < 8; j++) acc[i][j] = fmaf(av[i], wv[j], acc[i][j]);
+        }
+        if (kt + 1 < nk) sstore(buf ^ 1);
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < TM; i++) {
+        int m = m0 + ty * TM + i;
+        if (m >= M) continue;
+        size_t crow = a.cnt ? (size_t)seg * a.c_seg_rows + m : (size_t)m;
+        float *c = a.C + crow * a.ldc;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            int nb = n0 + 64 * h + tx * 4;
+            if (EPI == EPI_SWIGLU) {
+#pragma unroll
+                for (int p = 0; p < 4; p += 2)
+                    if (nb + p + 1 < a.N) c[(nb + p) >> 1] = __fmul_rn(silu_ref(acc[i][4 * h + p]), acc[i][4 * h + p + 1]);
+            } else {
+#pragma unroll
+                for (int p = 0; p < 4; p++) {
+                    int n = nb + p;
+                    if (n < a.N) {
+                        if (EPI == EPI_ADD) c[n] = __fadd_rn(c[n], acc[i][4 * h + p]);
+                        else c[n] = acc[i][4 * h + p];
+                    }
+                }
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------
+// RoPE on q and k heads of the fused qkv row, then append k and v to the cache at pos.
+// Own model: NeoX-half pairs from the alloc_run cache (janusdoe.c:536, 864-873, 893-897).
+// Host: NORM (2i,2i+1) or NEOX pairs (janusdoe.c:3198-3224).
+struct RopeArgs {
+    float *qkv;
+    int ld;          // row stride of qkv
+    int H, KVH, HD;
+    const float *cos_t, *sin_t;  // [max_seq][HD/2]
+    int pair_norm;
+    const int *pos;
+    int max_seq;
+    float *kc, *vc;  // layer base; slot b at + b*bstride, position t at + t*kd
+    long bstride;
+    int *err;
+};
+__global__ void k_rope_kv(RopeArgs a) {
+    const int b = blockIdx.x, p = a.pos[b];
+    if (p < 0 || p >= a.max_seq) {
+        if (threadIdx.x == 0) atomicOr(a.err, JDG_ERR_POS);
+        return;
+    }
+    const int half = a.HD >> 1, kd = a.KVH * a.HD, qd = a.H * a.HD;
+    float *row = a.qkv + (size_t)b * a.ld;
+    const float *ct = a.cos_t + (size_t)p * half, *st = a.sin_t + (size_t)p * half;
+    float *kdst = a.kc + (size_t)b * a.bstride + (size_t)p * kd;
+    float *vdst = a.vc + (size_t)b * a.bstride + (size_t)p * kd;
+    const int npair = (a.H + a.KVH) * half;
+    for (int idx = threadIdx.x; idx < npair; idx += blockDim.x) {
+        int h = idx / half, i = idx - h * half;
+        int i0 = a.pair_norm ? 2 * i : i, i1 = a.pair_norm ? 2 * i + 1 : i + half;
+        float *v = row + (size_t)h * a.HD;  // q heads then k heads are contiguous
+        float x0 = v[i0], x1 = v[i1], c = ct[i], s = st[i];
+        float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+        float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+        if (h < a.H) {
+            v[i0] = y0;
+            v[i1] = y1;
+        } else {
+            int kh = h - a.H;
+            kdst[kh * a.HD + i0] = y0;
+            kdst[kh * a.HD + i1] = y1;
+        }
+    }
+    const float *vsrc = row + qd + kd;
+    for (int i = threadIdx.x; i < kd; i += blockDim.x) vdst[i] = vsrc[i];
+}
+
+// ------------------------------------------------------------------------------------
+// Decode attention over t <= pos, split into chunks of 64 positions (flash-decoding):
+// s_t = (q.k_t)*scale*bias, clamp*tanh(s/clamp) when clamp > 0 (janusdoe.c:899-910, own
+// model), no clamp for host (janusdoe.c:3226-3252); softmax; o = sum a_t v_t.  Each CTA
+// writes (unnormalised o, chunk max, chunk sum) per head; k_attn_combine merges chunks.
+struct AttnArgs {
+    const float *qkv;
+    int ld;
+    const float *kc, *vc;
+    long bstride;
+    const int *pos;
+    int H, KVH, HD, hg, nchunk;
+    float scale, bias, clamp, inv_clamp;
+    float *part;  // [B][H][nchunk][HD+2]
+};
+template <int HD>
+__global__ __launch_bounds__(128) void k_attn_partial(AttnArgs a) {
+    constexpr int E = HD / 32;  // dims per lane
+    const int c = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+    const int p = a.pos[b], t0 = c * kAttnChunk;
+    if (t0 > p) return;
+    const int nt = min(kAttnChunk, p + 1 - t0);
+    const int kd = a.KVH * HD, hg = a.hg;
+    __shared__ __align__(16) float q_s[kMaxHG][HD];
+    __shared__ float s_s[kMaxHG][kAttnChunk];
+    __shared__ __align__(16) float o_s[4][kMaxHG][HD];
+    const float *qrow = a.qkv + (size_t)b * a.ld + (size_t)g * hg * HD;
+    for (int i = threadIdx.x; i < hg * HD; i += blockDim.x) q_s[i / HD][i % HD] = qrow[i];
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float *kbase = a.kc + (size_t)b * a.bstride + (size_t)t0 * kd + (size_t)g * HD;
+    const float *vbase = a.vc + (size_t)b * a.bstride + (size_t)t0 * kd + (size_t)g * HD;
+    for (int t = warp; t < nt; t += 4) {
+        const float *kr = kbase + (size_t)t * kd + lane * E;
+        float kv[E];
+#pragma unroll
+        for (int e = 0; e < E; e++) kv[e] = kr[e];
+        for (int j = 0; j < hg; j++) {
+            float d = 0.f;
+#pragma unroll
+            for (int e = 0; e < E; e++) d = fmaf(q_s[j][lane * E + e], kv[e], d);
+            d = warp_sum(d);
+            if (lane == 0) {
+                float s = __fmul_rn(d, a.scale);
+                if (a.bias != 1.0f) s = __fmul_rn(s, a.bias);
+                if (a.clamp > 0.f) s = __fmul_rn(a.clamp, tanhf(__fmul_rn(s, a.inv_clamp)));
+                s_s[j][t] = s;
+            }
+        }
+    }
+    __syncthreads();
+    __shared__ float m_s[kMaxHG], l_s[kMaxHG];
+    for (int j = warp; j < hg; j += 4) {
+        float m = -INFINITY;
+        for (int t = lane; t < nt; t += 32) m = fmaxf(m, s_s[j][t]);
+        m = warp_max(m);
+        float l = 0.f;
+        for (int t = lane; t < nt; t += 32) {
+            float e = expf(s_s[j][t] - m);
+            s_s[j][t] = e;
+            l += e;
+        }
+        l = warp_sum(l);
+        if (lane == 0) {
+            m_s[j] = m;
+            l_s[j] = l;
+        }
+    }
+    __syncthreads();
+    float o[kMaxHG][E];
+#pragma unroll
+    for (int j = 0; j < kMaxHG; j++)
+#pragma unroll
+        for (int e = 0; e < E; e++) o[j][e] = 0.f;
+    for (int t = warp; t < nt; t += 4) {
+        const float *vr = vbase + (size_t)t * kd + lane * E;
+        float vv[E];
+#pragma unroll
+        for (int e = 0; e < E; e++) vv[e] = vr[e];
+#pragma unroll
+        for (int j = 0; j < kMaxHG; j++) {
+            if (j < hg) {
+                float pj = s_s[j][t];
+#pragma unroll
+                for (int e = 0; e < E; e++) o[j][e] = fmaf(pj, vv[e], o[j][e]);
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kMaxHG; j++)
+        if (j < hg)
+#pragma unroll
+            for (int e = 0; e < E; e++) o_s[warp][j][lane * E + e] = o[j][e];
+    __syncthreads();
+    for (int i = threadIdx.x; i < hg * HD; i += blockDim.x) {
+        int j = i / HD, d = i % HD;
+        float v = o_s[0][j][d] + o_s[1][j][d] + o_s[2][j][d] + o_s[3][j][d];
+        int h = g * hg + j;
+        float *dst = a.part + (((size_t)b * a.H + h) * a.nchunk + c) * (HD + 2);
+        dst[d] = v;
+        if (d == 0) {
+            dst[HD] = m_s[j];
+            dst[HD + 1] = l_s[j];
+        }
+    }
+}
+
+// merge chunk partials: o = sum_c o_c e^{m_c-M} / sum_c l_c e^{m_c-M}; grid (H, B), block HD
+__global__ void k_attn_combine(const float *__restrict__ part, const int *__restrict__ pos, int H, int HD, int nchunk,
+                               float *__restrict__ out, int ldo) {
+    const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    const int nc = pos[b] / kAttnChunk + 1;
+    const float *pp = part + ((size_t)b * H + h) * nchunk * (HD + 2);
+    float M = -INFINITY;
+    for (int c = 0; c < nc; c++) M = fmaxf(M, pp[c * (HD + 2) + HD]);
+    float S = 0.f, o = 0.f;
+    for (int c = 0; c < nc; c++) {
+        float f = expf(pp[c * (HD + 2) + HD] - M);
+        S = fmaf(pp[c * (HD + 2) + HD + 1], f, S);
+        o = fmaf(pp[c * (HD + 2) + d], f, o);
+    }
+    if (d < HD) out[(size_t)b * ldo + h * HD + d] = o / S;
+}
+
+// ------------------------------------------------------------------------------------
+// Parliament election, one CTA per sequence (janusdoe.c:779-838 own; janusdoe.c:3054-3087
+// host).  Own: xb = rmsnorm(x, ffn_norm) first (janusdoe.c:915) and the votes read xb.
+// Host: the votes read the attention-norm output xn.  Votes are fp32 dots; the scalar
+// election (mean, var, consensus EMA, variable k, strict-> top-k, softmax) runs on one
+// thread in the reference's order.  The harmonic term is 0 during decode.
+struct ElectArgs {
+    const float *x;        // own: residual (normed here); host: xn (used as is)
+    const float *norm_w;   // own: ffn_norm
+    float eps;
+    int D;
+    int host;              // 1 = host_parliament_elect rules
+    const float *w_vote;   // [16][D]
+    const int *alive;      // [16]
+    float temperature;
+    float *consensus;      // [B][L]
+    int L, l;
+    float *xb;             // own: normed output [B][D]
+    int *kcnt;             // [B]
+    int *sel;              // [B][16]
+    float *selw;           // [B][16]
+    int *tr_k, *tr_sel;
+    float *tr_w, *tr_ema;  // [B][L](*16)
+};
+__global__ __launch_bounds__(256) void k_elect(ElectArgs a) {
+    extern __shared__ float xs[];
+    __shared__ float red[32];
+    __shared__ float votes[kMaxE];
+    const int b = blockIdx.x, D = a.D;
+    const float *xr = a.x + (size_t)b * D;
+    if (!a.host) {
+        float ss = 0.f;
+        for (int i = threadIdx.x; i < D; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+        ss = block_sum(ss, red);
+        float inv = 1.0f / sqrtf(ss / (float)D + a.eps);
+        for (int i = threadIdx.x; i < D; i += blockDim.x) {
+            float v = __fmul_rn(__fmul_rn(xr[i], inv), a.norm_w[i]);
+            xs[i] = v;
+            a.xb[(size_t)b * D + i] = v;
+        }
+    } else {
+        for (int i = threadIdx.x; i < D; i += blockDim.x) xs[i] = xr[i];
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int e = warp; e < kMaxE; e += nw) {
+        if (!a.alive[e]) continue;
+        const float *wr = a.w_vote + (size_t)e * D;
+        float d = 0.f;
+        for (int i = lane; i < D; i += 32) d = fmaf(wr[i], xs[i], d);
+        d = warp_sum(d);
+        if (lane == 0) votes[e] = d;
+    }
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    int alive_idx[kMaxE], na = 0;
+    for (int e = 0; e < kMaxE; e++)
+        if (a.alive[e]) alive_idx[na++] = e;
+    float *cons = a.consensus + (size_t)b * a.L + a.l;
+    int k = 0;
+    int sel[kMaxE];
+    float w[kMaxE];
+    if (a.host && na == 1) {
+        k = 1;
+        sel[0] = alive_idx[0];
+        w[0] = 1.0f;
+    } else if ((!a.host && na >= 2) || (a.host && na >= 2)) {
+        float v[kMaxE];
+        for (int i = 0; i < na; i++) {
+            int e = alive_idx[i];
+            float d = votes[e];
+            if (a.host && !isfinite(d)) d = -1e30f;
+            v[e] = d;  // own: dot + 0.1f * 0 (harmonic state is zero at decode)
+        }
+        float mean = 0.f;
+        for (int i = 0; i < na; i++) mean = __fadd_rn(mean, v[alive_idx[i]]);
+        mean = mean / (float)na;
+        float var = 0.f;
+        for (int i = 0; i < na; i++) {
+            float dd = __fsub_rn(v[alive_idx[i]], mean);
+            var = __fadd_rn(var, __fmul_rn(dd, dd));
+        }
+        var = var / (float)na;
+        float cs = fminf(1.0f, sqrtf(__fadd_rn(var, 1e-8f)) / __fadd_rn(fabsf(mean), 1.0f));
+        float ema = __fadd_rn(__fmul_rn(0.9f, *cons), __fmul_rn(0.1f, cs));
+        *cons = ema;
+        k = (int)__fmul_rn((float)na, __fsub_rn(1.0f, ema));
+        if (k < 2) k = 2;
+        if (k > na) k = na;
+        bool used[kMaxE];
+        for (int e = 0; e < kMaxE; e++) used[e] = false;
+        for (int ki = 0; ki < k; ki++) {
+            float bv = -1e30f;
+            int bi = a.host ? -1 : 0;
+            for (int i = 0; i < na; i++) {
+                int e = alive_idx[i];
+                if (!used[e] && v[e] > bv) {
+                    bv = v[e];
+                    bi = e;
+                }
+            }
+            if (bi < 0)
+                for (int i = 0; i < na; i++)
+                    if (!used[alive_idx[i]]) {
+                        bi = alive_idx[i];
+                        break;
+                    }
+            sel[ki] = bi;
+            w[ki] = v[bi];
+            used[bi] = true;
+        }
+        float temp = a.host ? 1.0f : (a.temperature > 0.05f ? a.temperature : 1.0f);
+        float mx = w[0];
+        for (int i = 1; i < k; i++)
+            if (w[i] > mx) mx = w[i];
+        float sum = 0.f;
+        for (int i = 0; i < k; i++) {
+            float arg = __fsub_rn(w[i], mx);
+            if (!a.host) arg = arg / temp;
+            w[i] = expf(arg);
+            sum = __fadd_rn(sum, w[i]);
+        }
+        if (!a.host || (sum > 0.0f && isfinite(sum))) {
+            for (int i = 0; i < k; i++) w[i] = w[i] / sum;
+        } else {
+            for (int i = 0; i < k; i++) w[i] = 1.0f / (float)k;
+        }
+    }
+    a.kcnt[b] = k;
+    for (int i = 0; i < kMaxE; i++) {
+        a.sel[b * kMaxE + i] = i < k ? sel[i] : -1;
+        a.selw[b * kMaxE + i] = i < k ? w[i] : 0.f;
+    }
+    size_t tl = (size_t)b * a.L + a.l;
+    a.tr_k[tl] = k;
+    a.tr_ema[tl] = *cons;
+    for (int i = 0; i < kMaxE; i++) {
+        a.tr_sel[tl * kMaxE + i] = i < k ? sel[i] : -1;
+        a.tr_w[tl * kMaxE + i] = i < k ? w[i] : 0.f;
+    }
+}
+
+// ------------------------------------------------------------------------------------
+// Bucket (sequence, election slot) pairs by expert, in ascending sequence order.
+// grid 1, block 512 (warp e = expert slot).  idx[e*B + j] = b; pairrow[b*16+ki] = e*B + j.
+__global__ __launch_bounds__(512) void k_route(const int *__restrict__ kcnt, const int *__restrict__ sel, int B,
+                                               int *__restrict__ cnt, int *__restrict__ idx, int *__restrict__ pairrow,
+                                               int *err) {
+    const int e = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int n = 0;
+    for (int b0 = 0; b0 < B; b0 += 32) {
+        int b = b0 + lane, ki = -1;
+        if (b < B) {
+            int k = kcnt[b];
+            for (int i = 0; i < k; i++)
+                if (sel[b * kMaxE + i] == e) ki = i;
+        }
+        unsigned m = __ballot_sync(JDG_FULL, ki >= 0);
+        if (ki >= 0) {
+            int j = n + __popc(m & ((1u << lane) - 1));
+            idx[e * B + j] = b;
+            pairrow[b * kMaxE + ki] = e * B + j;
+        }
+        n += __popc(m);
+    }
+    if (lane == 0) cnt[e] = n;
+    (void)err;
+}
+
+// x[b] += sum_ki w[b][ki] * y[pairrow(b,ki)] in election order (janusdoe.c:927-929)
+__global__ void k_combine(const int *__restrict__ kcnt, const float *__restrict__ selw, const int *__restrict__ pairrow,
+                          const float *__restrict__ y, int D, float *__restrict__ x) {
+    const int b = blockIdx.x, k = kcnt[b];
+    for (int r = threadIdx.x; r < D; r += blockDim.x) {
+        float eo = 0.f;
+        for (int ki = 0; ki < k; ki++)
+            eo = __fadd_rn(eo, __fmul_rn(selw[b * kMaxE + ki], y[(size_t)pairrow[b * kMaxE + ki] * D + r]));
+        x[(size_t)b * D + r] = __fadd_rn(x[(size_t)b * D + r], eo);
+    }
+}
+
+// ------------------------------------------------------------------------------------
+// Next token per sequence (one CTA, 1024 threads): the prompt's next id while it lasts
+// (sequential prefill, janusdoe.c:3660), else greedy first-index argmax (janusdoe.c:3637,
+// 3374-3375) or sample() with temperature and top-k (janusdoe.c:3638-3645) using the
+// sequence's own xorshift state.  Advances tok/pos and appends generated ids to history.
+struct PickArgs {
+    const float *logits;
+    int V, ldl;
+    float temp;
+    int top_k;
+    int *tok, *pos;
+    uint64_t *rng;
+    const int *plen, *prompt;
+    int Pmax;
+    int *hist, *hist_n;
+    int Hmax;
+    int *next_out;
+};
+__device__ __forceinline__ uint32_t f2key(float f) {
+    uint32_t u = __float_as_uint(f);
+    if (u == 0x80000000u) u = 0;
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key2f(uint32_t k) {
+    uint32_t u = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
+    return __uint_as_float(u);
+}
+constexpr int kCandCap = 2048;
+__global__ __launch_bounds__(1024) void k_pick(PickArgs a) {
+    const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float *lg = a.logits + (size_t)b * a.ldl;
+    const int V = a.V;
+    const int p = a.pos[b];
+    __shared__ int s_next;
+    __shared__ float rv[32];
+    __shared__ int ri[32];
+    __shared__ uint32_t hist[256];
+    __shared__ uint32_t s_prefix, s_mask, s_rank;
+    __shared__ int cand[kCandCap];
+    __shared__ int s_ncand;
+    __shared__ int wcount[32];
+    const bool from_prompt = a.plen && (p + 1 < a.plen[b]);
+    if (from_prompt) {
+        if (tid == 0) s_next = a.prompt[(size_t)b * a.Pmax + p + 1];
+    } else if (a.temp <= 0.f) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int i = tid; i < V; i += blockDim.x) {
+            float v = lg[i];
+            if (v > bv || (v == bv && i < bi)) {
+                bv = v;
+                bi = i;
+            }
+        }
+        for (int o = 16; o; o >>= 1) {
+            float ov = __shfl_xor_sync(JDG_FULL, bv, o);
+            int oi = __shfl_xor_sync(JDG_FULL, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (lane == 0) {
+            rv[warp] = bv;
+            ri[warp] = bi;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            float best = rv[0];
+            int bidx = ri[0];
+            for (int w = 1; w < (int)(blockDim.x >> 5); w++)
+                if (rv[w] > best || (rv[w] == best && ri[w] < bidx)) {
+                    best = rv[w];
+                    bidx = ri[w];
+                }
+            s_next = bidx == 0x7fffffff ? 0 : bidx;
+        }
+    } else {
+        // logits[i] /= temp, then the top_k-th largest value th by radix select
+        const float temp = a.temp;
+        const bool use_topk = a.top_k > 0 && a.top_k < V;
+        float th = -INFINITY;
+        if (use_topk) {
+            if (tid == 0) {
+                s_prefix = 0;
+                s_mask = 0;
+                s_rank = (uint32_t)a.top_k;
+            }
+            for (int shift = 24; shift >= 0; shift -= 8) {
+                for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+                __syncthreads();
+                uint32_t prefix = s_prefix, mask = s_mask;
+                for (int i = tid; i < V; i += blockDim.x) {
+                    uint32_t k = f2key(lg[i] / temp);
+                    if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1u);
+                }
+                __syncthreads();
+                if (tid == 0) {
+                    uint32_t rank = s_rank;
+                    for (int d = 255; d >= 0; d--) {
+                        if (rank <= hist[d]) {
+                            s_prefix = prefix | ((uint32_t)d << shift);
+                            s_mask = mask | (255u << shift);
+                            break;
+                        }
+                        rank -= hist[d];
+                    }
+                    s_rank = rank;
+                }
+                __syncthreads();
+            }
+            th = key2f(s_prefix);
+        }
+        // candidates: !(l < th), compacted in index order
+        if (tid == 0) s_ncand = 0;
+        __syncthreads();
+        bool overflow = false;
+        for (int base = 0; base < V; base += blockDim.x) {
+            int i = base + tid;
+            bool is_c = false;
+            if (i < V) {
+                float l = lg[i] / temp;
+                is_c = !use_topk || !(l < th);
+            }
+            unsigned m = __ballot_sync(JDG_FULL, is_c);
+            if (lane == 0) wcount[warp] = __popc(m);
+            __syncthreads();
+            int off = s_ncand;
+            for (int w = 0; w < warp; w++) off += wcount[w];
+            if (is_c) {
+                int j = off + __popc(m & ((1u << lane) - 1));
+                if (j < kCandCap) cand[j] = i;
+            }
+            __syncthreads();
+            if (tid == 0) {
+                int tot = 0;
+                for (int w = 0; w < (int)(blockDim.x >> 5); w++) tot += wcount[w];
+                s_ncand += tot;
+            }
+            __syncthreads();
+        }
+        overflow = s_ncand > kCandCap;
+        if (tid == 0) {
+            // softmax_n over the masked logits (janusdoe.c:534) restricted to the non-zero
+            // terms, summed in index order, then the CDF scan with r = rand_uniform()
+            int n = s_ncand;
+            float mx = -INFINITY;
+            if (!overflow) {
+                for (int j = 0; j < n; j++) mx = fmaxf(mx, lg[cand[j]] / temp);
+            } else {
+                for (int i = 0; i < V; i++) {
+                    float l = lg[i] / temp;
+                    if (!use_topk || !(l < th)) mx = fmaxf(mx, l);
+                }
+            }
+            float s = 0.f;
+            if (!overflow) {
+                for (int j = 0; j < n; j++) s = __fadd_rn(s, expf(__fsub_rn(lg[cand[j]] / temp, mx)));
+            } else {
+                for (int i = 0; i < V; i++) {
+                    float l = lg[i] / temp;
+                    if (!use_topk || !(l < th)) s = __fadd_rn(s, expf(__fsub_rn(l, mx)));
+                }
+            }
+            uint64_t st = a.rng[b];
+            float r = xs_uniform(st);
+            a.rng[b] = st;
+            int pick = V - 1;
+            float cum = 0.f;
+            if (r <= 0.f) pick = 0;
+            else if (!overflow) {
+                for (int j = 0; j < n; j++) {
+                    cum = __fadd_rn(cum, expf(__fsub_rn(lg[cand[j]] / temp, mx)) / s);
+                    if (cum >= r) {
+                        pick = cand[j];
+                        break;
+                    }
+                }
+            } else {
+                for (int i = 0; i < V; i++) {
+                    float l = lg[i] / temp;
+                    if (use_topk && l < th) continue;
+                    cum = __fadd_rn(cum, expf(__fsub_rn(l, mx)) / s);
+                    if (cum >= r) {
+                        pick = i;
+                        break;
+                    }
+                }
+            }
+            s_next = pick;
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int nx = s_next;
+        a.tok[b] = nx;
+        a.pos[b] = p + 1;
+        if (a.next_out) a.next_out[b] = nx;
+        if (!from_prompt && a.hist) {
+            int hn = a.hist_n[b];
+            if (hn < a.Hmax) a.hist[(size_t)b * a.Hmax + hn] = nx;
+            a.hist_n[b] = hn + 1;
+        }
+    }
+}
+
+}  // namespace jdg
