@@ -1,0 +1,343 @@
+"""Decode throughput of the janus.DoE token loop on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+One "step" is one decode step of the whole batch (one token per sequence) after a
+sequential prefill of the prompt.  Workloads (synthetic seeded weights, uniform-random
+prompts):
+  depth12_bs1    (default) own model depth 12 (dim 768, 12/4 heads, 8 experts with 5-8 alive
+                 per layer, vocab 8256, ctx 1024), 512-token prompt, greedy, batch 1 per GPU
+  depth12_bs256  same model, 256 sequences per GPU
+  depth4_bs1     depth 4 (dim 256, 4 experts, vocab 2256), 32-token prompt, greedy
+  depth8_bs64    depth 8 (dim 512, 8/4 heads, 6 experts, vocab 4256), 64 sequences,
+                 64-token prompt, temperature 0.8 / top-k 40
+Sequences are independent, so N GPUs each run their own batch (weak scaling, no collective).
+`value` is device-timed (CUDA events on the engine's stream, max over ranks); `e2e` goes
+through the public step call with host buffers (pinned H2D of token/position, D2H of the
+next token every step).
+"""
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "decode tok/s (bs1, bs256) depth-12 & host Q4_K 8B; % of HBM roofline"
+
+WORKLOADS = {
+    "depth12_bs1": dict(depth=12, over=dict(n_kv_heads=4, vocab_size=8256, seq_len=1024), masks=True, seed=2,
+                        B=1, prompt=512, temp=0.0, top_k=0, steps=256, warmup=8, ref_decode=64),
+    "depth12_bs256": dict(depth=12, over=dict(n_kv_heads=4, vocab_size=8256, seq_len=1024), masks=True, seed=2,
+                          B=256, prompt=512, temp=0.0, top_k=0, steps=32, warmup=4, ref_decode=8),
+    "depth4_bs1": dict(depth=4, over=dict(vocab_size=2256, seq_len=256), masks=False, seed=0,
+                       B=1, prompt=32, temp=0.0, top_k=0, steps=128, warmup=8, ref_decode=128),
+    "depth8_bs64": dict(depth=8, over=dict(n_kv_heads=4, vocab_size=4256, seq_len=512), masks=False, seed=1,
+                        B=64, prompt=64, temp=0.8, top_k=40, steps=128, warmup=8, ref_decode=32),
+}
+
+
+def load_pkg():
+    import importlib.util
+    name = "janus_doe_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    pkg = os.path.join(ROOT, "janus.doe_b200")
+    spec = importlib.util.spec_from_file_location(name, os.path.join(pkg, "__init__.py"),
+                                                  submodule_search_locations=[pkg])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def dram_traffic(workload):
+    p = os.path.join(ROOT, "profiles", "dram_traffic.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        if workload in d:
+            return d[workload]
+    return None
+
+
+class Clocks:
+    """nvidia-smi sampler for the timed region (SM clock and throttle reasons)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx, self.rows, self.proc = gpu_index, [], None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), "--query-gpu=" + self.Q,
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.th = threading.Thread(target=self._read, daemon=True)
+            self.th.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm = [float(r[1]) for r in self.rows if len(r) >= 8 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) >= 8 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) >= 8 for i in range(4) if r[4 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world == 1:
+        return None, 1, 0, 0
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    return dist, world, rank, local
+
+
+def barrier(dist):
+    if dist is not None:
+        import torch
+        dist.barrier()
+        torch.cuda.synchronize()
+
+
+def allmax(dist, v):
+    if dist is None:
+        return v
+    import torch
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def prompts_for(w, rank):
+    """Uniform-random prompt ids per sequence from splitmix64(seed*1000 + s)."""
+    V = w["over"]["vocab_size"]
+    B, P = w["B"], w["prompt"]
+    out = np.zeros((B, P), np.int32)
+    rngs = np.zeros(B, np.uint64)
+    for b in range(B):
+        s = w["seed"] * 1000 + rank * B + b
+        x = _splitmix(s)
+        for i in range(P):
+            x = _xs(x)
+            out[b, i] = x % V
+        rngs[b] = x
+    return out, rngs
+
+
+M64 = (1 << 64) - 1
+
+
+def _splitmix(x):
+    z = (x + 0x9E3779B97F4A7C15) & M64
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & M64
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & M64
+    z = z ^ (z >> 31)
+    return z or 1
+
+
+def _xs(x):
+    x ^= (x << 13) & M64
+    x ^= x >> 7
+    x ^= (x << 17) & M64
+    return x & M64
+
+
+def own_bytes(cfg, alive_counts, B, steps, stats):
+    """Algorithmic HBM bytes of `steps` decode steps (f32 weights and KV):
+    per step every attention matrix, norm and alive vote row, the LM head, the gathered
+    embedding rows; per (step, layer) the experts read (union over the batch, counted on
+    the device); KV read (sum of pos+1 over sequences, counted on the device) + append."""
+    D, H, V, L = cfg.dim, cfg.hidden_dim, cfg.vocab_size, cfg.depth
+    qd, kd = cfg.n_heads * cfg.head_dim, cfg.n_kv_heads * cfg.head_dim
+    fixed = 4 * (V * D + D + B * D)
+    for l in range(L):
+        fixed += 4 * (2 * D + (qd + 2 * kd) * D + D * qd + alive_counts[l] * D)
+    experts, kvpos, nsteps = stats
+    return steps * fixed + experts * 3 * H * D * 4 + kvpos * L * 2 * kd * 4 + steps * B * L * 2 * kd * 4
+
+
+def cpu_reference(w, n_decode, threads):
+    """Time the reference's own decode (janusdoe.c forward_token + greedy/sample, OpenBLAS
+    build from oracle/_ref) on the host cores: one sequence, prefill untimed, n_decode
+    decode tokens timed."""
+    os.environ["OPENBLAS_NUM_THREADS"] = str(threads)
+    sys.path.insert(0, ROOT)
+    from oracle.oracle import Reference
+    try:
+        ref = Reference("_blas")
+        kind = "reference"
+    except RuntimeError:
+        ref = Reference("")
+        kind = "reference"
+    ov = w["over"]
+    ref.own_setup(w["depth"], ov.get("n_kv_heads", 0), ov["vocab_size"], ov.get("seq_len", 256), w["seed"], 0.02,
+                  w["masks"])
+    pr, rngs = prompts_for(dict(w, B=1), 0)
+    pos, lg = 0, None
+    for t in pr[0]:
+        lg, _ = ref.own_forward(int(t), pos)
+        pos += 1
+    st = int(rngs[0])
+    t0 = time.perf_counter()
+    for _ in range(n_decode):
+        if w["temp"] > 0:
+            nxt, st = ref.sample(lg, w["temp"], w["top_k"], st)
+        else:
+            nxt = int(np.argmax(lg))
+        lg, _ = ref.own_forward(nxt, pos)
+        pos += 1
+    dt = time.perf_counter() - t0
+    return n_decode / dt, kind, "1 sequence, %d-token prefill untimed, %d decode tokens timed (positions %d-%d)" % (
+        w["prompt"], n_decode, w["prompt"], w["prompt"] + n_decode - 1)
+
+
+def run_reference_arm(args, w):
+    dist, world, rank, local = dist_setup()
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    n = max(1, min(args.steps, w["ref_decode"] * 4))
+    tps, kind, sample = cpu_reference(w, n, threads)
+    line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": n, "warmup": args.warmup, "ms_per_step": 1000.0 / tps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.workload, "batch_per_gpu": 1, "prompt": w["prompt"]},
+            "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": kind, "sample": sample},
+            "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
+    ap.add_argument("--workload", default="depth12_bs1", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    w = WORKLOADS[args.workload]
+    args.steps = w["steps"] if args.steps is None else args.steps
+    args.warmup = w["warmup"] if args.warmup is None else max(3, args.warmup)
+    if args.impl == "reference":
+        run_reference_arm(args, w)
+        return
+    dist, world, rank, local = dist_setup()
+    jd = load_pkg()
+    B, P = w["B"], w["prompt"]
+    cfg = jd.config_from_depth(w["depth"], **w["over"])
+    if P + args.warmup + args.steps + min(args.steps, 64) + 1 > cfg.seq_len:
+        args.steps = max(1, (cfg.seq_len - P - args.warmup - 2) * 2 // 3)
+    ctx = jd.Context(local)
+    model = jd.Model.seeded(cfg, w["seed"], 0.02, w["masks"])
+    alive = [sum(model.alive(l)) for l in range(cfg.depth)]
+    eng = jd.Engine.own(ctx, model, B)
+    eng.set_sampling(w["temp"], w["top_k"])
+    prompts, rngs = prompts_for(w, rank)
+    # prefill (sequential, timed separately)
+    eng.set_prompt(prompts, [P] * B, rngs)
+    prefill_ms = eng.run(B, P - 1)
+    # warm-up decode steps
+    eng.run(B, args.warmup)
+    # timed decode steps
+    clocks = Clocks(local)
+    barrier(dist)
+    eng.reset_stats()
+    l0 = eng.launches()
+    clocks.start()
+    ms = eng.run(B, args.steps)
+    ck = clocks.stop()
+    n_launch = eng.launches() - l0
+    stats = eng.stats()
+    ms = allmax(dist, ms)
+    barrier(dist)
+    tok = B * args.steps * world
+    value = tok / (ms / 1000.0)
+    # e2e through the public step call with host buffers
+    n_e2e = min(args.steps, 64)
+    tok_h, pos_h = eng.state(B)
+    rng_h = None if w["temp"] <= 0 else np.array(rngs, np.uint64)
+    barrier(dist)
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        nxt, rng_h, _, _ = eng.step(tok_h, pos_h, rng=rng_h)
+        tok_h = nxt
+        pos_h = pos_h + 1
+    e2e_s = allmax(dist, time.perf_counter() - t0)
+    barrier(dist)
+    e2e = B * n_e2e * world / e2e_s
+    # roofline: algorithmic bytes per step / device time per step (the decode step graph)
+    bytes_run = own_bytes(cfg, alive, B, args.steps, stats)
+    peak, peak_kind = peaks()
+    achieved = bytes_run / (ms / 1000.0) / 1e9
+    traffic = dram_traffic(args.workload)
+    roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "traffic": traffic, "peak_source": peak_kind,
+            "kernel": "whole decode step (CUDA graph of %d launches)" % (n_launch // max(1, args.steps)),
+            "algorithmic_bytes_per_step": bytes_run / args.steps}
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,0.02) weights, uniform prompts)",
+            "config": {"workload": args.workload, "depth": cfg.depth, "dim": cfg.dim, "heads": cfg.n_heads,
+                       "kv_heads": cfg.n_kv_heads, "experts_alive": alive, "vocab": cfg.vocab_size,
+                       "ctx": cfg.seq_len, "batch_per_gpu": B, "global_batch": B * world, "prompt": P,
+                       "positions": [P + args.warmup, P + args.warmup + args.steps - 1],
+                       "sampling": "greedy" if w["temp"] <= 0 else "temp %.1f top-k %d" % (w["temp"], w["top_k"]),
+                       "parallelism": "dp%d (independent sequences)" % world,
+                       "l2": "inputs larger than L2: %.0f MB of weights+KV per step vs 126 MB L2" % (
+                           bytes_run / args.steps / 1e6)},
+            "roofline": roof, "prefill_ms": prefill_ms, "clocks": ck, "gpu_launches": n_launch,
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B,
+                    "steps": n_e2e}}
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        tps, kind, sample = cpu_reference(w, w["ref_decode"], threads)
+        line["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": threads, "kind": kind, "sample": sample}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    eng.close()
+    model.close()
+    ctx.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -205,6 +205,11 @@ int jdg_last_run_ms(jdg_engine *e, float *ms);
 /* Per-kernel device time of one more step (events around each launch of a step). */
 int jdg_profile_step(jdg_engine *e, int B, float *ms_by_kernel, int max_kernels, int *n_kernels,
                      const char **names);
+/* Device-side counters since the last jdg_reset_stats: [0] experts read (per step and
+ * layer, the union over the batch of elected experts), [1] KV positions read (sum over
+ * sequences of pos+1 per step), [2] decode steps. */
+int jdg_get_stats(jdg_engine *e, uint64_t *out3);
+int jdg_reset_stats(jdg_engine *e);
 /* Counts of this library's kernel launches since the engine was created. */
 int jdg_launch_count(jdg_engine *e, long long *n);
 

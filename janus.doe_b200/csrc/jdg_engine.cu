@@ -15,6 +15,7 @@
 #include "../../include/jdgpu.h"
 #include "jdg_engine.h"
 #include "jdg_kernels.cuh"
+#include "jdg_b1.cuh"
 
 using namespace jdg;
 
@@ -146,6 +147,16 @@ int jdg_alloc_state(jdg_engine *e) {
     DALLOC(e->tr_w, (size_t)B * L * kMaxE * 4);
     DALLOC(e->err, 4);
     CK(cudaMemsetAsync(e->err, 0, 4, e->st));
+    DALLOC(e->stats, 4 * 8);
+    CK(cudaMemsetAsync(e->stats, 0, 4 * 8, e->st));
+    if (cudaHostAlloc((void **)&e->pin_tok, (size_t)B * 12 + 64, cudaHostAllocDefault) != cudaSuccess) {
+        jdg_set_err(e->ctx, "cudaHostAlloc failed");
+        return JD_ENOMEM;
+    }
+    e->pin_pos = e->pin_tok + B;
+    e->pin_next = e->pin_pos + B;
+    DALLOC(e->tickets, 1024 * 4);
+    CK(cudaMemsetAsync(e->tickets, 0, 1024 * 4, e->st));
     CK(cudaMemsetAsync(e->tok, 0, B * 4, e->st));
     CK(cudaMemsetAsync(e->pos, 0, B * 4, e->st));
     CK(cudaMemsetAsync(e->plen, 0, B * 4, e->st));
@@ -318,7 +329,19 @@ int jdg_own_upload_impl(jdg_engine *e, const jd_model *m, int max_batch) {
     DALLOC(e->xb, (size_t)B * D * 4);
     DALLOC(e->qkv, (size_t)B * e->qkvd * 4);
     DALLOC(e->att, (size_t)B * e->qd * 4);
-    DALLOC(e->part, (size_t)B * e->Hh * e->nchunk * (e->HD + 2) * 4);
+    size_t part_a = (size_t)B * e->Hh * e->nchunk * (e->HD + 2);
+    size_t part_b = (size_t)e->Hh * (e->max_seq / kB1Chunk + 1) * (e->HD + 2);
+    DALLOC(e->part, (part_a > part_b ? part_a : part_b) * 4);
+    DALLOC(e->amax_v, ((size_t)V / 4 + 2) * 4);
+    DALLOC(e->amax_i, ((size_t)V / 4 + 2) * 4);
+    DALLOC(e->vpart, ((size_t)D / 4 + 2) * 17 * 4);
+    DALLOC(e->ffn_inv, 4);
+    {
+        const char *g = getenv("JDG_GENERIC");
+        e->force_generic = g && g[0] == '1';
+    }
+    e->b1_ok = D % 128 == 0 && H % 128 == 0 && D / 128 <= 8 && H / 128 <= 12 && e->qd == D && D <= 1024 &&
+               (e->HD == 64 || e->HD == 128) && D / 4 + 64 <= 1024 && e->max_seq <= 1024;
     DALLOC(e->hbuf, (size_t)B * kMaxE * H * 4);
     DALLOC(e->ybuf, (size_t)B * kMaxE * D * 4);
     DALLOC(e->logits, (size_t)B * V * 4);
@@ -432,6 +455,7 @@ void jdg_launch_pick(jdg_engine *e, int B) {
     pa.hist_n = e->hist_n;
     pa.Hmax = e->Hmax;
     pa.next_out = e->next_out;
+    pa.stats = e->stats;
     k_pick<<<B, 1024, 0, e->st>>>(pa);
     e->launches++;
 }
@@ -462,9 +486,97 @@ void jdg_launch_elect(jdg_engine *e, int l, int B, const float *xin, const float
     e->launches++;
 }
 
+
+// ------------------------------------------------------------------------------------
+// Batch-1 chain (jdg_b1.cuh), every kernel launched with programmatic stream serialization.
+template <typename... KArgs, typename... Args>
+static void launch_pdl(jdg_engine *e, void (*kern)(KArgs...), dim3 grid, dim3 block, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = e->st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, args...);
+    e->launches++;
+}
+
+#define NV_SWITCH(n, KERN, ...)                                        \
+    switch (n) {                                                       \
+    case 2: launch_pdl(e, KERN<2>, __VA_ARGS__); break;                \
+    case 4: launch_pdl(e, KERN<4>, __VA_ARGS__); break;                \
+    case 6: launch_pdl(e, KERN<6>, __VA_ARGS__); break;                \
+    default: launch_pdl(e, KERN<8>, __VA_ARGS__); break;               \
+    }
+#define NH_SWITCH(n, KERN, ...)                                        \
+    switch (n) {                                                       \
+    case 3: launch_pdl(e, KERN<3>, __VA_ARGS__); break;                \
+    case 4: launch_pdl(e, KERN<4>, __VA_ARGS__); break;                \
+    case 6: launch_pdl(e, KERN<6>, __VA_ARGS__); break;                \
+    case 8: launch_pdl(e, KERN<8>, __VA_ARGS__); break;                \
+    case 9: launch_pdl(e, KERN<9>, __VA_ARGS__); break;                \
+    default: launch_pdl(e, KERN<12>, __VA_ARGS__); break;              \
+    }
+
+static bool b1_shape_ok(jdg_engine *e) {
+    int nv = e->D / 128, nh = e->hidden / 128;
+    return e->b1_ok && (nv == 2 || nv == 4 || nv == 6 || nv == 8) &&
+           (nh == 3 || nh == 4 || nh == 6 || nh == 8 || nh == 9 || nh == 12);
+}
+
+static void enqueue_own_step_b1(jdg_engine *e) {
+    B1Args a = {};
+    a.tok_emb = e->tok_emb;
+    a.V = e->V; a.D = e->D; a.H = e->Hh; a.KVH = e->KVH; a.HD = e->HD; a.hidden = e->hidden;
+    a.qd = e->qd; a.kd = e->kd; a.qkvd = e->qkvd; a.max_seq = e->max_seq; a.L = e->L;
+    a.eps = e->eps; a.scale = 1.0f / sqrtf((float)e->HD); a.clamp = e->clamp;
+    a.inv_clamp = e->clamp > 0 ? 1.0f / e->clamp : 0.f;
+    a.rope_norm = 0; a.rope_cos = e->rope_cos; a.rope_sin = e->rope_sin;
+    a.output = e->output; a.output_norm = e->output_norm;
+    a.tok = e->tok; a.pos = e->pos; a.x = e->x; a.xb = e->xb; a.qkv = e->qkv; a.att = e->att; a.part = e->part;
+    a.hbuf = e->hbuf; a.ybuf = e->ybuf; a.logits = e->logits; a.kv_bstride = e->kv_bstride;
+    a.kcnt = e->kcnt; a.sel = e->sel; a.selw = e->selw; a.consensus = e->consensus;
+    a.tickets = e->tickets; a.amax_v = e->amax_v; a.amax_i = e->amax_i; a.vpart = e->vpart; a.ffn_inv = e->ffn_inv;
+    a.tok_out = e->tok; a.plen = e->plen; a.prompt = e->prompt; a.hist = e->hist; a.hist_n = e->hist_n;
+    a.next_out = e->next_out; a.Pmax = e->Pmax; a.Hmax = e->Hmax; a.err = e->err;
+    a.greedy_pick = e->temp <= 0.f;
+    a.stats = e->stats;
+    const int nv = e->D / 128, nh = e->hidden / 128;
+    const dim3 blk(128);
+    for (int l = 0; l < e->L; l++) {
+        LayerDev &ly = e->layers[l];
+        a.l = l;
+        a.attn_norm = ly.attn_norm; a.ffn_norm = ly.ffn_norm; a.wqkv = ly.wqkv; a.wo = ly.wo; a.w_vote = ly.w_vote;
+        a.alive = e->alive_dev + (size_t)l * kMaxE; a.temperature = ly.temperature;
+        a.gu_tab = e->gu_tab + (size_t)l * kMaxE; a.dn_tab = e->dn_tab + (size_t)l * kMaxE;
+        a.kc = e->kc + (size_t)l * e->max_seq * e->kd; a.vc = e->vc + (size_t)l * e->max_seq * e->kd;
+        a.tr_k = e->tr_k; a.tr_sel = e->tr_sel; a.tr_w = e->tr_w; a.tr_ema = e->tr_ema;
+        a.embed = l == 0;
+        NV_SWITCH(nv, k_b1_qkv, dim3((e->qkvd + 3) / 4), blk, a);
+        dim3 ga((e->max_seq + kB1Chunk - 1) / kB1Chunk, e->KVH);
+        if (e->HD == 64) launch_pdl(e, k_b1_attn<64>, ga, blk, a);
+        else launch_pdl(e, k_b1_attn<128>, ga, blk, a);
+        NV_SWITCH(nv, k_b1_wo, dim3((e->D + 3) / 4), blk, a);
+        if (e->n_alive[l] < 2) continue;
+        NV_SWITCH(nv, k_b1_ffn1, dim3((e->hidden + 3) / 4, e->n_alive[l]), blk, a);
+        NH_SWITCH(nh, k_b1_ffn2, dim3((e->D + 3) / 4, e->n_alive[l]), blk, a);
+    }
+    NV_SWITCH(nv, k_b1_lmhead, dim3((e->V + 7) / 8), blk, a);
+    if (!a.greedy_pick) jdg_launch_pick(e, 1);
+}
+
+
 // One own-model decode step for slots 0..B-1 (forward_token, janusdoe.c:879-934, then
 // the next-token pick).
 static void enqueue_own_step(jdg_engine *e, int B) {
+    if (B == 1 && b1_shape_ok(e) && !e->force_generic) {
+        enqueue_own_step_b1(e);
+        return;
+    }
     const int D = e->D, H = e->hidden, L = e->L, V = e->V, qd = e->qd;
     const float scale = 1.0f / sqrtf((float)e->HD);
     k_embed<<<B, 256, 0, e->st>>>(e->tok_emb, V, D, e->tok, e->x, e->err);
@@ -494,13 +606,15 @@ static void enqueue_own_step(jdg_engine *e, int B) {
         const float *const *dn = e->dn_tab + (size_t)l * kMaxE;
         if (e->n_alive[l] < 2) continue;  // parliament_elect returns 0 below MIN_EXPERTS
         if (B == 1) {
+            k_route<<<1, 512, 0, e->st>>>(e->kcnt, e->sel, B, e->rcnt, e->ridx, e->pairrow, e->stats);
+            e->launches++;
             dim3 g1((H + 3) / 4, e->n_alive[l]);
             k_expert_gu_b1<<<g1, 128, (size_t)D * 4, e->st>>>(gu, e->kcnt, e->sel, H, D, e->xb, e->hbuf, e->err);
             k_expert_down_b1<<<(D + 3) / 4, 128, (size_t)e->n_alive[l] * H * 4, e->st>>>(dn, e->kcnt, e->sel, e->selw, D,
                                                                                          H, e->hbuf, e->x);
             e->launches += 2;
         } else {
-            k_route<<<1, 512, 0, e->st>>>(e->kcnt, e->sel, B, e->rcnt, e->ridx, e->pairrow, e->err);
+            k_route<<<1, 512, 0, e->st>>>(e->kcnt, e->sel, B, e->rcnt, e->ridx, e->pairrow, e->stats);
             SgemmArgs a = {};
             a.A = e->xb; a.lda = D; a.idx = e->ridx; a.ldi = B; a.cnt = e->rcnt; a.Wtab = gu; a.N = 2 * H; a.K = D;
             a.C = e->hbuf; a.ldc = H; a.c_seg_rows = B;
@@ -600,6 +714,7 @@ extern "C" void jdg_engine_free(jdg_engine *e) {
     drop_graphs(e);
     jdg_host_release(e);
     for (void *p : e->allocs) cudaFree(p);
+    if (e->pin_tok) cudaFreeHost(e->pin_tok);
     if (e->ev0) cudaEventDestroy(e->ev0);
     if (e->ev1) cudaEventDestroy(e->ev1);
     if (e->st) cudaStreamDestroy(e->st);
@@ -677,6 +792,24 @@ extern "C" int jdg_last_run_ms(jdg_engine *e, float *ms) {
     return JD_OK;
 }
 
+extern "C" int jdg_get_stats(jdg_engine *e, uint64_t *out3) {
+    if (!e || !out3) return JD_EINVAL;
+    cudaSetDevice(e->ctx->device);
+    unsigned long long h[3];
+    CK(cudaMemcpyAsync(h, e->stats, 3 * 8, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    for (int i = 0; i < 3; i++) out3[i] = h[i];
+    return JD_OK;
+}
+
+extern "C" int jdg_reset_stats(jdg_engine *e) {
+    if (!e) return JD_EINVAL;
+    cudaSetDevice(e->ctx->device);
+    CK(cudaMemsetAsync(e->stats, 0, 4 * 8, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    return JD_OK;
+}
+
 extern "C" int jdg_launch_count(jdg_engine *e, long long *n) {
     if (!e || !n) return JD_EINVAL;
     *n = e->launches;
@@ -746,19 +879,22 @@ extern "C" int jdg_step(jdg_engine *e, int B, const int *tok, const int *pos, ui
     cudaGraphExec_t ge;
     int rc = get_graph(e, B, &ge);
     if (rc != JD_OK) return rc;
-    CK(cudaMemcpyAsync(e->tok, tok, B * 4, cudaMemcpyHostToDevice, e->st));
-    CK(cudaMemcpyAsync(e->pos, pos, B * 4, cudaMemcpyHostToDevice, e->st));
+    memcpy(e->pin_tok, tok, B * 4);
+    memcpy(e->pin_pos, pos, B * 4);
+    CK(cudaMemcpyAsync(e->tok, e->pin_tok, B * 4, cudaMemcpyHostToDevice, e->st));
+    CK(cudaMemcpyAsync(e->pos, e->pin_pos, B * 4, cudaMemcpyHostToDevice, e->st));
     CK(cudaMemsetAsync(e->plen, 0, B * 4, e->st));
     if (rng) CK(cudaMemcpyAsync(e->rng, rng, B * 8, cudaMemcpyHostToDevice, e->st));
     CK(cudaEventRecord(e->ev0, e->st));
     CK(cudaGraphLaunch(ge, e->st));
     CK(cudaEventRecord(e->ev1, e->st));
     e->launches += e->launches_per_step[B];
-    if (next_tok) CK(cudaMemcpyAsync(next_tok, e->next_out, B * 4, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaMemcpyAsync(e->pin_next, e->next_out, B * 4, cudaMemcpyDeviceToHost, e->st));
     if (rng) CK(cudaMemcpyAsync(rng, e->rng, B * 8, cudaMemcpyDeviceToHost, e->st));
     if (logits) CK(cudaMemcpyAsync(logits, e->logits, (size_t)B * e->V * 4, cudaMemcpyDeviceToHost, e->st));
     rc = check_err(e);
     if (rc != JD_OK) return rc;
+    if (next_tok) memcpy(next_tok, e->pin_next, B * 4);
     float ms = 0.f;
     CK(cudaEventElapsedTime(&ms, e->ev0, e->ev1));
     e->last_ms = ms;

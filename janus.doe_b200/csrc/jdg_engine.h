@@ -70,6 +70,13 @@ struct jdg_engine {
     float *kc = nullptr, *vc = nullptr;
     long kv_bstride = 0;
     int *err = nullptr;
+    unsigned *tickets = nullptr;  // last-CTA counters of the batch-1 chain (1024)
+    float *amax_v = nullptr, *vpart = nullptr, *ffn_inv = nullptr;
+    unsigned long long *stats = nullptr;  // [0] experts read, [1] KV positions read, [2] steps
+    int *pin_tok = nullptr, *pin_pos = nullptr, *pin_next = nullptr;  // pinned staging for jdg_step
+    int *amax_i = nullptr;
+    int b1_ok = 0;                // shapes fit the batch-1 PDL chain
+    int force_generic = 0;        // JDG_GENERIC=1: use the generic kernels at batch 1
     int *tr_k = nullptr, *tr_sel = nullptr;
     float *tr_w = nullptr, *tr_ema = nullptr;
     // sampling

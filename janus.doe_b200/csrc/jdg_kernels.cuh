@@ -645,7 +645,7 @@ __global__ __launch_bounds__(256) void k_elect(ElectArgs a) {
 // grid 1, block 512 (warp e = expert slot).  idx[e*B + j] = b; pairrow[b*16+ki] = e*B + j.
 __global__ __launch_bounds__(512) void k_route(const int *__restrict__ kcnt, const int *__restrict__ sel, int B,
                                                int *__restrict__ cnt, int *__restrict__ idx, int *__restrict__ pairrow,
-                                               int *err) {
+                                               unsigned long long *stats) {
     const int e = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int n = 0;
     for (int b0 = 0; b0 < B; b0 += 32) {
@@ -663,8 +663,10 @@ __global__ __launch_bounds__(512) void k_route(const int *__restrict__ kcnt, con
         }
         n += __popc(m);
     }
-    if (lane == 0) cnt[e] = n;
-    (void)err;
+    if (lane == 0) {
+        cnt[e] = n;
+        if (n > 0) atomicAdd(stats, 1ull);
+    }
 }
 
 // x[b] += sum_ki w[b][ki] * y[pairrow(b,ki)] in election order (janusdoe.c:927-929)
@@ -696,6 +698,8 @@ struct PickArgs {
     int *hist, *hist_n;
     int Hmax;
     int *next_out;
+    unsigned long long *stats;
+    int count_experts;  // batch 1 without route: the election count is the expert count
 };
 __device__ __forceinline__ uint32_t f2key(float f) {
     uint32_t u = __float_as_uint(f);
@@ -873,6 +877,10 @@ __global__ __launch_bounds__(1024) void k_pick(PickArgs a) {
     }
     __syncthreads();
     if (tid == 0) {
+        if (a.stats) {
+            atomicAdd(a.stats + 1, (unsigned long long)(p + 1));
+            if (b == 0) atomicAdd(a.stats + 2, 1ull);
+        }
         int nx = s_next;
         a.tok[b] = nx;
         a.pos[b] = p + 1;

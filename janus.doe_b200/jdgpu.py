@@ -114,6 +114,8 @@ def lib():
         "jdg_get_trace": [C.c_void_p, C.c_int, C.POINTER(JdgTrace)],
         "jdg_last_run_ms": [C.c_void_p, F32P],
         "jdg_launch_count": [C.c_void_p, C.POINTER(C.c_longlong)],
+        "jdg_get_stats": [C.c_void_p, U64P],
+        "jdg_reset_stats": [C.c_void_p],
         "jdg_qmatvec": [C.c_void_p, F32P, C.c_void_p, C.c_int, F32P, C.c_int, C.c_int, C.c_int],
     }
     for name, args in sig.items():
@@ -337,6 +339,15 @@ class Engine:
         t, d = self._trace_bufs(B)
         self._ck(lib().jdg_get_trace(self.h, B, C.byref(t)))
         return d
+
+    def stats(self):
+        """(experts read, KV positions read, steps) since reset_stats()."""
+        out = np.zeros(3, np.uint64)
+        self._ck(lib().jdg_get_stats(self.h, _p(out, U64P)))
+        return int(out[0]), int(out[1]), int(out[2])
+
+    def reset_stats(self):
+        self._ck(lib().jdg_reset_stats(self.h))
 
     def launches(self):
         n = C.c_longlong(0)

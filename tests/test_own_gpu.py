@@ -13,6 +13,16 @@ from oracle.oracle import OwnModel
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(params=["chain", "generic"])
+def b1_path(request, monkeypatch):
+    """Batch 1 runs either the PDL kernel chain (default) or the generic batched kernels."""
+    if request.param == "generic":
+        monkeypatch.setenv("JDG_GENERIC", "1")
+    else:
+        monkeypatch.delenv("JDG_GENERIC", raising=False)
+    return request.param
+
+
 def _pair(jd, orc, depth, seed, masks=False, **over):
     cfg_o = orc.config(depth, **over)
     om = OwnModel(orc, cfg_o, seed, 0.02, masks)
@@ -64,7 +74,7 @@ def _oracle_greedy(om, prompt, n_gen):
     return stream
 
 
-def test_depth4_greedy_full(jd, orc, gpu_ctx):
+def test_depth4_greedy_full(jd, orc, gpu_ctx, b1_path):
     """depth-4, seed 0, 32-token prompt + 128 greedy tokens at batch 1."""
     om, pm = _pair(jd, orc, 4, 0, vocab_size=2256, seq_len=256)
     prompt, _ = orc.prompt(0 * 1000 + 0, 2256, 32)
@@ -84,7 +94,7 @@ def test_depth4_greedy_full(jd, orc, gpu_ctx):
         om.close()
 
 
-def test_depth12_masks_greedy(jd, orc, gpu_ctx):
+def test_depth12_masks_greedy(jd, orc, gpu_ctx, b1_path):
     """depth-12 variable topology (5-8 alive experts per layer), GQA 12/4, ctx 1024."""
     om, pm = _pair(jd, orc, 12, 3, True, n_kv_heads=4, vocab_size=8256, seq_len=1024)
     n_alive = [sum(om.alive(l)) for l in range(12)]
@@ -103,7 +113,7 @@ def test_depth12_masks_greedy(jd, orc, gpu_ctx):
         om.close()
 
 
-def test_long_context_attention(jd, orc, gpu_ctx):
+def test_long_context_attention(jd, orc, gpu_ctx, b1_path):
     """Attention over ~1000 positions (16 chunks of the split-K kernel) on a depth-4 model."""
     om, pm = _pair(jd, orc, 4, 7, vocab_size=2256, seq_len=1024)
     prompt, _ = orc.prompt(7 * 1000 + 1, 2256, 1000)
