@@ -210,6 +210,10 @@ int jdg_profile_step(jdg_engine *e, int B, float *ms_by_kernel, int max_kernels,
  * sequences of pos+1 per step), [2] decode steps. */
 int jdg_get_stats(jdg_engine *e, uint64_t *out3);
 int jdg_reset_stats(jdg_engine *e);
+/* Debug timeline of the batch-1 kernel chain: the first call allocates it (later steps
+ * record into it); out[slot*3+{0,1,2}] = earliest CTA entry, earliest return from the
+ * dependency wait, latest CTA exit, in ns of the GPU global timer; each call re-arms it. */
+int jdg_debug_timeline(jdg_engine *e, int n_slots, uint64_t *out);
 /* Counts of this library's kernel launches since the engine was created. */
 int jdg_launch_count(jdg_engine *e, long long *n);
 

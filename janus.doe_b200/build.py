@@ -20,7 +20,6 @@ NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompil
               "-diag-suppress", "177"]
 CU_SOURCES = ["jdg_engine.cu", "jdg_host.cu"]
 C_SOURCES = ["jd_model.c"]
-HEADERS = ["jdg_common.cuh", "jdg_kernels.cuh", "jdg_engine.h", "jdg_host_kernels.cuh"]
 
 
 def _nvcc():
@@ -54,7 +53,8 @@ def _run(cmd):
 
 def build_lib(force=False, verbose=False):
     os.makedirs(BUILD, exist_ok=True)
-    headers = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(INC, "jdgpu.h")]
+    headers = [os.path.join(CSRC, h) for h in sorted(os.listdir(CSRC)) if h.endswith((".cuh", ".h"))]
+    headers.append(os.path.join(INC, "jdgpu.h"))
     objs = []
     nvcc = _nvcc()
     for s in CU_SOURCES:

@@ -3,6 +3,7 @@
 // a CUDA graph per batch size, and the device-resident decode loop.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -335,6 +336,10 @@ int jdg_own_upload_impl(jdg_engine *e, const jd_model *m, int max_batch) {
     DALLOC(e->amax_v, ((size_t)V / 4 + 2) * 4);
     DALLOC(e->amax_i, ((size_t)V / 4 + 2) * 4);
     DALLOC(e->vpart, ((size_t)D / 4 + 2) * 17 * 4);
+    DALLOC(e->sel_gu, kMaxE * sizeof(float *));
+    DALLOC(e->ema_new, 4);
+    DALLOC(e->x2, (size_t)D * 4);
+    DALLOC(e->sel_dn, kMaxE * sizeof(float *));
     DALLOC(e->ffn_inv, 4);
     {
         const char *g = getenv("JDG_GENERIC");
@@ -344,6 +349,8 @@ int jdg_own_upload_impl(jdg_engine *e, const jd_model *m, int max_batch) {
                (e->HD == 64 || e->HD == 128) && D / 4 + 64 <= 1024 && e->max_seq <= 1024;
     DALLOC(e->hbuf, (size_t)B * kMaxE * H * 4);
     DALLOC(e->ybuf, (size_t)B * kMaxE * D * 4);
+    CK(cudaMemset(e->ybuf, 0, (size_t)B * kMaxE * D * 4));
+    CK(cudaMemset(e->hbuf, 0, (size_t)B * kMaxE * H * 4));
     DALLOC(e->logits, (size_t)B * V * 4);
     // KV cache [B][L][S][kd]
     e->kv_bstride = (long)L * e->max_seq * e->kd;
@@ -490,11 +497,11 @@ void jdg_launch_elect(jdg_engine *e, int l, int B, const float *xin, const float
 // ------------------------------------------------------------------------------------
 // Batch-1 chain (jdg_b1.cuh), every kernel launched with programmatic stream serialization.
 template <typename... KArgs, typename... Args>
-static void launch_pdl(jdg_engine *e, void (*kern)(KArgs...), dim3 grid, dim3 block, Args... args) {
+static void launch_pdl_sm(jdg_engine *e, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, Args... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = e->st;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -503,6 +510,10 @@ static void launch_pdl(jdg_engine *e, void (*kern)(KArgs...), dim3 grid, dim3 bl
     cfg.numAttrs = 1;
     cudaLaunchKernelEx(&cfg, kern, args...);
     e->launches++;
+}
+template <typename... KArgs, typename... Args>
+static void launch_pdl(jdg_engine *e, void (*kern)(KArgs...), dim3 grid, dim3 block, Args... args) {
+    launch_pdl_sm(e, kern, grid, block, 0, args...);
 }
 
 #define NV_SWITCH(n, KERN, ...)                                        \
@@ -522,6 +533,13 @@ static void launch_pdl(jdg_engine *e, void (*kern)(KArgs...), dim3 grid, dim3 bl
     default: launch_pdl(e, KERN<12>, __VA_ARGS__); break;              \
     }
 
+#define WO_SWITCH(n, HDV, ...)                                         \
+    switch (n) {                                                       \
+    case 2: launch_pdl(e, k_b1_wo<2, HDV>, __VA_ARGS__); break;        \
+    case 4: launch_pdl(e, k_b1_wo<4, HDV>, __VA_ARGS__); break;        \
+    case 6: launch_pdl(e, k_b1_wo<6, HDV>, __VA_ARGS__); break;        \
+    default: launch_pdl(e, k_b1_wo<8, HDV>, __VA_ARGS__); break;       \
+    }
 static bool b1_shape_ok(jdg_engine *e) {
     int nv = e->D / 128, nh = e->hidden / 128;
     return e->b1_ok && (nv == 2 || nv == 4 || nv == 6 || nv == 8) &&
@@ -545,8 +563,20 @@ static void enqueue_own_step_b1(jdg_engine *e) {
     a.next_out = e->next_out; a.Pmax = e->Pmax; a.Hmax = e->Hmax; a.err = e->err;
     a.greedy_pick = e->temp <= 0.f;
     a.stats = e->stats;
+    a.sel_gu = e->sel_gu;
+    a.sel_dn = e->sel_dn;
+    a.tl = e->timeline;
     const int nv = e->D / 128, nh = e->hidden / 128;
     const dim3 blk(128);
+    a.vpart = e->vpart;
+    a.nparts = (e->D + 3) / 4;
+    a.ema_new = e->ema_new;
+    a.ffn_inv = e->ffn_inv;
+    const size_t attn_sm = (size_t)2 * kB1Chunk * (e->HD + 4) * 4;
+    // FFN1 grid: enough warps to cover the hidden units of ~4 experts once
+    int n_sm = 148;
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, e->ctx->device);
+    const int ffn1_grid = 2 * n_sm;
     for (int l = 0; l < e->L; l++) {
         LayerDev &ly = e->layers[l];
         a.l = l;
@@ -556,16 +586,25 @@ static void enqueue_own_step_b1(jdg_engine *e) {
         a.kc = e->kc + (size_t)l * e->max_seq * e->kd; a.vc = e->vc + (size_t)l * e->max_seq * e->kd;
         a.tr_k = e->tr_k; a.tr_sel = e->tr_sel; a.tr_w = e->tr_w; a.tr_ema = e->tr_ema;
         a.embed = l == 0;
+        a.combine = 0;
+        a.x = e->x;
         NV_SWITCH(nv, k_b1_qkv, dim3((e->qkvd + 3) / 4), blk, a);
         dim3 ga((e->max_seq + kB1Chunk - 1) / kB1Chunk, e->KVH);
-        if (e->HD == 64) launch_pdl(e, k_b1_attn<64>, ga, blk, a);
-        else launch_pdl(e, k_b1_attn<128>, ga, blk, a);
-        NV_SWITCH(nv, k_b1_wo, dim3((e->D + 3) / 4), blk, a);
-        if (e->n_alive[l] < 2) continue;
-        NV_SWITCH(nv, k_b1_ffn1, dim3((e->hidden + 3) / 4, e->n_alive[l]), blk, a);
-        NH_SWITCH(nh, k_b1_ffn2, dim3((e->D + 3) / 4, e->n_alive[l]), blk, a);
+        if (e->HD == 64) launch_pdl_sm(e, k_b1_attn<64>, ga, blk, attn_sm, a);
+        else launch_pdl_sm(e, k_b1_attn<128>, ga, blk, attn_sm, a);
+        if (e->HD == 64) {
+            WO_SWITCH(nv, 64, dim3((e->D + 3) / 4), blk, a);
+        } else {
+            WO_SWITCH(nv, 128, dim3((e->D + 3) / 4), blk, a);
+        }
+        NV_SWITCH(nv, k_b1_ffn1, dim3(ffn1_grid), blk, a);
+        NH_SWITCH(nh, k_b1_ffn2, dim3((e->D + 3) / 4, std::max(1, e->n_alive[l])), blk, a);
     }
-    NV_SWITCH(nv, k_b1_lmhead, dim3((e->V + 7) / 8), blk, a);
+    a.l = e->L;
+    a.combine = 0;
+    a.embed = 0;
+    a.x = e->x;
+    NV_SWITCH(nv, k_b1_lmhead, dim3(2 * n_sm), blk, a);
     if (!a.greedy_pick) jdg_launch_pick(e, 1);
 }
 
@@ -659,6 +698,8 @@ static int get_graph(jdg_engine *e, int B, cudaGraphExec_t *out) {
         CK(cudaFuncSetAttribute(k_expert_down_b1, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
         CK(cudaFuncSetAttribute(k_expert_gu_b1, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
         CK(cudaFuncSetAttribute(k_elect, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        CK(cudaFuncSetAttribute(k_b1_attn<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        CK(cudaFuncSetAttribute(k_b1_attn<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
         int rc = jdg_host_set_attrs(e);
         if (rc != JD_OK) return rc;
         attr_done = true;
@@ -806,6 +847,30 @@ extern "C" int jdg_reset_stats(jdg_engine *e) {
     if (!e) return JD_EINVAL;
     cudaSetDevice(e->ctx->device);
     CK(cudaMemsetAsync(e->stats, 0, 4 * 8, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    return JD_OK;
+}
+
+// Debug: enable (n_slots > 0) or read the batch-1 kernel timeline.  out[slot*3 + {0,1,2}] =
+// earliest CTA entry, earliest return from the dependency wait, latest CTA exit (ns).
+extern "C" int jdg_debug_timeline(jdg_engine *e, int n_slots, uint64_t *out) {
+    if (!e || n_slots < 0) return JD_EINVAL;
+    cudaSetDevice(e->ctx->device);
+    if (!e->timeline) {
+        DALLOC(e->timeline, (size_t)3 * 256 * 8);
+        drop_graphs(e);
+    }
+    if (out) {
+        CK(cudaMemcpyAsync(out, e->timeline, (size_t)3 * n_slots * 8, cudaMemcpyDeviceToHost, e->st));
+        CK(cudaStreamSynchronize(e->st));
+    }
+    std::vector<unsigned long long> init(3 * 256);
+    for (int i = 0; i < 256; i++) {
+        init[3 * i] = ~0ull;
+        init[3 * i + 1] = ~0ull;
+        init[3 * i + 2] = 0;
+    }
+    CK(cudaMemcpyAsync(e->timeline, init.data(), init.size() * 8, cudaMemcpyHostToDevice, e->st));
     CK(cudaStreamSynchronize(e->st));
     return JD_OK;
 }

@@ -72,7 +72,10 @@ struct jdg_engine {
     int *err = nullptr;
     unsigned *tickets = nullptr;  // last-CTA counters of the batch-1 chain (1024)
     float *amax_v = nullptr, *vpart = nullptr, *ffn_inv = nullptr;
-    unsigned long long *stats = nullptr;  // [0] experts read, [1] KV positions read, [2] steps
+    const float **sel_gu = nullptr, **sel_dn = nullptr;
+    float *ema_new = nullptr, *x2 = nullptr;  // x2: ping-pong residual of the batch-1 chain  // elected expert weights (batch-1 chain)
+    unsigned long long *stats = nullptr;
+    unsigned long long *timeline = nullptr;  // optional per-kernel timeline (jdg_debug_timeline)  // [0] experts read, [1] KV positions read, [2] steps
     int *pin_tok = nullptr, *pin_pos = nullptr, *pin_next = nullptr;  // pinned staging for jdg_step
     int *amax_i = nullptr;
     int b1_ok = 0;                // shapes fit the batch-1 PDL chain

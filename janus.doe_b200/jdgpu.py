@@ -116,6 +116,7 @@ def lib():
         "jdg_launch_count": [C.c_void_p, C.POINTER(C.c_longlong)],
         "jdg_get_stats": [C.c_void_p, U64P],
         "jdg_reset_stats": [C.c_void_p],
+        "jdg_debug_timeline": [C.c_void_p, C.c_int, U64P],
         "jdg_qmatvec": [C.c_void_p, F32P, C.c_void_p, C.c_int, F32P, C.c_int, C.c_int, C.c_int],
     }
     for name, args in sig.items():
@@ -345,6 +346,12 @@ class Engine:
         out = np.zeros(3, np.uint64)
         self._ck(lib().jdg_get_stats(self.h, _p(out, U64P)))
         return int(out[0]), int(out[1]), int(out[2])
+
+    def timeline(self, n_slots=0):
+        """Arm (n_slots=0) or read the batch-1 kernel timeline as an [n_slots, 3] array (ns)."""
+        out = np.zeros((max(n_slots, 1), 3), np.uint64)
+        self._ck(lib().jdg_debug_timeline(self.h, n_slots, _p(out, U64P) if n_slots else None))
+        return out[:n_slots]
 
     def reset_stats(self):
         self._ck(lib().jdg_reset_stats(self.h))
