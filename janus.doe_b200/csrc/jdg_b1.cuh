@@ -299,7 +299,7 @@ __device__ __forceinline__ void b1_load_x(const B1Args &a, float *xs) {
 // QKV: qkv = Wqkv . rmsnorm(x, attn_norm); layer 0 first gathers x = tok_emb[tok], later
 // layers first add the previous layer's expert outputs.
 template <int NV>
-__global__ __launch_bounds__(128) void k_b1_qkv(B1Args a) {
+static __global__ __launch_bounds__(128) void k_b1_qkv(B1Args a) {
     TlMark tlm(a.tl, a.l * 5 + 0);
     __shared__ __align__(16) float xs[NV * 128];
     __shared__ float red[32];
@@ -363,7 +363,7 @@ __global__ __launch_bounds__(128) void k_b1_qkv(B1Args a) {
 // partials (unnormalised o, chunk max m, chunk sum l); WO merges them.
 // s = (q.k)*scale, then clamp*tanh(s/clamp) (janusdoe.c:899-910).
 template <int HD>
-__global__ __launch_bounds__(128) void k_b1_attn(B1Args a) {
+static __global__ __launch_bounds__(128) void k_b1_attn(B1Args a) {
     TlMark tlm(a.tl, a.l * 5 + 1);
     constexpr int RS = HD + 4;  // padded row stride (conflict-free float4 reads)
     constexpr int CH = kB1Chunk;
@@ -486,7 +486,7 @@ __global__ __launch_bounds__(128) void k_b1_attn(B1Args a) {
 // sums  sum x_r^2  and  sum (w_vote[e][r] * ffn_norm[r]) * x_r  (e < 16): the FFN RMSNorm
 // and the 16 votes in factored form, vote_e = inv * sum (janusdoe.c:915, 795-797).
 template <int NV, int HD>
-__global__ __launch_bounds__(128) void k_b1_wo(B1Args a) {
+static __global__ __launch_bounds__(128) void k_b1_wo(B1Args a) {
     TlMark tlm(a.tl, a.l * 5 + 2);
     constexpr int CH = kB1Chunk, MAXC = 1024 / CH;
     __shared__ __align__(16) float xs[NV * 128];
@@ -632,7 +632,7 @@ __global__ __launch_bounds__(128) void k_b1_wo(B1Args a) {
 // Warps walk the (ki, i) hidden units with a stride of all warps of the grid; rows
 // (2i, 2i+1) of the interleaved gate/up matrix.
 template <int NV>
-__global__ __launch_bounds__(128) void k_b1_ffn1(B1Args a) {
+static __global__ __launch_bounds__(128) void k_b1_ffn1(B1Args a) {
     TlMark tlm(a.tl, a.l * 5 + 3);
     __shared__ __align__(16) float xs[NV * 128];
     __shared__ const float *gu_s[kMaxE];
@@ -724,7 +724,7 @@ __global__ __launch_bounds__(128) void k_b1_ffn1(B1Args a) {
 // FFN2: y_ki[r] = Wd_e[r] . h_ki for the elected experts (janusdoe.c:926); the weighted
 // sum and residual add happen in the next kernel's prologue.  grid (D/4, kmax).
 template <int NH>
-__global__ __launch_bounds__(128) void k_b1_ffn2(B1Args a) {
+static __global__ __launch_bounds__(128) void k_b1_ffn2(B1Args a) {
     TlMark tlm(a.tl, a.l * 5 + 4);
     __shared__ __align__(16) float hs[NH * 128];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -773,7 +773,7 @@ __global__ __launch_bounds__(128) void k_b1_ffn2(B1Args a) {
 // (janusdoe.c:931-932).  Per-CTA argmax partials; with greedy_pick the last CTA takes the
 // first-index maximum (janusdoe.c:3637) or the prompt's next id and advances tok/pos/history.
 template <int NV>
-__global__ __launch_bounds__(128) void k_b1_lmhead(B1Args a) {
+static __global__ __launch_bounds__(128) void k_b1_lmhead(B1Args a) {
     TlMark tlm(a.tl, a.L * 5);
     __shared__ __align__(16) float xs[NV * 128];
     __shared__ float red[32];

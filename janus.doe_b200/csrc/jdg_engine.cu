@@ -167,7 +167,9 @@ int jdg_alloc_state(jdg_engine *e) {
     return JD_OK;
 }
 
-static int engine_new(jdg_ctx *ctx, int kind, jdg_engine **out) {
+int jdg_engine_create(jdg_ctx *ctx, int kind, jdg_engine **out);
+static int engine_new(jdg_ctx *ctx, int kind, jdg_engine **out) { return jdg_engine_create(ctx, kind, out); }
+int jdg_engine_create(jdg_ctx *ctx, int kind, jdg_engine **out) {
     jdg_engine *e = new (std::nothrow) jdg_engine();
     if (!e) return JD_ENOMEM;
     e->ctx = ctx;
@@ -225,6 +227,7 @@ int jdg_own_upload_impl(jdg_engine *e, const jd_model *m, int max_batch) {
     e->HD = c.head_dim;
     e->hidden = c.hidden_dim;
     e->V = c.vocab_size;
+    e->ldl = c.vocab_size;
     e->max_seq = c.seq_len;
     e->qd = c.n_heads * c.head_dim;
     e->kd = c.n_kv_heads * c.head_dim;
@@ -448,8 +451,8 @@ void jdg_launch_attention(jdg_engine *e, int l, int B, float scale, float bias) 
 void jdg_launch_pick(jdg_engine *e, int B) {
     PickArgs pa;
     pa.logits = e->logits;
-    pa.V = e->V;
-    pa.ldl = e->V;
+    pa.V = e->ldl;
+    pa.ldl = e->ldl;
     pa.temp = e->temp;
     pa.top_k = e->top_k;
     pa.tok = e->tok;
@@ -465,6 +468,11 @@ void jdg_launch_pick(jdg_engine *e, int B) {
     pa.stats = e->stats;
     k_pick<<<B, 1024, 0, e->st>>>(pa);
     e->launches++;
+}
+
+void jdg_launch_pick_tp(jdg_engine *e, int B, const float *v, const int *ix, int world) {
+    k_pick_tp<<<(B + 127) / 128, 128, 0, e->st>>>(v, ix, world, B, e->tok, e->pos, e->plen, e->prompt, e->Pmax, e->hist,
+                                                  e->hist_n, e->Hmax, e->next_out, e->stats);
 }
 
 void jdg_launch_elect(jdg_engine *e, int l, int B, const float *xin, const float *norm_w, const float *w_vote,
@@ -910,7 +918,7 @@ extern "C" int jdg_get_history(jdg_engine *e, int B, int n, int *tokens) {
 extern "C" int jdg_get_logits(jdg_engine *e, int B, float *logits) {
     if (!e || B < 1 || B > e->B_max || !logits) return JD_EINVAL;
     cudaSetDevice(e->ctx->device);
-    CK(cudaMemcpyAsync(logits, e->logits, (size_t)B * e->V * 4, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaMemcpyAsync(logits, e->logits, (size_t)B * e->ldl * 4, cudaMemcpyDeviceToHost, e->st));
     CK(cudaStreamSynchronize(e->st));
     return JD_OK;
 }
@@ -956,7 +964,7 @@ extern "C" int jdg_step(jdg_engine *e, int B, const int *tok, const int *pos, ui
     e->launches += e->launches_per_step[B];
     CK(cudaMemcpyAsync(e->pin_next, e->next_out, B * 4, cudaMemcpyDeviceToHost, e->st));
     if (rng) CK(cudaMemcpyAsync(rng, e->rng, B * 8, cudaMemcpyDeviceToHost, e->st));
-    if (logits) CK(cudaMemcpyAsync(logits, e->logits, (size_t)B * e->V * 4, cudaMemcpyDeviceToHost, e->st));
+    if (logits) CK(cudaMemcpyAsync(logits, e->logits, (size_t)B * e->ldl * 4, cudaMemcpyDeviceToHost, e->st));
     rc = check_err(e);
     if (rc != JD_OK) return rc;
     if (next_tok) memcpy(next_tok, e->pin_next, B * 4);

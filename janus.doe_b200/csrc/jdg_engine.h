@@ -38,6 +38,7 @@ struct jdg_engine {
     // shapes
     int B_max = 0, L = 0, D = 0, Hh = 0, KVH = 0, HD = 0, hidden = 0, V = 0, max_seq = 0;
     int qd = 0, kd = 0, qkvd = 0, nchunk = 0, kmax = 1;
+    int ldl = 0;  // logits row stride (the rank's vocab slice under tensor parallelism)
     float eps = 1e-5f, clamp = 0.f;
     int rope_norm = 0;
     int n_alive[JD_MAX_LAYERS] = {0};
@@ -99,6 +100,8 @@ int jdg_own_upload_impl(jdg_engine *e, const jd_model *m, int max_batch);
 void jdg_launch_rope(jdg_engine *e, int l, int B);
 void jdg_launch_attention(jdg_engine *e, int l, int B, float scale, float bias);
 void jdg_launch_pick(jdg_engine *e, int B);
+void jdg_launch_pick_tp(jdg_engine *e, int B, const float *v, const int *ix, int world);
+int jdg_engine_create(jdg_ctx *ctx, int kind, jdg_engine **out);
 void jdg_launch_elect(jdg_engine *e, int l, int B, const float *xin, const float *norm_w, const float *w_vote,
                       const int *alive, float temperature, int host);
 // host-model half (jdg_host.cu)

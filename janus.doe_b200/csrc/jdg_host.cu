@@ -1,18 +1,542 @@
-// jdg_host.cu — host GGUF model half of the engine (placeholder until the packed kernels land).
-#include "jdg_engine.h"
+// jdg_host.cu — host GGUF model half of the engine: upload (repacking packed Q8_0/Q4_K
+// rows losslessly, tensor-parallel sharding), the decode step (gguf_host_forward,
+// janusdoe.c:3160-3322, for a batch of independent sequences), NCCL all-reduce for the
+// tensor-parallel case, and the standalone packed GEMV entry point.
+#include <nccl.h>
 
-int jdg_enqueue_host_step(jdg_engine *e, int B) { (void)e; (void)B; return JD_EUNSUPPORTED; }
-int jdg_host_set_attrs(jdg_engine *e) { (void)e; return JD_OK; }
-void jdg_host_release(jdg_engine *e) { (void)e; }
-extern "C" int jdg_host_upload(jdg_ctx *ctx, const jd_host_model *h, int max_batch, int max_seq, jdg_engine **out) {
-    (void)ctx; (void)h; (void)max_batch; (void)max_seq; (void)out; return JD_EUNSUPPORTED;
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "jdg_engine.h"
+#include "jdg_host_kernels.cuh"
+
+using namespace jdg;
+
+#define E_CTX (e->ctx)
+#define CK(call)                                                                                                    \
+    do {                                                                                                            \
+        cudaError_t _e = (call);                                                                                    \
+        if (_e != cudaSuccess) {                                                                                    \
+            jdg_set_err(E_CTX, "%s failed: %s (%s:%d)", #call, cudaGetErrorString(_e), __FILE__, __LINE__);         \
+            return JD_ECUDA;                                                                                        \
+        }                                                                                                           \
+    } while (0)
+#define NK(call)                                                                                                    \
+    do {                                                                                                            \
+        ncclResult_t _r = (call);                                                                                   \
+        if (_r != ncclSuccess) {                                                                                    \
+            jdg_set_err(E_CTX, "%s failed: %s", #call, ncclGetErrorString(_r));                                     \
+            return JD_ECOMM;                                                                                        \
+        }                                                                                                           \
+    } while (0)
+
+namespace {
+
+struct HostPriv {
+    ncclComm_t comm = nullptr;
+    int rank = 0, world = 1;
+    int H_loc = 0, KVH_loc = 0, hidden_loc = 0, V_loc = 0, V_off = 0;
+    float *partial = nullptr;               // [B][D] partial sums to all-reduce
+    float *amx_v = nullptr;                 // [world][B]
+    int *amx_i = nullptr;
+    float *amx_v_loc = nullptr;
+    int *amx_i_loc = nullptr;
+    float *lora_A[JD_MAX_LAYERS] = {}, *lora_B[JD_MAX_LAYERS] = {};
+    QW wqkv[JD_MAX_LAYERS], wo[JD_MAX_LAYERS], gu[JD_MAX_LAYERS], dn[JD_MAX_LAYERS];
+    QW out;
+    float *ones = nullptr;                  // [D] of 1.0f for absent norms
+};
+
+HostPriv *priv(jdg_engine *e) { return (HostPriv *)e->host_priv; }
+
+int block_elems(int dt) { return dt == JD_Q8_0 ? 32 : dt == JD_Q4_K ? 256 : dt == JD_F32 ? 1 : 0; }
+size_t block_bytes(int dt) { return dt == JD_Q8_0 ? 34 : dt == JD_Q4_K ? 144 : dt == JD_F32 ? 4 : 0; }
+
+// Host-side repack of selected rows (and a block-aligned column range) of a packed tensor
+// into the device layout described in jdg_host_kernels.cuh.
+struct Packed {
+    std::vector<uint8_t> q, s;
+    int dt = 0, rows = 0, cols = 0;
+};
+bool repack(const void *src, int dt, int src_cols, const std::vector<int> &rows, int c0, int c1, Packed &out) {
+    const int be = block_elems(dt);
+    if (!be || src_cols % be || c0 % be || c1 % be || c1 <= c0) return false;
+    const size_t bb = block_bytes(dt), row_bytes = (size_t)(src_cols / be) * bb;
+    const int nb = (c1 - c0) / be, cols = c1 - c0;
+    out.dt = dt;
+    out.rows = (int)rows.size();
+    out.cols = cols;
+    const uint8_t *base = (const uint8_t *)src;
+    if (dt == JD_F32) {
+        out.q.resize((size_t)out.rows * cols * 4);
+        for (size_t r = 0; r < rows.size(); r++)
+            memcpy(&out.q[r * cols * 4], base + (size_t)rows[r] * row_bytes + (size_t)c0 * 4, (size_t)cols * 4);
+    } else if (dt == JD_Q8_0) {
+        out.q.resize((size_t)out.rows * cols);
+        out.s.resize((size_t)out.rows * nb * 2);
+        for (size_t r = 0; r < rows.size(); r++) {
+            const uint8_t *rp = base + (size_t)rows[r] * row_bytes + (size_t)(c0 / 32) * 34;
+            for (int b = 0; b < nb; b++) {
+                memcpy(&out.s[(r * nb + b) * 2], rp + (size_t)b * 34, 2);
+                memcpy(&out.q[r * cols + (size_t)b * 32], rp + (size_t)b * 34 + 2, 32);
+            }
+        }
+    } else {
+        out.q.resize((size_t)out.rows * cols / 2);
+        out.s.resize((size_t)out.rows * nb * 16);
+        for (size_t r = 0; r < rows.size(); r++) {
+            const uint8_t *rp = base + (size_t)rows[r] * row_bytes + (size_t)(c0 / 256) * 144;
+            for (int b = 0; b < nb; b++) {
+                memcpy(&out.s[(r * nb + b) * 16], rp + (size_t)b * 144, 16);
+                memcpy(&out.q[r * (cols / 2) + (size_t)b * 128], rp + (size_t)b * 144 + 16, 128);
+            }
+        }
+    }
+    return true;
 }
-extern "C" int jdg_comm_unique_id(void *id) { (void)id; return JD_EUNSUPPORTED; }
+
+std::vector<int> range(int a, int b) {
+    std::vector<int> v;
+    for (int i = a; i < b; i++) v.push_back(i);
+    return v;
+}
+
+}  // namespace
+
+static int dalloc(jdg_engine *e, void **p, size_t bytes) {
+    cudaError_t r = cudaMalloc(p, bytes ? bytes : 256);
+    if (r != cudaSuccess) {
+        jdg_set_err(e->ctx, "cudaMalloc(%zu) failed: %s", bytes, cudaGetErrorString(r));
+        return JD_ENOMEM;
+    }
+    e->allocs.push_back(*p);
+    return JD_OK;
+}
+#define DALLOC(ptr, bytes)                                       \
+    do {                                                         \
+        int _r = dalloc(e, (void **)&(ptr), (size_t)(bytes));    \
+        if (_r != JD_OK) return _r;                              \
+    } while (0)
+
+static int upload_packed(jdg_engine *e, const Packed &p, QW &w) {
+    w.dt = p.dt;
+    w.rows = p.rows;
+    w.cols = p.cols;
+    uint8_t *q = nullptr, *s = nullptr;
+    DALLOC(q, p.q.size());
+    CK(cudaMemcpy(q, p.q.data(), p.q.size(), cudaMemcpyHostToDevice));
+    if (!p.s.empty()) {
+        DALLOC(s, p.s.size());
+        CK(cudaMemcpy(s, p.s.data(), p.s.size(), cudaMemcpyHostToDevice));
+    }
+    w.q = q;
+    w.s = s;
+    return JD_OK;
+}
+
+static int upload_f32(jdg_engine *e, const float *src, size_t n, float **dst) {
+    DALLOC(*dst, n * 4);
+    CK(cudaMemcpy(*dst, src, n * 4, cudaMemcpyHostToDevice));
+    return JD_OK;
+}
+
+int jdg_alloc_state(jdg_engine *e);
+int jdg_reset(jdg_engine *e, int slot);
+
+static int host_upload_impl(jdg_engine *e, const jd_host_model *h, int max_batch, int max_seq, int rank, int world) {
+    HostPriv *hp = priv(e);
+    const int D = h->dim, Hh = h->n_heads, KVH = h->n_kv_heads, HD = h->head_dim, HH = h->hidden;
+    const int L = std::min(h->n_layers, JD_MAX_LAYERS);
+    if (Hh % world || KVH % world || HH % world) {
+        jdg_set_err(e->ctx, "heads %d/%d or hidden %d not divisible by %d ranks", Hh, KVH, HH, world);
+        return JD_EINVAL;
+    }
+    hp->rank = rank;
+    hp->world = world;
+    hp->H_loc = Hh / world;
+    hp->KVH_loc = KVH / world;
+    hp->hidden_loc = HH / world;
+    hp->V_loc = (h->vocab + world - 1) / world;
+    hp->V_off = rank * hp->V_loc;
+    if (hp->V_off + hp->V_loc > h->vocab) hp->V_loc = std::max(0, h->vocab - hp->V_off);
+    e->B_max = max_batch;
+    e->L = L;
+    e->D = D;
+    e->Hh = hp->H_loc;
+    e->KVH = hp->KVH_loc;
+    e->HD = HD;
+    e->hidden = hp->hidden_loc;
+    e->V = h->vocab;
+    e->ldl = std::max(1, hp->V_loc);
+    e->max_seq = max_seq;
+    e->qd = hp->H_loc * HD;
+    e->kd = hp->KVH_loc * HD;
+    e->qkvd = e->qd + 2 * e->kd;
+    e->eps = h->rms_eps;
+    e->clamp = 0.f;
+    e->rope_norm = h->rope_norm;
+    e->nchunk = (max_seq + kAttnChunk - 1) / kAttnChunk;
+    e->lora_rank = h->lora_rank;
+    e->lora_alpha = h->lora_alpha;
+    const int R = h->lora_rank;
+    // --- weights
+    for (int l = 0; l < L; l++) {
+        const jd_host_layer &ly = h->layers[l];
+        if (!ly.wq || !ly.wk || !ly.wv || !ly.wo || !ly.gate || !ly.up || !ly.down) {
+            jdg_set_err(e->ctx, "layer %d lacks attention or FFN weights", l);
+            return JD_EUNSUPPORTED;
+        }
+        if (ly.wq_dt != ly.wk_dt || ly.wq_dt != ly.wv_dt || ly.gate_dt != ly.up_dt) {
+            jdg_set_err(e->ctx, "layer %d mixes dtypes inside q/k/v or gate/up", l);
+            return JD_EUNSUPPORTED;
+        }
+        // q|k|v rows of this rank's heads
+        Packed pq, pk, pv, po, pg, pu, pd, pqkv, pgu;
+        const int q0 = rank * hp->H_loc * HD, q1 = q0 + hp->H_loc * HD;
+        const int k0 = rank * hp->KVH_loc * HD, k1 = k0 + hp->KVH_loc * HD;
+        if (!repack(ly.wq, ly.wq_dt, D, range(q0, q1), 0, D, pq) || !repack(ly.wk, ly.wk_dt, D, range(k0, k1), 0, D, pk) ||
+            !repack(ly.wv, ly.wv_dt, D, range(k0, k1), 0, D, pv)) {
+            jdg_set_err(e->ctx, "layer %d q/k/v: dtype %d has no kernel for dim %d", l, ly.wq_dt, D);
+            return JD_EUNSUPPORTED;
+        }
+        pqkv.dt = pq.dt;
+        pqkv.rows = pq.rows + pk.rows + pv.rows;
+        pqkv.cols = D;
+        for (const Packed *x : {&pq, &pk, &pv}) {
+            pqkv.q.insert(pqkv.q.end(), x->q.begin(), x->q.end());
+            pqkv.s.insert(pqkv.s.end(), x->s.begin(), x->s.end());
+        }
+        // Wo: all rows, the contraction columns of this rank's heads
+        if (!repack(ly.wo, ly.wo_dt, Hh * HD, range(0, D), q0, q1, po)) {
+            jdg_set_err(e->ctx, "layer %d wo: dtype %d cannot be split at %d", l, ly.wo_dt, q0);
+            return JD_EUNSUPPORTED;
+        }
+        // gate/up interleaved rows (g_i, u_i) of this rank's hidden slice
+        const int h0 = rank * hp->hidden_loc, h1 = h0 + hp->hidden_loc;
+        std::vector<int> gi = range(h0, h1);
+        if (!repack(ly.gate, ly.gate_dt, D, gi, 0, D, pg) || !repack(ly.up, ly.up_dt, D, gi, 0, D, pu)) {
+            jdg_set_err(e->ctx, "layer %d gate/up: dtype %d has no kernel", l, ly.gate_dt);
+            return JD_EUNSUPPORTED;
+        }
+        {
+            pgu.dt = pg.dt;
+            pgu.rows = 2 * pg.rows;
+            pgu.cols = D;
+            const size_t qr = pg.q.size() / pg.rows, sr = pg.rows ? pg.s.size() / pg.rows : 0;
+            pgu.q.resize(pg.q.size() * 2);
+            pgu.s.resize(pg.s.size() * 2);
+            for (int i = 0; i < pg.rows; i++) {
+                memcpy(&pgu.q[(2 * i) * qr], &pg.q[i * qr], qr);
+                memcpy(&pgu.q[(2 * i + 1) * qr], &pu.q[i * qr], qr);
+                if (sr) {
+                    memcpy(&pgu.s[(2 * i) * sr], &pg.s[i * sr], sr);
+                    memcpy(&pgu.s[(2 * i + 1) * sr], &pu.s[i * sr], sr);
+                }
+            }
+        }
+        if (!repack(ly.down, ly.down_dt, HH, range(0, D), h0, h1, pd)) {
+            jdg_set_err(e->ctx, "layer %d down: dtype %d cannot be split at %d", l, ly.down_dt, h0);
+            return JD_EUNSUPPORTED;
+        }
+        int rc;
+        if ((rc = upload_packed(e, pqkv, hp->wqkv[l])) || (rc = upload_packed(e, po, hp->wo[l])) ||
+            (rc = upload_packed(e, pgu, hp->gu[l])) || (rc = upload_packed(e, pd, hp->dn[l])))
+            return rc;
+        HostLayerDev &hl = e->hl[l];
+        if (ly.attn_norm) { if ((rc = upload_f32(e, ly.attn_norm, D, &hl.attn_norm))) return rc; }
+        if (ly.ffn_norm) { if ((rc = upload_f32(e, ly.ffn_norm, D, &hl.ffn_norm))) return rc; }
+        // LoRA parliament: vote rows, alive mask, A [16][D][R], B [16][R][D]
+        if (!h->w_vote[l]) {
+            jdg_set_err(e->ctx, "layer %d has no LoRA vote rows", l);
+            return JD_EINVAL;
+        }
+        if ((rc = upload_f32(e, h->w_vote[l], (size_t)JD_MAX_EXPERTS * D, &hl.w_vote))) return rc;
+        std::vector<float> A((size_t)JD_MAX_EXPERTS * D * R, 0.f), Bm((size_t)JD_MAX_EXPERTS * R * D, 0.f);
+        std::vector<int> alive(JD_MAX_EXPERTS, 0);
+        int na = 0;
+        for (int x = 0; x < JD_MAX_EXPERTS; x++) {
+            // an elected expert without factors is skipped by the reference (janusdoe.c:3289);
+            // its slot is kept alive for the election with zero factors
+            alive[x] = h->alive[l][x] ? 1 : 0;
+            na += alive[x];
+            if (alive[x] && h->A[l][x] && h->B[l][x]) {
+                memcpy(&A[(size_t)x * D * R], h->A[l][x], (size_t)D * R * 4);
+                memcpy(&Bm[(size_t)x * R * D], h->B[l][x], (size_t)R * D * 4);
+            }
+        }
+        e->n_alive[l] = na;
+        if ((rc = upload_f32(e, A.data(), A.size(), &hp->lora_A[l]))) return rc;
+        if ((rc = upload_f32(e, Bm.data(), Bm.size(), &hp->lora_B[l]))) return rc;
+        DALLOC(hl.alive, JD_MAX_EXPERTS * 4);
+        CK(cudaMemcpy(hl.alive, alive.data(), JD_MAX_EXPERTS * 4, cudaMemcpyHostToDevice));
+        hl.focus = h->layer_focus[l];
+        hl.attn_bias = h->attention_bias[l];
+        e->layer_consensus[l] = h->consensus0[l];
+    }
+    {
+        int rc;
+        std::vector<float> ones(D, 1.0f);
+        if ((rc = upload_f32(e, ones.data(), D, &hp->ones))) return rc;
+        if ((rc = upload_f32(e, h->tok_emb, (size_t)h->vocab * D, &e->tok_emb))) return rc;
+        if (h->output_norm) { if ((rc = upload_f32(e, h->output_norm, D, &e->output_norm))) return rc; }
+        else e->output_norm = hp->ones;
+        Packed po;
+        const void *outw = h->output;
+        int odt = h->output_dt;
+        if (!repack(outw, odt, D, range(hp->V_off, hp->V_off + hp->V_loc), 0, D, po)) {
+            jdg_set_err(e->ctx, "output: dtype %d has no kernel", odt);
+            return JD_EUNSUPPORTED;
+        }
+        if ((rc = upload_packed(e, po, hp->out))) return rc;
+    }
+    // RoPE table: ang = pos / powf(theta, 2i/HD) (janusdoe.c:3203)
+    {
+        const int half = HD / 2;
+        std::vector<float> cs((size_t)max_seq * half), sn((size_t)max_seq * half);
+        for (int p = 0; p < max_seq; p++)
+            for (int i = 0; i < half; i++) {
+                float ang = (float)p / powf(h->rope_theta, 2.0f * i / (float)HD);
+                cs[(size_t)p * half + i] = cosf(ang);
+                sn[(size_t)p * half + i] = sinf(ang);
+            }
+        int rc;
+        if ((rc = upload_f32(e, cs.data(), cs.size(), &e->rope_cos))) return rc;
+        if ((rc = upload_f32(e, sn.data(), sn.size(), &e->rope_sin))) return rc;
+    }
+    // activations and state
+    const int B = max_batch;
+    DALLOC(e->x, (size_t)B * D * 4);
+    DALLOC(e->xn, (size_t)B * D * 4);
+    DALLOC(e->xb, (size_t)B * D * 4);
+    DALLOC(e->qkv, (size_t)B * e->qkvd * 4);
+    DALLOC(e->att, (size_t)B * e->qd * 4);
+    DALLOC(e->part, (size_t)B * e->Hh * e->nchunk * (HD + 2) * 4);
+    DALLOC(e->hbuf, (size_t)B * e->hidden * 4);
+    DALLOC(e->logits, (size_t)B * std::max(1, hp->V_loc) * 4);
+    DALLOC(e->lora_t, (size_t)B * kMaxE * R * 4);
+    DALLOC(hp->partial, (size_t)B * D * 4);
+    DALLOC(hp->amx_v, (size_t)world * B * 4);
+    DALLOC(hp->amx_i, (size_t)world * B * 4);
+    DALLOC(hp->amx_v_loc, (size_t)B * 4);
+    DALLOC(hp->amx_i_loc, (size_t)B * 4);
+    e->kv_bstride = (long)L * max_seq * e->kd;
+    DALLOC(e->kc, (size_t)B * e->kv_bstride * 4);
+    DALLOC(e->vc, (size_t)B * e->kv_bstride * 4);
+    int rc = jdg_alloc_state(e);
+    if (rc != JD_OK) return rc;
+    rc = jdg_reset(e, -1);
+    if (rc != JD_OK) return rc;
+    CK(cudaStreamSynchronize(e->st));
+    return JD_OK;
+}
+
+// ------------------------------------------------------------------------------------
+template <int EPI>
+static void launch_q(jdg_engine *e, const QW &w, const float *X, int ldx, int M, float *C, int ldc, float alpha) {
+    if (M == 1) {
+        QGemvArgs a{w, X, C, alpha};
+        const int units = EPI == EPI_SWIGLU ? w.rows / 2 : w.rows;  // one unit per warp, 8 warps
+        const int grid = (units + 7) / 8;
+        const size_t sm = ((size_t)w.cols + w.cols / 16) * 4;
+        switch (w.dt) {
+        case JD_Q8_0: k_qgemv<8, EPI><<<grid, 256, sm, e->st>>>(a); break;
+        case JD_Q4_K: k_qgemv<12, EPI><<<grid, 256, sm, e->st>>>(a); break;
+        default: k_qgemv<0, EPI><<<grid, 256, sm, e->st>>>(a); break;
+        }
+    } else {
+        QGemmArgs a{w, X, ldx, M, C, ldc, alpha};
+        dim3 grid((w.rows + 63) / 64, (M + 31) / 32);
+        const size_t sm = (size_t)(64 + 32) * 257 * 4;
+        switch (w.dt) {
+        case JD_Q8_0: k_qgemm<8, EPI><<<grid, 256, sm, e->st>>>(a); break;
+        case JD_Q4_K: k_qgemm<12, EPI><<<grid, 256, sm, e->st>>>(a); break;
+        default: k_qgemm<0, EPI><<<grid, 256, sm, e->st>>>(a); break;
+        }
+    }
+    e->launches++;
+}
+
+int jdg_host_set_attrs(jdg_engine *e) {
+    (void)e;
+    const int big = 200 * 1024;
+#define SETA(K) cudaFuncSetAttribute(K, cudaFuncAttributeMaxDynamicSharedMemorySize, big)
+    SETA((k_qgemv<8, EPI_STORE>)); SETA((k_qgemv<8, EPI_ADD>)); SETA((k_qgemv<8, EPI_SWIGLU>));
+    SETA((k_qgemv<12, EPI_STORE>)); SETA((k_qgemv<12, EPI_ADD>)); SETA((k_qgemv<12, EPI_SWIGLU>));
+    SETA((k_qgemv<0, EPI_STORE>)); SETA((k_qgemv<0, EPI_ADD>)); SETA((k_qgemv<0, EPI_SWIGLU>));
+    SETA((k_qgemm<8, EPI_STORE>)); SETA((k_qgemm<8, EPI_ADD>)); SETA((k_qgemm<8, EPI_SWIGLU>));
+    SETA((k_qgemm<12, EPI_STORE>)); SETA((k_qgemm<12, EPI_ADD>)); SETA((k_qgemm<12, EPI_SWIGLU>));
+    SETA((k_qgemm<0, EPI_STORE>)); SETA((k_qgemm<0, EPI_ADD>)); SETA((k_qgemm<0, EPI_SWIGLU>));
+#undef SETA
+    return JD_OK;
+}
+
+// One decode step of gguf_host_forward (janusdoe.c:3160-3322) for slots 0..B-1.
+int jdg_enqueue_host_step(jdg_engine *e, int B) {
+    HostPriv *hp = priv(e);
+    const int D = e->D, L = e->L;
+    const bool tp = hp->world > 1;
+    const float scale = 1.0f / sqrtf((float)e->HD);
+    k_embed<<<B, 256, 0, e->st>>>(e->tok_emb, e->V, D, e->tok, e->x, e->err);
+    e->launches++;
+    for (int l = 0; l < L; l++) {
+        HostLayerDev &hl = e->hl[l];
+        k_rmsnorm<<<B, 256, 0, e->st>>>(e->x, hl.attn_norm, e->xn, D, e->eps);
+        e->launches++;
+        launch_q<EPI_STORE>(e, hp->wqkv[l], e->xn, D, B, e->qkv, e->qkvd, 1.f);
+        jdg_launch_rope(e, l, B);
+        jdg_launch_attention(e, l, B, scale, 1.0f + hl.attn_bias);
+        if (!tp) {
+            launch_q<EPI_ADD>(e, hp->wo[l], e->att, e->qd, B, e->x, D, 1.f);
+        } else {
+            launch_q<EPI_STORE>(e, hp->wo[l], e->att, e->qd, B, hp->partial, D, 1.f);
+            ncclAllReduce(hp->partial, hp->partial, (size_t)B * D, ncclFloat, ncclSum, hp->comm, e->st);
+            k_add<<<(unsigned)(((size_t)B * D + 255) / 256), 256, 0, e->st>>>(e->x, hp->partial, (size_t)B * D);
+            e->launches++;
+        }
+        k_rmsnorm<<<B, 256, 0, e->st>>>(e->x, hl.ffn_norm, e->xb, D, e->eps);
+        e->launches++;
+        launch_q<EPI_SWIGLU>(e, hp->gu[l], e->xb, D, B, e->hbuf, e->hidden, 1.f);
+        if (!tp) {
+            launch_q<EPI_ADD>(e, hp->dn[l], e->hbuf, e->hidden, B, e->x, D, hl.focus);
+        } else {
+            launch_q<EPI_STORE>(e, hp->dn[l], e->hbuf, e->hidden, B, hp->partial, D, 1.f);
+            ncclAllReduce(hp->partial, hp->partial, (size_t)B * D, ncclFloat, ncclSum, hp->comm, e->st);
+            k_add<<<(unsigned)(((size_t)B * D + 255) / 256), 256, 0, e->st>>>(e->x, hp->partial, (size_t)B * D);
+            e->launches++;
+        }
+        // LoRA parliament on xn (janusdoe.c:3281-3303)
+        jdg_launch_elect(e, l, B, e->xn, nullptr, hl.w_vote, hl.alive, 0.f, 1);
+        if (e->n_alive[l] > 0) {
+            k_lora_t<<<dim3(e->lora_rank, e->n_alive[l], B), 256, 0, e->st>>>(hp->lora_B[l], e->lora_rank, D, e->kcnt,
+                                                                              e->sel, e->xn, e->lora_t);
+            k_lora_apply<<<dim3((D + 255) / 256, B), 256, 0, e->st>>>(hp->lora_A[l], e->lora_rank, D, e->lora_alpha,
+                                                                      e->kcnt, e->sel, e->selw, e->lora_t, e->x);
+            e->launches += 2;
+        }
+    }
+    k_rmsnorm<<<B, 256, 0, e->st>>>(e->x, e->output_norm, e->xb, D, e->eps);
+    e->launches++;
+    if (!tp) {
+        launch_q<EPI_STORE>(e, hp->out, e->xb, D, B, e->logits, hp->V_loc, 1.f);
+        jdg_launch_pick(e, B);
+    } else {
+        launch_q<EPI_STORE>(e, hp->out, e->xb, D, B, e->logits, hp->V_loc, 1.f);
+        k_argmax_part<<<B, 1024, 0, e->st>>>(e->logits, hp->V_loc, hp->V_loc, hp->V_off, hp->amx_v_loc, hp->amx_i_loc);
+        ncclAllGather(hp->amx_v_loc, hp->amx_v, B, ncclFloat, hp->comm, e->st);
+        ncclAllGather(hp->amx_i_loc, hp->amx_i, B, ncclInt32, hp->comm, e->st);
+        jdg_launch_pick_tp(e, B, hp->amx_v, hp->amx_i, hp->world);
+        e->launches++;
+    }
+    return JD_OK;
+}
+
+void jdg_host_release(jdg_engine *e) {
+    HostPriv *hp = priv(e);
+    if (!hp) return;
+    if (hp->comm) ncclCommDestroy(hp->comm);
+    delete hp;
+    e->host_priv = nullptr;
+}
+
+int jdg_engine_create(jdg_ctx *ctx, int kind, jdg_engine **out);
+
+extern "C" int jdg_host_upload(jdg_ctx *ctx, const jd_host_model *h, int max_batch, int max_seq, jdg_engine **out) {
+    return jdg_host_upload_tp(ctx, h, max_batch, max_seq, 0, 1, nullptr, out);
+}
+
+extern "C" int jdg_comm_unique_id(void *id) {
+    if (!id) return JD_EINVAL;
+    ncclUniqueId u;
+    if (ncclGetUniqueId(&u) != ncclSuccess) return JD_ECOMM;
+    static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId size");
+    memcpy(id, &u, 128);
+    return JD_OK;
+}
+
 extern "C" int jdg_host_upload_tp(jdg_ctx *ctx, const jd_host_model *h, int max_batch, int max_seq, int rank, int world,
                                   const void *id, jdg_engine **out) {
-    (void)ctx; (void)h; (void)max_batch; (void)max_seq; (void)rank; (void)world; (void)id; (void)out;
-    return JD_EUNSUPPORTED;
+    if (!ctx || !h || !out || max_batch < 1 || max_batch > 4096 || max_seq < 1 || world < 1 || rank < 0 ||
+        rank >= world || (world > 1 && !id) || !h->tok_emb || h->n_layers < 1) {
+        if (ctx) jdg_set_err(ctx, "jdg_host_upload: bad arguments");
+        return JD_EINVAL;
+    }
+    if ((h->head_dim != 64 && h->head_dim != 128) || h->n_kv_heads < 1 || h->n_heads % h->n_kv_heads ||
+        h->n_heads / h->n_kv_heads > kMaxHG || h->dim % 32 || h->lora_rank < 1 || h->lora_rank > 64) {
+        jdg_set_err(ctx, "jdg_host_upload: unsupported shape (dim %d heads %d/%d hd %d rank %d)", h->dim, h->n_heads,
+                    h->n_kv_heads, h->head_dim, h->lora_rank);
+        return JD_EUNSUPPORTED;
+    }
+    jdg_engine *e = nullptr;
+    int rc = jdg_engine_create(ctx, 1, &e);
+    if (rc != JD_OK) return rc;
+    e->host_priv = new (std::nothrow) HostPriv();
+    if (!e->host_priv) {
+        jdg_engine_free(e);
+        return JD_ENOMEM;
+    }
+    if (world > 1) {
+        ncclUniqueId u;
+        memcpy(&u, id, 128);
+        ncclResult_t r = ncclCommInitRank(&priv(e)->comm, world, u, rank);
+        if (r != ncclSuccess) {
+            jdg_set_err(ctx, "ncclCommInitRank(%d of %d): %s", rank, world, ncclGetErrorString(r));
+            jdg_engine_free(e);
+            return JD_ECOMM;
+        }
+    }
+    rc = host_upload_impl(e, h, max_batch, max_seq, rank, world);
+    if (rc != JD_OK) {
+        jdg_engine_free(e);
+        return rc;
+    }
+    *out = e;
+    return JD_OK;
 }
+
+// ------------------------------------------------------------------------------------
+// Standalone packed GEMV/GEMM through host buffers (jd_qmatvec, janusdoe.c:2685).
 extern "C" int jdg_qmatvec(jdg_ctx *ctx, float *out, const void *W, int dt, const float *x, int r, int c, int B) {
-    (void)ctx; (void)out; (void)W; (void)dt; (void)x; (void)r; (void)c; (void)B; return JD_EUNSUPPORTED;
+    if (!ctx || !out || !W || !x || r < 1 || c < 1 || B < 1) return JD_EINVAL;
+    const int be = block_elems(dt);
+    if (!be || c % be) {
+        jdg_set_err(ctx, "jdg_qmatvec: dtype %d with %d columns has no kernel", dt, c);
+        return JD_EUNSUPPORTED;
+    }
+    if (dt == JD_Q4_K && c % 256) return JD_EUNSUPPORTED;
+    if (dt == JD_F32 && c % 4) return JD_EUNSUPPORTED;
+    if (B > 1 && c % 256) {
+        jdg_set_err(ctx, "jdg_qmatvec: batched product needs columns in multiples of 256");
+        return JD_EUNSUPPORTED;
+    }
+    jdg_engine *e = nullptr;
+    int rc = jdg_engine_create(ctx, 1, &e);
+    if (rc != JD_OK) return rc;
+    Packed p;
+    if (!repack(W, dt, c, range(0, r), 0, c, p)) {
+        jdg_engine_free(e);
+        return JD_EUNSUPPORTED;
+    }
+    QW w;
+    float *dx = nullptr, *dy = nullptr;
+    rc = upload_packed(e, p, w);
+    if (rc == JD_OK) rc = dalloc(e, (void **)&dx, (size_t)B * c * 4);
+    if (rc == JD_OK) rc = dalloc(e, (void **)&dy, (size_t)B * r * 4);
+    if (rc == JD_OK) rc = jdg_host_set_attrs(e);
+    if (rc == JD_OK) {
+        cudaError_t ce = cudaMemcpy(dx, x, (size_t)B * c * 4, cudaMemcpyHostToDevice);
+        if (ce == cudaSuccess) {
+            launch_q<EPI_STORE>(e, w, dx, c, B, dy, r, 1.f);
+            ce = cudaStreamSynchronize(e->st);
+        }
+        if (ce == cudaSuccess) ce = cudaMemcpy(out, dy, (size_t)B * r * 4, cudaMemcpyDeviceToHost);
+        if (ce != cudaSuccess) {
+            jdg_set_err(ctx, "jdg_qmatvec: %s", cudaGetErrorString(ce));
+            rc = JD_ECUDA;
+        }
+    }
+    jdg_engine_free(e);
+    return rc;
 }

@@ -13,7 +13,7 @@ constexpr int kMaxHG = 8;       // query heads per KV head supported by the atte
 
 // ------------------------------------------------------------------------------------
 // x[b] = tok_emb[tok[b]] (janusdoe.c:882; host janusdoe.c:3177 zero row for token >= V)
-__global__ void k_embed(const float *__restrict__ emb, int V, int D, const int *__restrict__ tok, float *__restrict__ x,
+static __global__ void k_embed(const float *__restrict__ emb, int V, int D, const int *__restrict__ tok, float *__restrict__ x,
                         int *err) {
     int b = blockIdx.x, t = tok[b];
     float *xr = x + (size_t)b * D;
@@ -27,7 +27,7 @@ __global__ void k_embed(const float *__restrict__ emb, int V, int D, const int *
 }
 
 // out[b] = x[b] * (1/sqrtf(sum(x^2)/D + eps)) * w   (janusdoe.c:504, 3181-3186); w may be null
-__global__ void k_rmsnorm(const float *__restrict__ x, const float *__restrict__ w, float *__restrict__ out, int D,
+static __global__ void k_rmsnorm(const float *__restrict__ x, const float *__restrict__ w, float *__restrict__ out, int D,
                           float eps) {
     __shared__ float red[32];
     int b = blockIdx.x;
@@ -61,7 +61,7 @@ struct GemvArgs {
 };
 
 template <int NB, int RPW, int EPI>
-__global__ __launch_bounds__(128) void k_gemv_f32(GemvArgs a) {
+static __global__ __launch_bounds__(128) void k_gemv_f32(GemvArgs a) {
     extern __shared__ float xs[];  // [NB][K]
     __shared__ float red[32];
     const int K = a.K, K4 = K >> 2;
@@ -135,7 +135,7 @@ __global__ __launch_bounds__(128) void k_gemv_f32(GemvArgs a) {
 // ------------------------------------------------------------------------------------
 // Expert FFN for one token (janusdoe.c:921-929): gate/up of each elected expert.
 // grid (ceil(2H / (4 warps * 2 rows)), 16): y = election slot ki; rows 2i/2i+1 = gate_i/up_i.
-__global__ __launch_bounds__(128) void k_expert_gu_b1(const float *const *__restrict__ gu_tab, const int *__restrict__ kcnt,
+static __global__ __launch_bounds__(128) void k_expert_gu_b1(const float *const *__restrict__ gu_tab, const int *__restrict__ kcnt,
                                                       const int *__restrict__ sel, int H, int D,
                                                       const float *__restrict__ xb, float *__restrict__ hbuf, int *err) {
     extern __shared__ float xs[];
@@ -170,7 +170,7 @@ __global__ __launch_bounds__(128) void k_expert_gu_b1(const float *const *__rest
 // Down projection of every elected expert for one token, then the weighted sum in election
 // order and the residual add: expert_out += w_ki * (Wd_e . h_ki); x += expert_out
 // (janusdoe.c:926-929).  grid ceil(D / 4 warps).
-__global__ __launch_bounds__(128) void k_expert_down_b1(const float *const *__restrict__ dn_tab, const int *__restrict__ kcnt,
+static __global__ __launch_bounds__(128) void k_expert_down_b1(const float *const *__restrict__ dn_tab, const int *__restrict__ kcnt,
                                                         const int *__restrict__ sel, const float *__restrict__ selw, int D, int H,
                                                         const float *__restrict__ hbuf, float *__restrict__ x) {
     extern __shared__ float hs[];  // [k][H]
@@ -216,7 +216,7 @@ struct SgemmArgs {
 };
 
 template <int BM, int EPI>
-__global__ __launch_bounds__(256) void k_sgemm(SgemmArgs a) {
+static __global__ __launch_bounds__(256) void k_sgemm(SgemmArgs a) {
     constexpr int BN = 128, BK = 16, TM = BM / 16;
     const int seg = blockIdx.z;
     const int M = a.cnt ? a.cnt[seg] : a.M;
@@ -342,7 +342,7 @@ struct RopeArgs {
     long bstride;
     int *err;
 };
-__global__ void k_rope_kv(RopeArgs a) {
+static __global__ void k_rope_kv(RopeArgs a) {
     const int b = blockIdx.x, p = a.pos[b];
     if (p < 0 || p >= a.max_seq) {
         if (threadIdx.x == 0) atomicOr(a.err, JDG_ERR_POS);
@@ -390,7 +390,7 @@ struct AttnArgs {
     float *part;  // [B][H][nchunk][HD+2]
 };
 template <int HD>
-__global__ __launch_bounds__(128) void k_attn_partial(AttnArgs a) {
+static __global__ __launch_bounds__(128) void k_attn_partial(AttnArgs a) {
     constexpr int E = HD / 32;  // dims per lane
     const int c = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int p = a.pos[b], t0 = c * kAttnChunk;
@@ -482,7 +482,7 @@ __global__ __launch_bounds__(128) void k_attn_partial(AttnArgs a) {
 }
 
 // merge chunk partials: o = sum_c o_c e^{m_c-M} / sum_c l_c e^{m_c-M}; grid (H, B), block HD
-__global__ void k_attn_combine(const float *__restrict__ part, const int *__restrict__ pos, int H, int HD, int nchunk,
+static __global__ void k_attn_combine(const float *__restrict__ part, const int *__restrict__ pos, int H, int HD, int nchunk,
                                float *__restrict__ out, int ldo) {
     const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
     const int nc = pos[b] / kAttnChunk + 1;
@@ -522,7 +522,7 @@ struct ElectArgs {
     int *tr_k, *tr_sel;
     float *tr_w, *tr_ema;  // [B][L](*16)
 };
-__global__ __launch_bounds__(256) void k_elect(ElectArgs a) {
+static __global__ __launch_bounds__(256) void k_elect(ElectArgs a) {
     extern __shared__ float xs[];
     __shared__ float red[32];
     __shared__ float votes[kMaxE];
@@ -643,7 +643,7 @@ __global__ __launch_bounds__(256) void k_elect(ElectArgs a) {
 // ------------------------------------------------------------------------------------
 // Bucket (sequence, election slot) pairs by expert, in ascending sequence order.
 // grid 1, block 512 (warp e = expert slot).  idx[e*B + j] = b; pairrow[b*16+ki] = e*B + j.
-__global__ __launch_bounds__(512) void k_route(const int *__restrict__ kcnt, const int *__restrict__ sel, int B,
+static __global__ __launch_bounds__(512) void k_route(const int *__restrict__ kcnt, const int *__restrict__ sel, int B,
                                                int *__restrict__ cnt, int *__restrict__ idx, int *__restrict__ pairrow,
                                                unsigned long long *stats) {
     const int e = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -670,7 +670,7 @@ __global__ __launch_bounds__(512) void k_route(const int *__restrict__ kcnt, con
 }
 
 // x[b] += sum_ki w[b][ki] * y[pairrow(b,ki)] in election order (janusdoe.c:927-929)
-__global__ void k_combine(const int *__restrict__ kcnt, const float *__restrict__ selw, const int *__restrict__ pairrow,
+static __global__ void k_combine(const int *__restrict__ kcnt, const float *__restrict__ selw, const int *__restrict__ pairrow,
                           const float *__restrict__ y, int D, float *__restrict__ x) {
     const int b = blockIdx.x, k = kcnt[b];
     for (int r = threadIdx.x; r < D; r += blockDim.x) {
@@ -711,7 +711,7 @@ __device__ __forceinline__ float key2f(uint32_t k) {
     return __uint_as_float(u);
 }
 constexpr int kCandCap = 2048;
-__global__ __launch_bounds__(1024) void k_pick(PickArgs a) {
+static __global__ __launch_bounds__(1024) void k_pick(PickArgs a) {
     const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float *lg = a.logits + (size_t)b * a.ldl;
     const int V = a.V;
@@ -890,6 +890,41 @@ __global__ __launch_bounds__(1024) void k_pick(PickArgs a) {
             if (hn < a.Hmax) a.hist[(size_t)b * a.Hmax + hn] = nx;
             a.hist_n[b] = hn + 1;
         }
+    }
+}
+
+// Tensor-parallel greedy pick: each rank contributed (max, first global index) of its vocab
+// slice; the first-index maximum over ranks is the global first-index maximum
+// (janusdoe.c:3374-3375).  Prompt and history handling as in k_pick.  One thread per sequence.
+static __global__ void k_pick_tp(const float *__restrict__ v, const int *__restrict__ ix, int world, int B, int *tok, int *pos,
+                          const int *plen, const int *prompt, int Pmax, int *hist, int *hist_n, int Hmax, int *next_out,
+                          unsigned long long *stats) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int r = 0; r < world; r++) {
+        float vv = v[r * B + b];
+        int ii = ix[r * B + b];
+        if (vv > bv || (vv == bv && ii < bi)) {
+            bv = vv;
+            bi = ii;
+        }
+    }
+    const int p = pos[b];
+    if (stats) {
+        atomicAdd(stats + 1, (unsigned long long)(p + 1));
+        if (b == 0) atomicAdd(stats + 2, 1ull);
+    }
+    const bool from_prompt = plen && p + 1 < plen[b];
+    const int nx = from_prompt ? prompt[(size_t)b * Pmax + p + 1] : (bi == 0x7fffffff ? 0 : bi);
+    tok[b] = nx;
+    pos[b] = p + 1;
+    if (next_out) next_out[b] = nx;
+    if (!from_prompt && hist) {
+        int hn = hist_n[b];
+        if (hn < Hmax) hist[(size_t)b * Hmax + hn] = nx;
+        hist_n[b] = hn + 1;
     }
 }
 
