@@ -29,7 +29,24 @@ def _nvcc():
     raise RuntimeError("nvcc not found")
 
 
+def _nccl_root():
+    """The NCCL that ships with the Python environment (the one PyTorch loads), so that the
+    engine and torch.distributed share one libnccl in a process."""
+    try:
+        import nvidia.nccl
+        root = list(nvidia.nccl.__path__)[0]
+        if os.path.exists(os.path.join(root, "lib", "libnccl.so.2")):
+            return root
+    except ImportError:
+        pass
+    return None
+
+
 def _nccl_flags():
+    root = _nccl_root()
+    if root:
+        d = os.path.join(root, "lib")
+        return ["-L" + d, "-l:libnccl.so.2", "-Xlinker", "-rpath=" + d]
     for d in ("/usr/lib/x86_64-linux-gnu", "/usr/local/lib", "/usr/lib64"):
         if os.path.exists(os.path.join(d, "libnccl.so")) or os.path.exists(os.path.join(d, "libnccl.so.2")):
             name = "nccl" if os.path.exists(os.path.join(d, "libnccl.so")) else ":libnccl.so.2"
@@ -61,7 +78,9 @@ def build_lib(force=False, verbose=False):
         src = os.path.join(CSRC, s)
         obj = os.path.join(BUILD, s + ".o")
         if force or _newer(obj, [src] + headers):
-            _run([nvcc] + ARCH + NVCC_FLAGS + ["-I" + INC, "-c", src, "-o", obj])
+            root = _nccl_root()
+            inc = ["-I" + os.path.join(root, "include")] if root else []
+            _run([nvcc] + ARCH + NVCC_FLAGS + inc + ["-I" + INC, "-c", src, "-o", obj])
             if verbose:
                 print("compiled", s)
         objs.append(obj)
