@@ -222,6 +222,19 @@ int jdg_launch_count(jdg_engine *e, long long *n);
  * (janusdoe.c:2685): JD_EUNSUPPORTED where the reference returns -1. */
 int jdg_qmatvec(jdg_ctx *ctx, float *out, const void *W, int dt, const float *x, int r, int c, int B);
 
+/* No counterpart in the reference.  Greedy vocabulary pick for callers that cannot allocate
+ * device memory (all their buffers come from another allocator or a preallocated pool):
+ * logits_dev[r] = W_dev[r][:] . x_dev (W f32 row-major [rows][cols], cols a multiple of 4)
+ * and *argmax_dev = the first index of the maximum, enqueued on `stream` (a cudaStream_t,
+ * NULL for the default stream); returns once enqueued.  It calls no allocator: its scratch
+ * (per-CTA partial maxima and a completion ticket) is a fixed device array of about 64 KB
+ * per GPU, held until the process exits, which limits a call to 131072 rows and 16384
+ * columns (larger sizes return JD_EINVAL, message in jdg_last_error(NULL)).  The first call
+ * on a device looks up that array's address, so make the first call before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU (other streams, other
+ * host threads) race and must be serialised by the caller. */
+int jdg_logits_argmax_noalloc(const float *W_dev, const float *x_dev, int rows, int cols, float *logits_dev,
+                              int *argmax_dev, void *stream);
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

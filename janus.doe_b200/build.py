@@ -18,7 +18,7 @@ BUILD = os.path.join(HERE, "_build")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
               "-diag-suppress", "177"]
-CU_SOURCES = ["jdg_engine.cu", "jdg_host.cu"]
+CU_SOURCES = ["jdg_engine.cu", "jdg_host.cu", "jdg_noalloc.cu"]
 C_SOURCES = ["jd_model.c"]
 
 
