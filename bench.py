@@ -137,10 +137,12 @@ def barrier(dist):
 
 
 def allmax(dist, v):
+    """Max of a host float over ranks (device tensor under NCCL, host tensor under gloo)."""
     if dist is None:
         return v
     import torch
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
