@@ -40,6 +40,13 @@ WORKLOADS = {
                        B=1, prompt=32, temp=0.0, top_k=0, steps=128, warmup=8, ref_decode=128),
     "depth8_bs64": dict(depth=8, over=dict(n_kv_heads=4, vocab_size=4256, seq_len=512), masks=False, seed=1,
                         B=64, prompt=64, temp=0.8, top_k=40, steps=128, warmup=8, ref_decode=32),
+    # host GGUF mode: synthetic llama-family models, weights N(0, 0.02) quantised per block
+    "host_q8_bs1": dict(host=True, arch="qwen2", L=22, D=2048, H=32, KV=4, FF=5632, V=32000, dtype=8, theta=1e4,
+                        rank=8, adapters=4, seed=3, B=1, prompt=64, max_seq=320, steps=128, warmup=8,
+                        ref_prompt=8, ref_decode=8, temp=0.0, top_k=0),
+    "host_q4k_bs32": dict(host=True, arch="llama", L=32, D=4096, H=32, KV=8, FF=14336, V=128256, dtype=12,
+                          theta=5e5, rank=16, adapters=8, seed=4, B=32, prompt=128, max_seq=384, steps=32, warmup=4,
+                          ref_prompt=4, ref_decode=4, temp=0.0, top_k=0),
 }
 
 
@@ -230,11 +237,69 @@ def cpu_reference(w, n_decode, threads):
         w["prompt"], n_decode, w["prompt"], w["prompt"] + n_decode - 1)
 
 
+def host_gguf_path(w):
+    """Synthetic GGUF of a host workload, generated once per machine (all cores)."""
+    d = os.environ.get("JD_BENCH_DIR", "/tmp")
+    return os.path.join(d, "jd_%s_L%d_D%d_V%d_s%d.gguf" % (w["arch"], w["L"], w["D"], w["V"], w["seed"]))
+
+
+def ensure_host_gguf(jd, w):
+    path = host_gguf_path(w)
+    if not os.path.exists(path):
+        tmp = path + ".part%d" % os.getpid()
+        jd.write_synthetic_gguf(tmp, w["arch"], w["L"], w["D"], w["FF"], w["H"], w["KV"], w["V"], w["theta"], 1e-5,
+                                w["dtype"], w["seed"], 0.02, 0)
+        os.replace(tmp, path)
+    return path
+
+
+def lora_args(w):
+    # A, B ~ N(0, 0.01); vote rows uniform in [-1/sqrt(D), 1/sqrt(D))
+    return w["seed"] * 7 + 1, w["adapters"], 0.01, 1.0 / w["D"] ** 0.5
+
+
+def cpu_reference_host(w, n_prompt, n_decode):
+    """The reference's gguf_host_forward (its own pthread row kernels, janusdoe.c:2685) on the
+    host cores: one sequence, n_prompt prompt tokens untimed, n_decode greedy tokens timed."""
+    sys.path.insert(0, ROOT)
+    from oracle.oracle import Reference
+    jd = load_pkg()
+    path = ensure_host_gguf(jd, w)
+    ref = Reference("_r8" if w["rank"] == 8 else "")
+    ref.host_load(path)
+    ref.lib.jdr_host_lora_seed(*lora_args(w))
+    ref.lib.jdr_host_reset_seq(n_prompt + n_decode + 1)
+    pr, _ = prompts_for(dict(w, B=1, over=dict(vocab_size=w["V"]), prompt=n_prompt), 0)
+    lg = None
+    for pos, t in enumerate(pr[0]):
+        lg, _ = ref.host_forward(int(t), pos)
+    pos = n_prompt
+    t0 = time.perf_counter()
+    for _ in range(n_decode):
+        lg, _ = ref.host_forward(int(np.argmax(lg)), pos)
+        pos += 1
+    dt = time.perf_counter() - t0
+    ref.lib.jdr_host_free()
+    threads = min(32, os.cpu_count() or 1)
+    return n_decode / dt, threads, "1 sequence, %d-token prompt untimed, %d greedy tokens timed" % (n_prompt, n_decode)
+
+
 def run_reference_arm(args, w):
     dist, world, rank, local = dist_setup()
     if rank != 0:
         return
     threads = os.cpu_count() or 1
+    if w.get("host"):
+        tps, threads, sample = cpu_reference_host(w, w["ref_prompt"], w["ref_decode"])
+        kind, n = "reference", w["ref_decode"]
+        line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": args.gpus,
+                "steps": n, "warmup": 0, "ms_per_step": 1000.0 / tps, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": args.workload, "batch": 1},
+                "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": kind, "sample": sample},
+                "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     n = max(1, min(args.steps, w["ref_decode"] * 4))
     tps, kind, sample = cpu_reference(w, n, threads)
     line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": args.gpus,
@@ -244,6 +309,104 @@ def run_reference_arm(args, w):
             "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": kind, "sample": sample},
             "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def packed_bytes(w):
+    """Packed weight bytes of a host model (per weight: 34/32 B for Q8_0, 144/256 B for Q4_K)."""
+    bpw = {8: 34 / 32, 12: 144 / 256, 0: 4}[w["dtype"]]
+    D, FF, V, L = w["D"], w["FF"], w["V"], w["L"]
+    hd = D // w["H"]
+    per_layer = (w["H"] * hd + 2 * w["KV"] * hd) * D + D * w["H"] * hd + 3 * FF * D
+    return bpw * (L * per_layer + V * D)
+
+
+def run_host(args, w, dist, world, rank, local):
+    jd = load_pkg()
+    B, P, S = w["B"], w["prompt"], w["max_seq"]
+    if rank == 0:
+        ensure_host_gguf(jd, w)
+    barrier(dist)
+    path = ensure_host_gguf(jd, w)
+    hm = jd.HostModel(path, lora_rank=w["rank"])
+    hm.lora_seed(*lora_args(w))
+    ctx = jd.Context(local)
+    if world > 1:
+        import torch
+        ids = [None]
+        if rank == 0:
+            buf = C.create_string_buffer(128)
+            jd.check(jd.lib().jdg_comm_unique_id(buf))
+            ids[0] = bytes(buf.raw)
+        dist.broadcast_object_list(ids, src=0)
+        eng = jd.Engine.host_tp(ctx, hm, B, S, rank, world, ids[0])
+    else:
+        eng = jd.Engine.host(ctx, hm, B, S)
+    prompts, _ = prompts_for(dict(w, over=dict(vocab_size=w["V"])), 0)
+    eng.set_prompt(prompts, [P] * B)
+    prefill_ms = eng.run(B, P - 1)
+    eng.run(B, args.warmup)
+    clocks = Clocks(local)
+    barrier(dist)
+    eng.reset_stats()
+    l0 = eng.launches()
+    clocks.start()
+    ms = eng.run(B, args.steps)
+    ck = clocks.stop()
+    n_launch = eng.launches() - l0
+    stats = eng.stats()
+    ms = allmax(dist, ms)
+    barrier(dist)
+    value = B * args.steps / (ms / 1000.0)
+    n_e2e = min(args.steps, 16)
+    tok_h, pos_h = eng.state(B)
+    barrier(dist)
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        nxt, _, _, _ = eng.step(tok_h, pos_h)
+        tok_h, pos_h = nxt, pos_h + 1
+    e2e_s = allmax(dist, time.perf_counter() - t0)
+    barrier(dist)
+    tr = eng.trace(B)
+    # algorithmic bytes per step: packed weights (each rank reads its shard), f32 tok_emb rows,
+    # the LoRA factors and vote rows of the experts elected by any sequence (last step's trace)
+    # in every layer, KV read (device count) + append
+    L, D, R = w["L"], w["D"], w["rank"]
+    kd = w["KV"] * (D // w["H"])
+    lora = 0
+    for l in range(L):
+        used = {int(e) for b in range(B) for e in tr["sel"][b, l] if e >= 0}
+        lora += len(used) * 2 * D * R * 4 + w["adapters"] * D * 4
+    per_step = packed_bytes(w) + B * D * 4 + world * lora + 4 * D * (2 * L + 1)
+    bytes_run = args.steps * per_step + stats[1] * L * 2 * kd * 4 + args.steps * B * L * 2 * kd * 4
+    peak, peak_kind = peaks()
+    achieved = bytes_run / (ms / 1000.0) / 1e9
+    roof = {"bound": "hbm", "achieved": achieved, "peak": peak * world, "unit": "GB/s",
+            "frac": achieved / (peak * world), "traffic": dram_traffic(args.workload), "peak_source": peak_kind,
+            "kernel": "whole decode step (CUDA graph of %d launches)" % (n_launch // max(1, args.steps)),
+            "algorithmic_bytes_per_step": bytes_run / args.steps}
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (GGUF of N(0,0.02) weights quantised per block, uniform prompts)",
+            "config": {"workload": args.workload, "arch": w["arch"], "layers": L, "dim": D, "heads": w["H"],
+                       "kv_heads": w["KV"], "ffn": w["FF"], "vocab": w["V"], "dtype": {8: "Q8_0", 12: "Q4_K"}[w["dtype"]],
+                       "lora": "%d x rank %d" % (w["adapters"], R), "global_batch": B, "prompt": P,
+                       "parallelism": "tp%d" % world if world > 1 else "1 GPU",
+                       "l2": "inputs larger than L2: %.0f MB per step" % (per_step / 1e6)},
+            "roofline": roof, "prefill_ms": prefill_ms, "clocks": ck, "gpu_launches": n_launch,
+            "e2e": {"value": B * n_e2e / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 8 * B,
+                    "d2h_bytes_per_step": 4 * B, "steps": n_e2e}}
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        tps, threads, sample = cpu_reference_host(w, w["ref_prompt"], w["ref_decode"])
+        line["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": threads, "kind": "reference",
+                                "sample": sample}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    eng.close()
+    hm.close()
+    ctx.close()
+    if dist is not None:
+        dist.destroy_process_group()
 
 
 def main():
@@ -262,6 +425,9 @@ def main():
         run_reference_arm(args, w)
         return
     dist, world, rank, local = dist_setup()
+    if w.get("host"):
+        run_host(args, w, dist, world, rank, local)
+        return
     jd = load_pkg()
     B, P = w["B"], w["prompt"]
     cfg = jd.config_from_depth(w["depth"], **w["over"])
