@@ -417,8 +417,11 @@ def main():
     ap.add_argument("--workload", default="depth12_bs1", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prompt", type=int, default=None, help="override the prompt length (profiling runs)")
     args = ap.parse_args()
-    w = WORKLOADS[args.workload]
+    w = dict(WORKLOADS[args.workload])
+    if args.prompt:
+        w["prompt"] = max(2, args.prompt)
     args.steps = w["steps"] if args.steps is None else args.steps
     args.warmup = w["warmup"] if args.warmup is None else max(3, args.warmup)
     if args.impl == "reference":

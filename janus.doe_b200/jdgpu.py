@@ -255,8 +255,11 @@ class Context:
 class Engine:
     """Uploaded model + per-sequence state on one GPU."""
 
-    def __init__(self, ctx, handle, n_layers, vocab):
+    def __init__(self, ctx, handle, n_layers, vocab, ldl=None):
+        # ldl: logits per sequence held by this engine (the rank's vocabulary slice under
+        # tensor parallelism, the whole vocabulary otherwise)
         self.ctx, self.h, self.L, self.V = ctx, handle, n_layers, vocab
+        self.ldl = vocab if ldl is None else ldl
 
     @classmethod
     def own(cls, ctx, model, max_batch=1):
@@ -277,7 +280,9 @@ class Engine:
         h = C.c_void_p()
         buf = C.create_string_buffer(bytes(nccl_id), 128)
         ctx.check(lib().jdg_host_upload_tp(ctx.h, C.byref(hm.h), max_batch, max_seq, rank, world, buf, C.byref(h)))
-        return cls(ctx, h, min(hm.h.n_layers, MAXL), hm.h.vocab)
+        V = hm.h.vocab
+        per = (V + world - 1) // world
+        return cls(ctx, h, min(hm.h.n_layers, MAXL), V, max(1, min(per, V - rank * per)))
 
     def _ck(self, rc):
         return self.ctx.check(rc)
@@ -318,7 +323,7 @@ class Engine:
         B = tok.size
         nxt = np.zeros(B, np.int32)
         r = None if rng is None else np.ascontiguousarray(rng, np.uint64).copy()
-        lg = np.zeros((B, self.V), np.float32) if logits else None
+        lg = np.zeros((B, self.ldl), np.float32) if logits else None
         tr, trd = (self._trace_bufs(B) if trace else (None, None))
         self._ck(lib().jdg_step(self.h, B, _p(tok, I32P), _p(pos, I32P), None if r is None else _p(r, U64P),
                                 _p(nxt, I32P), None if lg is None else _p(lg, F32P),
@@ -332,7 +337,7 @@ class Engine:
         return t, d
 
     def logits(self, B):
-        lg = np.zeros((B, self.V), np.float32)
+        lg = np.zeros((B, self.ldl), np.float32)
         self._ck(lib().jdg_get_logits(self.h, B, _p(lg, F32P)))
         return lg
 
