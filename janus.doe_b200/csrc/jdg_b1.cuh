@@ -130,7 +130,7 @@ struct ElectOut {
     float ema;
     float inv;  // 1/sqrt(mean(x^2)+eps) of the FFN RMSNorm
 };
-__device__ void b1_elect(const B1Args &a, ElectOut &eo, const float cons_in) {
+static __device__ void b1_elect(const B1Args &a, ElectOut &eo, const float cons_in) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nb = a.nparts;  // <= 256
     __shared__ float tot[4][17];
@@ -362,9 +362,10 @@ static __global__ __launch_bounds__(128) void k_b1_qkv(B1Args a) {
 // pos is RoPE'd from qkv, appended to the cache and used directly.  Writes per-head
 // partials (unnormalised o, chunk max m, chunk sum l); WO merges them.
 // s = (q.k)*scale, then clamp*tanh(s/clamp) (janusdoe.c:899-910).
+// One attention CTA: positions [128c, 128c+128) of KV head g (called by k_b1_attn and by
+// the host chain's attention kernel).  Dynamic shared memory: 2*128*(HD+4) floats.
 template <int HD>
-static __global__ __launch_bounds__(128) void k_b1_attn(B1Args a) {
-    TlMark tlm(a.tl, a.l * 5 + 1);
+__device__ __forceinline__ void b1_attn_cta(const B1Args &a, const int c, const int g, TlMark &tlm) {
     constexpr int RS = HD + 4;  // padded row stride (conflict-free float4 reads)
     constexpr int CH = kB1Chunk;
     extern __shared__ __align__(16) float dsm[];
@@ -372,7 +373,7 @@ static __global__ __launch_bounds__(128) void k_b1_attn(B1Args a) {
     float(*vs)[RS] = reinterpret_cast<float(*)[RS]>(dsm + CH * RS);
     __shared__ __align__(16) float qs[kMaxHG][HD];
     __shared__ float ps[kMaxHG][CH];
-    const int c = blockIdx.x, g = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int p = a.pos[0];
     const int t0 = c * CH;
     const int hg = a.H / a.KVH, kd = a.kd;
@@ -478,6 +479,12 @@ static __global__ __launch_bounds__(128) void k_b1_attn(B1Args a) {
             dst[HD + 1] = l;
         }
     }
+}
+
+template <int HD>
+static __global__ __launch_bounds__(128) void k_b1_attn(B1Args a) {
+    TlMark tlm(a.tl, a.l * 5 + 1);
+    b1_attn_cta<HD>(a, blockIdx.x, blockIdx.y, tlm);
 }
 
 // ---------------------------------------------------------------------------------

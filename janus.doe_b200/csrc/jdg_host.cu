@@ -11,7 +11,7 @@
 #include <vector>
 
 #include "jdg_engine.h"
-#include "jdg_host_kernels.cuh"
+#include "jdg_hb1.cuh"
 
 using namespace jdg;
 
@@ -48,12 +48,24 @@ struct HostPriv {
     QW wqkv[JD_MAX_LAYERS], wo[JD_MAX_LAYERS], gu[JD_MAX_LAYERS], dn[JD_MAX_LAYERS];
     QW out;
     float *ones = nullptr;                  // [D] of 1.0f for absent norms
+    // batch-1 chain (jdg_hb1.cuh)
+    bool hb1 = false;                       // shapes and dtypes fit the chain
+    int *alive_list[JD_MAX_LAYERS] = {};    // alive expert ids, ascending
+    int gu_ctas = 0, lm_ctas = 0;           // persistent grids: resident CTAs on all SMs
+    float *votes = nullptr, *tall = nullptr;
 };
 
 HostPriv *priv(jdg_engine *e) { return (HostPriv *)e->host_priv; }
 
 int block_elems(int dt) { return dt == JD_Q8_0 ? 32 : dt == JD_Q4_K ? 256 : dt == JD_F32 ? 1 : 0; }
 size_t block_bytes(int dt) { return dt == JD_Q8_0 ? 34 : dt == JD_Q4_K ? 144 : dt == JD_F32 ? 4 : 0; }
+
+// register bucket of the batch-1 chain for a packed matrix (0: not supported there)
+int hb1_maxc(const QW &w) {
+    if (w.dt != JD_Q8_0 && w.dt != JD_Q4_K) return 0;
+    const int n = prow_chunks(w.dt, w.cols);
+    return n <= 4 ? 4 : n <= 8 ? 8 : n <= 12 ? 12 : n <= 16 ? 16 : 0;
+}
 
 // Host-side repack of selected rows (and a block-aligned column range) of a packed tensor
 // into the device layout described in jdg_host_kernels.cuh.
@@ -145,6 +157,27 @@ static int upload_f32(jdg_engine *e, const float *src, size_t n, float **dst) {
 
 int jdg_alloc_state(jdg_engine *e);
 int jdg_reset(jdg_engine *e, int slot);
+int jdg_host_set_attrs(jdg_engine *e);
+
+// resident 128-thread CTAs per SM of the chain's GU (which 0) or LM (which 1) kernel for w
+static int hb1_resident(const QW &w, size_t smem, int which) {
+    int nb = 0;
+#define OCC(DTV, MC)                                                                                            \
+    (which ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_hb1_lm<DTV, MC>, 128, smem)                    \
+           : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_hb1_gu<DTV, MC>, 128, smem))
+    switch (w.dt * 100 + hb1_maxc(w)) {
+    case 804: OCC(8, 4); break;
+    case 808: OCC(8, 8); break;
+    case 812: OCC(8, 12); break;
+    case 816: OCC(8, 16); break;
+    case 1204: OCC(12, 4); break;
+    case 1208: OCC(12, 8); break;
+    case 1212: OCC(12, 12); break;
+    default: OCC(12, 16); break;
+    }
+#undef OCC
+    return nb;
+}
 
 static int host_upload_impl(jdg_engine *e, const jd_host_model *h, int max_batch, int max_seq, int rank, int world) {
     HostPriv *hp = priv(e);
@@ -325,6 +358,46 @@ static int host_upload_impl(jdg_engine *e, const jd_host_model *h, int max_batch
     e->kv_bstride = (long)L * max_seq * e->kd;
     DALLOC(e->kc, (size_t)B * e->kv_bstride * 4);
     DALLOC(e->vc, (size_t)B * e->kv_bstride * 4);
+    DALLOC(hp->votes, kMaxE * 4);
+    DALLOC(hp->tall, (size_t)kMaxE * R * 4);
+    DALLOC(e->amax_v, 1024 * 4);
+    DALLOC(e->amax_i, 1024 * 4);
+    for (int l = 0; l < L; l++) {
+        std::vector<int> al;
+        for (int x = 0; x < kMaxE; x++)
+            if (h->alive[l][x]) al.push_back(x);
+        al.resize(kMaxE, 0);
+        DALLOC(hp->alive_list[l], kMaxE * 4);
+        CK(cudaMemcpy(hp->alive_list[l], al.data(), kMaxE * 4, cudaMemcpyHostToDevice));
+    }
+    {
+        // batch-1 chain: one GPU, packed Q8_0/Q4_K matrices with at most 16 code chunks per
+        // row held in registers, head sizes the attention CTA handles, float4 vector loads
+        bool ok = world == 1 && HD % 64 == 0 && HD <= 128 && hp->H_loc <= 64 && max_seq <= 1024 && D % 128 == 0 &&
+                  e->qd % 128 == 0 && e->hidden % 64 == 0 && hb1_maxc(hp->out) > 0;
+        for (int l = 0; l < L && ok; l++)
+            ok = hb1_maxc(hp->wqkv[l]) > 0 && hb1_maxc(hp->wo[l]) > 0 && hb1_maxc(hp->gu[l]) > 0 &&
+                 hb1_maxc(hp->dn[l]) > 0;
+        hp->hb1 = ok;
+        const char *g = getenv("JDG_GENERIC");
+        e->force_generic = g && g[0] == '1';
+        if (ok) {
+            // persistent GU and LM grids: as many CTAs as stay resident on every SM
+            int rc2 = jdg_host_set_attrs(e);
+            if (rc2 != JD_OK) return rc2;
+            int dev = 0, n_sm = 148;
+            CK(cudaGetDevice(&dev));
+            CK(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
+            const size_t vec_sm = ((size_t)D + D / 16) * 4;
+            hp->gu_ctas = hb1_resident(hp->gu[0], vec_sm, 0) * n_sm;
+            hp->lm_ctas = hb1_resident(hp->out, vec_sm, 1) * n_sm;
+            if (hp->gu_ctas < 1 || hp->lm_ctas < 1) {
+                jdg_set_err(e->ctx, "batch-1 chain: occupancy query failed");
+                return JD_ECUDA;
+            }
+            hp->lm_ctas = std::min(hp->lm_ctas, 1024);  // argmax partials
+        }
+    }
     int rc = jdg_alloc_state(e);
     if (rc != JD_OK) return rc;
     rc = jdg_reset(e, -1);
@@ -369,13 +442,143 @@ int jdg_host_set_attrs(jdg_engine *e) {
     SETA((k_qgemm<8, EPI_STORE>)); SETA((k_qgemm<8, EPI_ADD>)); SETA((k_qgemm<8, EPI_SWIGLU>));
     SETA((k_qgemm<12, EPI_STORE>)); SETA((k_qgemm<12, EPI_ADD>)); SETA((k_qgemm<12, EPI_SWIGLU>));
     SETA((k_qgemm<0, EPI_STORE>)); SETA((k_qgemm<0, EPI_ADD>)); SETA((k_qgemm<0, EPI_SWIGLU>));
+    SETA((k_hb1_attn<64>)); SETA((k_hb1_attn<128>));
+#define SETA_Q(K)                                                                                             \
+    SETA((K<8, 4>)); SETA((K<8, 8>)); SETA((K<8, 12>)); SETA((K<8, 16>));                                     \
+    SETA((K<12, 4>)); SETA((K<12, 8>)); SETA((K<12, 12>)); SETA((K<12, 16>));
+    SETA_Q(k_hb1_qkv) SETA_Q(k_hb1_gu) SETA_Q(k_hb1_dn) SETA_Q(k_hb1_lm)
+    SETA((k_hb1_wo<8, 4, 64>)); SETA((k_hb1_wo<8, 8, 64>)); SETA((k_hb1_wo<8, 12, 64>)); SETA((k_hb1_wo<8, 16, 64>));
+    SETA((k_hb1_wo<12, 4, 64>)); SETA((k_hb1_wo<12, 8, 64>)); SETA((k_hb1_wo<12, 12, 64>));
+    SETA((k_hb1_wo<12, 16, 64>));
+    SETA((k_hb1_wo<8, 4, 128>)); SETA((k_hb1_wo<8, 8, 128>)); SETA((k_hb1_wo<8, 12, 128>));
+    SETA((k_hb1_wo<8, 16, 128>));
+    SETA((k_hb1_wo<12, 4, 128>)); SETA((k_hb1_wo<12, 8, 128>)); SETA((k_hb1_wo<12, 12, 128>));
+    SETA((k_hb1_wo<12, 16, 128>));
+#undef SETA_Q
 #undef SETA
     return JD_OK;
+}
+
+// ------------------------------------------------------------------------------------
+// Batch-1 chain launches (Programmatic Dependent Launch, jdg_hb1.cuh)
+template <typename... KArgs, typename... Args>
+static void hb1_launch(jdg_engine *e, void (*kern)(KArgs...), unsigned grid, size_t smem, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = e->st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, args...);
+    e->launches++;
+}
+#define HB1_Q(KERN, QWV, GRID, SMEM, ARG)                                                          \
+    switch ((QWV).dt * 100 + hb1_maxc(QWV)) {                                                      \
+    case 804: hb1_launch(e, KERN<8, 4>, GRID, SMEM, ARG); break;                                  \
+    case 808: hb1_launch(e, KERN<8, 8>, GRID, SMEM, ARG); break;                                  \
+    case 812: hb1_launch(e, KERN<8, 12>, GRID, SMEM, ARG); break;                                 \
+    case 816: hb1_launch(e, KERN<8, 16>, GRID, SMEM, ARG); break;                                 \
+    case 1204: hb1_launch(e, KERN<12, 4>, GRID, SMEM, ARG); break;                                \
+    case 1208: hb1_launch(e, KERN<12, 8>, GRID, SMEM, ARG); break;                                \
+    case 1212: hb1_launch(e, KERN<12, 12>, GRID, SMEM, ARG); break;                               \
+    default: hb1_launch(e, KERN<12, 16>, GRID, SMEM, ARG); break;                                 \
+    }
+#define HB1_WO(HDV, QWV, GRID, SMEM, ARG)                                                          \
+    switch ((QWV).dt * 100 + hb1_maxc(QWV)) {                                                      \
+    case 804: hb1_launch(e, k_hb1_wo<8, 4, HDV>, GRID, SMEM, ARG); break;                         \
+    case 808: hb1_launch(e, k_hb1_wo<8, 8, HDV>, GRID, SMEM, ARG); break;                         \
+    case 812: hb1_launch(e, k_hb1_wo<8, 12, HDV>, GRID, SMEM, ARG); break;                        \
+    case 816: hb1_launch(e, k_hb1_wo<8, 16, HDV>, GRID, SMEM, ARG); break;                        \
+    case 1204: hb1_launch(e, k_hb1_wo<12, 4, HDV>, GRID, SMEM, ARG); break;                       \
+    case 1208: hb1_launch(e, k_hb1_wo<12, 8, HDV>, GRID, SMEM, ARG); break;                       \
+    case 1212: hb1_launch(e, k_hb1_wo<12, 12, HDV>, GRID, SMEM, ARG); break;                      \
+    default: hb1_launch(e, k_hb1_wo<12, 16, HDV>, GRID, SMEM, ARG); break;                        \
+    }
+
+static void enqueue_host_step_hb1(jdg_engine *e) {
+    HostPriv *hp = priv(e);
+    const int D = e->D, L = e->L, HD = e->HD, R = e->lora_rank;
+    int n_sm = 148, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    HB1Args a = {};
+    a.D = D; a.H = e->Hh; a.KVH = e->KVH; a.HD = HD; a.qd = e->qd; a.kd = e->kd; a.qkvd = e->qkvd;
+    a.hidden = e->hidden; a.V = e->V; a.max_seq = e->max_seq; a.L = L; a.R = R;
+    a.eps = e->eps; a.lora_alpha = e->lora_alpha;
+    a.tok_emb = e->tok_emb; a.tok = e->tok; a.pos = e->pos;
+    a.x = e->x; a.xn = e->xn;
+    a.votes = hp->votes; a.tall = hp->tall;
+    a.kcnt = e->kcnt; a.sel = e->sel; a.selw = e->selw; a.consensus = e->consensus;
+    a.tr_k = e->tr_k; a.tr_sel = e->tr_sel; a.tr_w = e->tr_w; a.tr_ema = e->tr_ema;
+    a.part = e->part;
+    a.tickets = e->tickets; a.amax_v = e->amax_v; a.amax_i = e->amax_i;
+    a.tok_out = e->tok; a.plen = e->plen; a.prompt = e->prompt; a.hist = e->hist; a.hist_n = e->hist_n;
+    a.next_out = e->next_out; a.Hmax = e->Hmax; a.greedy_pick = e->temp <= 0.f;
+    a.stats = e->stats; a.err = e->err; a.tl = e->timeline;
+    // the attention CTAs take the own-model chain's arguments
+    B1Args ab = {};
+    ab.H = e->Hh; ab.KVH = e->KVH; ab.HD = HD; ab.qd = e->qd; ab.kd = e->kd; ab.max_seq = e->max_seq;
+    ab.rope_norm = e->rope_norm; ab.rope_cos = e->rope_cos; ab.rope_sin = e->rope_sin;
+    ab.clamp = 0.f; ab.inv_clamp = 0.f;
+    ab.pos = e->pos; ab.qkv = e->qkv; ab.part = e->part; ab.err = e->err;
+    const int nch = (e->max_seq + kB1Chunk - 1) / kB1Chunk;
+    const size_t vec_sm = ((size_t)D + D / 16) * 4;
+    const size_t attn_sm = (size_t)2 * kB1Chunk * (HD + 4) * 4;
+    for (int l = 0; l < L; l++) {
+        HostLayerDev &hl = e->hl[l];
+        a.l = l;
+        a.embed = l == 0;
+        a.focus = hl.focus;
+        a.w_vote = hl.w_vote; a.lora_A = hp->lora_A[l]; a.lora_B = hp->lora_B[l];
+        a.alive = hl.alive; a.alive_list = hp->alive_list[l]; a.n_alive = e->n_alive[l];
+        // QKV
+        a.w = hp->wqkv[l];
+        a.norm = hl.attn_norm ? hl.attn_norm : hp->ones;
+        a.y = e->qkv;
+        HB1_Q(k_hb1_qkv, a.w, (unsigned)((e->qkvd + 3) / 4), vec_sm, a);
+        // ATTN (+ votes and LoRA projections)
+        ab.l = l;
+        ab.kc = e->kc + (size_t)l * e->max_seq * e->kd;
+        ab.vc = e->vc + (size_t)l * e->max_seq * e->kd;
+        ab.scale = (1.0f / sqrtf((float)HD)) * (1.0f + hl.attn_bias);
+        a.natt = nch * e->KVH;
+        const unsigned naux = (unsigned)((kMaxE + e->n_alive[l] * R + 3) / 4);
+        if (HD == 64) hb1_launch(e, k_hb1_attn<64>, (unsigned)a.natt + naux, attn_sm, ab, a);
+        else hb1_launch(e, k_hb1_attn<128>, (unsigned)a.natt + naux, attn_sm, ab, a);
+        // WO (+ election CTA)
+        a.w = hp->wo[l];
+        const size_t wo_sm = ((size_t)e->qd + e->qd / 16) * 4;
+        if (HD == 64) { HB1_WO(64, a.w, (unsigned)((D + 3) / 4), wo_sm, a); }
+        else { HB1_WO(128, a.w, (unsigned)((D + 3) / 4), wo_sm, a); }
+        // GU
+        a.w = hp->gu[l];
+        a.norm = hl.ffn_norm ? hl.ffn_norm : hp->ones;
+        a.y = e->hbuf;
+        HB1_Q(k_hb1_gu, a.w, (unsigned)(1 + hp->gu_ctas), vec_sm, a);
+        // DN (+ LoRA deltas)
+        a.w = hp->dn[l];
+        a.hin = e->hbuf;
+        HB1_Q(k_hb1_dn, a.w, (unsigned)((D + 3) / 4), ((size_t)e->hidden + e->hidden / 16) * 4, a);
+    }
+    a.w = hp->out;
+    a.norm = e->output_norm;
+    a.y = e->logits;
+    a.embed = 0;
+    HB1_Q(k_hb1_lm, a.w, (unsigned)hp->lm_ctas, vec_sm, a);
+    if (!a.greedy_pick) jdg_launch_pick(e, 1);
 }
 
 // One decode step of gguf_host_forward (janusdoe.c:3160-3322) for slots 0..B-1.
 int jdg_enqueue_host_step(jdg_engine *e, int B) {
     HostPriv *hp = priv(e);
+    if (B == 1 && hp->hb1 && !e->force_generic) {
+        enqueue_host_step_hb1(e);
+        return JD_OK;
+    }
     const int D = e->D, L = e->L;
     const bool tp = hp->world > 1;
     const float scale = 1.0f / sqrtf((float)e->HD);

@@ -20,10 +20,26 @@ SMALL = {
     "q4k_norm": ("llama", 512, 3, 4, 2, 1024, 2000, 12, 5e5, 16, 8),
     "q8_gqa8": ("qwen2", 512, 2, 8, 1, 1024, 1500, 8, 1e4, 8, 4),
 }
+# full-width layers of the 1.1B Q8_0 and 8B Q4_K shapes (fewer layers, smaller vocabulary):
+# rows of 5632 and 14336 weights exercise the widest register buckets of the batch-1 chain
+WIDE = {
+    "q8_c4_layer": ("qwen2", 2048, 2, 32, 4, 5632, 3000, 8, 1e4, 8, 4),
+    "q4k_c5_layer": ("llama", 4096, 1, 32, 8, 14336, 2000, 12, 5e5, 16, 8),
+}
+
+
+@pytest.fixture(params=["chain", "generic"])
+def b1_path(request, monkeypatch):
+    """Batch 1 runs either the PDL kernel chain (default) or the generic kernels."""
+    if request.param == "generic":
+        monkeypatch.setenv("JDG_GENERIC", "1")
+    else:
+        monkeypatch.delenv("JDG_GENERIC", raising=False)
+    return request.param
 
 
 def _models(jd, orc, name, tmp_path, max_seq=96):
-    arch, D, L, H, KV, FF, V, dt, theta, R, na = SMALL[name]
+    arch, D, L, H, KV, FF, V, dt, theta, R, na = SMALL[name] if name in SMALL else WIDE[name]
     path = str(tmp_path / ("%s.gguf" % name))
     jd.write_synthetic_gguf(path, arch, L, D, FF, H, KV, V, theta, 1e-5, dt, 17, 0.02)
     hm = jd.HostModel(path, lora_rank=R)
@@ -95,12 +111,12 @@ def _oracle_stream(om, prompt, n_gen):
     return st, lgs, trs
 
 
-@pytest.mark.parametrize("name", sorted(SMALL))
-def test_host_greedy_parity(jd, orc, gpu_ctx, tmp_path, name):
+@pytest.mark.parametrize("name", sorted(SMALL) + sorted(WIDE))
+def test_host_greedy_parity(jd, orc, gpu_ctx, tmp_path, name, b1_path):
     """Teacher-forced logits/elections, then the free-running device loop's greedy stream."""
     hm, om, V = _models(jd, orc, name, tmp_path)
     L = hm.h.n_layers
-    P, G = 12, 24
+    P, G = (12, 24) if name in SMALL else (5, 6)
     prompt = np.random.default_rng(5).integers(0, V, P).astype(np.int32)
     stream, lgs, trs = _oracle_stream(om, prompt, G)
     eng = jd.Engine.host(gpu_ctx, hm, 1, 96)
