@@ -72,12 +72,14 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def dram_traffic(workload):
+def dram_traffic(workload, alg_bytes_per_step):
+    """DRAM bytes per step from an ncu capture of this workload (profiles/dram_traffic.json):
+    the captured traffic/algorithmic ratio applied to this run's algorithmic bytes."""
     p = os.path.join(ROOT, "profiles", "dram_traffic.json")
     if os.path.exists(p):
         d = json.load(open(p))
         if workload in d:
-            return d[workload]
+            return d[workload]["traffic_over_algorithmic"] * alg_bytes_per_step
     return None
 
 
@@ -381,7 +383,8 @@ def run_host(args, w, dist, world, rank, local):
     peak, peak_kind = peaks()
     achieved = bytes_run / (ms / 1000.0) / 1e9
     roof = {"bound": "hbm", "achieved": achieved, "peak": peak * world, "unit": "GB/s",
-            "frac": achieved / (peak * world), "traffic": dram_traffic(args.workload), "peak_source": peak_kind,
+            "frac": achieved / (peak * world), "traffic": dram_traffic(args.workload, bytes_run / args.steps),
+            "peak_source": peak_kind,
             "kernel": "whole decode step (CUDA graph of %d launches)" % (n_launch // max(1, args.steps)),
             "algorithmic_bytes_per_step": bytes_run / args.steps}
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -478,7 +481,7 @@ def main():
     bytes_run = own_bytes(cfg, alive, B, args.steps, stats)
     peak, peak_kind = peaks()
     achieved = bytes_run / (ms / 1000.0) / 1e9
-    traffic = dram_traffic(args.workload)
+    traffic = dram_traffic(args.workload, bytes_run / args.steps)
     roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
             "traffic": traffic, "peak_source": peak_kind,
             "kernel": "whole decode step (CUDA graph of %d launches)" % (n_launch // max(1, args.steps)),

@@ -11,6 +11,7 @@ enum {
     JDG_ERR_POS = 2,     // position outside [0, max_seq)
     JDG_ERR_ROUTE = 4,   // election produced an invalid expert slot
     JDG_ERR_SHAPE = 8,   // a kernel met a shape it does not support
+    JDG_ERR_TIMEOUT = 16,  // a bounded wait on an asynchronous copy ran out
 };
 
 __device__ __forceinline__ float warp_sum(float v) {

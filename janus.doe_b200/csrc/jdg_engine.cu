@@ -747,9 +747,9 @@ static int check_err(jdg_engine *e) {
     CK(cudaStreamSynchronize(e->st));
     if (h) {
         CK(cudaMemsetAsync(e->err, 0, 4, e->st));
-        jdg_set_err(e->ctx, "device-side check failed (flags 0x%x: %s%s%s%s)", h, (h & JDG_ERR_TOKEN) ? "token " : "",
+        jdg_set_err(e->ctx, "device-side check failed (flags 0x%x: %s%s%s%s%s)", h, (h & JDG_ERR_TOKEN) ? "token " : "",
                     (h & JDG_ERR_POS) ? "position " : "", (h & JDG_ERR_ROUTE) ? "route " : "",
-                    (h & JDG_ERR_SHAPE) ? "shape" : "");
+                    (h & JDG_ERR_SHAPE) ? "shape " : "", (h & JDG_ERR_TIMEOUT) ? "copy wait timed out" : "");
         return JD_ESTATE;
     }
     return JD_OK;

@@ -15,9 +15,10 @@
 // then LM (final RMSNorm prologue, logits, last-CTA greedy pick).
 //
 // Every kernel loads its first weight rows into registers before griddepcontrol.wait, so
-// that HBM traffic overlaps the previous kernel.  The election, the LoRA projections and
-// the residual row a DN CTA updates are two or more kernels old when DN starts, so DN
-// reads them (and finishes the LoRA dot products) before its wait as well.
+// that HBM traffic overlaps the previous kernel.  Only data written two or more kernels
+// back is read before a wait: DN finishes the LoRA dot products of every alive expert (t_e
+// from ATTN) and reads its residual row (from WO) early, and the election (from GU, the
+// kernel just before) after its wait.
 #pragma once
 #include "jdg_b1.cuh"
 #include "jdg_host_kernels.cuh"
@@ -496,8 +497,8 @@ static __global__ __launch_bounds__(128) void k_hb1_gu(HB1Args a) {
 // ---------------------------------------------------------------------------------
 // DN: x[row] += focus * (Wd[row] . h) (janusdoe.c:3239-3240), then for each elected expert
 // in order x[row] += (alpha * w_ki) * (A_e[row] . t_e) (janusdoe.c:3293-3300).  The LoRA dot
-// products use data two or more kernels old and finish before the wait; lane ki holds
-// expert ki's.  Dynamic smem: hidden + hidden/16 floats.
+// products of every alive expert use data two or more kernels old and finish before the
+// wait; the election (GU) is read after it.  Dynamic smem: hidden + hidden/16 floats.
 template <int DT, int MAXC>
 static __global__ __launch_bounds__(128) void k_hb1_dn(HB1Args a) {
     TlMark tlm(a.tl, a.l * 5 + 4);
@@ -505,25 +506,38 @@ static __global__ __launch_bounds__(128) void k_hb1_dn(HB1Args a) {
     float *hs = hsm, *hsum = hsm + a.hidden;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int row = blockIdx.x * 4 + warp;
+    __shared__ float lo_s[4][kMaxE];
     PRow<DT, MAXC> r;
     if (row < a.D) prow_load<DT, MAXC>(r, a.w, row, lane);
-    float lora = 0.f, wk = 0.f;
-    int k = 0;
     float xold = 0.f;
     if (row < a.D) {
-        k = __ldcg(a.kcnt);
+        // t_e (ATTN) and this row of x (WO) are two or more kernels old: the LoRA dot
+        // products A_e[row] . t_e of every alive expert finish before the wait
         xold = __ldcg(a.x + row);
-        if (lane < k) {
-            const int e = __ldcg(a.sel + lane);
-            wk = __fmul_rn(a.lora_alpha, __ldcg(a.selw + lane));
+        if (lane < a.n_alive) {
+            const int e = a.alive_list[lane];
             const float *Ar = a.lora_A + ((size_t)e * a.D + row) * a.R;
             const float *tr = a.tall + (size_t)e * a.R;
+            float lora = 0.f;
             for (int q = 0; q < a.R; q++) lora = fmaf(__ldg(Ar + q), __ldcg(tr + q), lora);
+            lo_s[warp][e] = lora;
         }
     }
     pdl_wait();
     tlm.waited();
     pdl_trigger();
+    // the election was made by GU, the kernel just before: read after the wait
+    const int k = min(__ldcg(a.kcnt), kMaxE);
+    int ek = 0;
+    float wk = 0.f;
+    if (lane < k) {
+        ek = __ldcg(a.sel + lane);
+        wk = __fmul_rn(a.lora_alpha, __ldcg(a.selw + lane));
+        if (ek < 0 || ek >= kMaxE) {
+            ek = 0;
+            wk = 0.f;
+        }
+    }
     for (int i = threadIdx.x; i < a.hidden / 4; i += 128)
         xput4<DT>(hs, i, __ldcg(reinterpret_cast<const float4 *>(a.hin) + i));
     __syncthreads();
@@ -540,8 +554,9 @@ static __global__ __launch_bounds__(128) void k_hb1_dn(HB1Args a) {
     const float v = prow_dot<DT, MAXC>(r, a.hidden, hs, hsum, lane);
     float xr = __fadd_rn(xold, __fmul_rn(v, a.focus));
     for (int ki = 0; ki < k; ki++) {
-        const float s = __shfl_sync(JDG_FULL, lora, ki), w = __shfl_sync(JDG_FULL, wk, ki);
-        xr = __fadd_rn(xr, __fmul_rn(w, s));
+        const int e = __shfl_sync(JDG_FULL, ek, ki);
+        const float w = __shfl_sync(JDG_FULL, wk, ki);
+        xr = __fadd_rn(xr, __fmul_rn(w, lo_s[warp][e]));
     }
     if (lane == 0) a.x[row] = xr;
 }
