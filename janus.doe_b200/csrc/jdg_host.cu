@@ -12,6 +12,7 @@
 
 #include "jdg_engine.h"
 #include "jdg_hb1.cuh"
+#include "jdg_qmma.cuh"
 
 using namespace jdg;
 
@@ -53,6 +54,7 @@ struct HostPriv {
     int *alive_list[JD_MAX_LAYERS] = {};    // alive expert ids, ascending
     int gu_ctas = 0, lm_ctas = 0;           // persistent grids: resident CTAs on all SMs
     float *votes = nullptr, *tall = nullptr;
+    uint8_t *xprep = nullptr;               // batched Q4_K GEMM: activations as fp16 hi/lo tiles
 };
 
 HostPriv *priv(jdg_engine *e) { return (HostPriv *)e->host_priv; }
@@ -358,6 +360,10 @@ static int host_upload_impl(jdg_engine *e, const jd_host_model *h, int max_batch
     e->kv_bstride = (long)L * max_seq * e->kd;
     DALLOC(e->kc, (size_t)B * e->kv_bstride * 4);
     DALLOC(e->vc, (size_t)B * e->kv_bstride * 4);
+    if (max_batch > 1) {
+        const int kmax = std::max(D, std::max(e->qd, e->hidden));
+        if (kmax % 256 == 0) DALLOC(hp->xprep, (size_t)(kmax / 256) * kQmBBytes);
+    }
     DALLOC(hp->votes, kMaxE * 4);
     DALLOC(hp->tall, (size_t)kMaxE * R * 4);
     DALLOC(e->amax_v, 1024 * 4);
@@ -419,6 +425,24 @@ static void launch_q(jdg_engine *e, const QW &w, const float *X, int ldx, int M,
         case JD_Q4_K: k_qgemv<12, EPI><<<grid, 256, sm, e->st>>>(a); break;
         default: k_qgemv<0, EPI><<<grid, 256, sm, e->st>>>(a); break;
         }
+    } else if (w.dt == JD_Q4_K && w.cols % 256 == 0 && priv(e) && priv(e)->xprep) {
+        // tensor cores (tcgen05): 32 tokens per launch
+        for (int t0 = 0; t0 < M; t0 += kQmTok) {
+            const int mt = std::min(kQmTok, M - t0);
+            k_qm_prep_x<<<w.cols / 256, 256, 0, e->st>>>(X + (size_t)t0 * ldx, ldx, mt, w.cols, priv(e)->xprep);
+            QmArgs q = {};
+            q.w = w;
+            q.xprep = priv(e)->xprep;
+            q.M = mt;
+            q.C = C + (size_t)t0 * ldc;
+            q.ldc = ldc;
+            q.epi = EPI;
+            q.alpha = alpha;
+            q.err = e->err;
+            k_qm_q4k<<<(w.rows + kQmRows - 1) / kQmRows, kQmThreads, kQmSmem, e->st>>>(q);
+            e->launches += 2;
+        }
+        return;
     } else {
         QGemmArgs a{w, X, ldx, M, C, ldc, alpha};
         dim3 grid((w.rows + 63) / 64, (M + 31) / 32);
@@ -456,6 +480,10 @@ int jdg_host_set_attrs(jdg_engine *e) {
     SETA((k_hb1_wo<12, 16, 128>));
 #undef SETA_Q
 #undef SETA
+    if (cudaFuncSetAttribute(k_qm_q4k, cudaFuncAttributeMaxDynamicSharedMemorySize, kQmSmem) != cudaSuccess) {
+        jdg_set_err(e->ctx, "cannot reserve %d bytes of shared memory for the tensor-core GEMM", kQmSmem);
+        return JD_ECUDA;
+    }
     return JD_OK;
 }
 
