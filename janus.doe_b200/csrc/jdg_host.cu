@@ -53,8 +53,11 @@ struct HostPriv {
     bool hb1 = false;                       // shapes and dtypes fit the chain
     int *alive_list[JD_MAX_LAYERS] = {};    // alive expert ids, ascending
     int gu_ctas = 0, lm_ctas = 0;           // persistent grids: resident CTAs on all SMs
+    int n_sm = 148;
     float *votes = nullptr, *tall = nullptr;
     uint8_t *xprep = nullptr;               // batched Q4_K GEMM: activations as fp16 hi/lo tiles
+    float *qm_part = nullptr;               // split-K partials
+    unsigned *qm_tickets = nullptr;         // split-K row-tile tickets
 };
 
 HostPriv *priv(jdg_engine *e) { return (HostPriv *)e->host_priv; }
@@ -360,9 +363,20 @@ static int host_upload_impl(jdg_engine *e, const jd_host_model *h, int max_batch
     e->kv_bstride = (long)L * max_seq * e->kd;
     DALLOC(e->kc, (size_t)B * e->kv_bstride * 4);
     DALLOC(e->vc, (size_t)B * e->kv_bstride * 4);
+    {
+        int dev = 0;
+        CK(cudaGetDevice(&dev));
+        CK(cudaDeviceGetAttribute(&hp->n_sm, cudaDevAttrMultiProcessorCount, dev));
+    }
     if (max_batch > 1) {
         const int kmax = std::max(D, std::max(e->qd, e->hidden));
-        if (kmax % 256 == 0) DALLOC(hp->xprep, (size_t)(kmax / 256) * kQmBBytes);
+        if (kmax % 256 == 0) {
+            DALLOC(hp->xprep, (size_t)(kmax / 256) * kQmBBytes);
+            // split K only for matrices with fewer row tiles than SMs: rows < 148 * 128
+            DALLOC(hp->qm_part, (size_t)kQmMaxSplit * kQmTok * 160 * kQmRows * 4);
+            DALLOC(hp->qm_tickets, 1024 * 4);
+            CK(cudaMemset(hp->qm_tickets, 0, 1024 * 4));
+        }
     }
     DALLOC(hp->votes, kMaxE * 4);
     DALLOC(hp->tall, (size_t)kMaxE * R * 4);
@@ -439,7 +453,15 @@ static void launch_q(jdg_engine *e, const QW &w, const float *X, int ldx, int M,
             q.epi = EPI;
             q.alpha = alpha;
             q.err = e->err;
-            k_qm_q4k<<<(w.rows + kQmRows - 1) / kQmRows, kQmThreads, kQmSmem, e->st>>>(q);
+            // split K across CTAs of a row tile until the tiles fill the SMs once (each split
+            // keeps at least two superblocks)
+            const int tiles = (w.rows + kQmRows - 1) / kQmRows, nsb = w.cols / 256;
+            int ks = 1;
+            if (tiles < priv(e)->n_sm) ks = std::max(1, std::min(std::min(priv(e)->n_sm / tiles, nsb / 2), kQmMaxSplit));
+            q.ksplit = ks;
+            q.part = priv(e)->qm_part;
+            q.tickets = priv(e)->qm_tickets;
+            k_qm_q4k<<<dim3(tiles, ks), kQmThreads, kQmSmem, e->st>>>(q);
             e->launches += 2;
         }
         return;

@@ -61,6 +61,7 @@ constexpr int kQmTok = 32;              // tokens (B rows 0..31 hi, 32..63 lo)
 constexpr int kQmN = 2 * kQmTok;        // MMA N
 constexpr int kQmStages = 2;            // smem stages (one superblock each)
 constexpr int kQmRegions = 4;           // TMEM regions (128 columns: 64 main + 64 min)
+constexpr int kQmMaxSplit = 8;          // split-K ways at most
 constexpr int kQmProd = 8;                      // producer warps
 constexpr int kQmRowsPerProd = kQmRows / kQmProd;  // 16
 constexpr int kQmPasses = kQmRowsPerProd / 4;      // 8 rows x 4 pieces per pass
@@ -125,6 +126,11 @@ struct QmArgs {
     int epi;               // EPI_STORE, EPI_ADD (C += alpha * Y), EPI_SWIGLU (C[t][n/2] = silu(Y[2i]) * Y[2i+1])
     float alpha;
     int *err;
+    // split-K: grid.y = ksplit CTAs share a row tile; partials [ksplit][32][rows] in `part`,
+    // the last CTA of the tile (ticket) adds them in split order and applies the epilogue
+    int ksplit;
+    float *part;
+    unsigned *tickets;
 };
 
 // X [M][K] f32 -> prepared B superblocks: fp16 hi/lo of x (rows 0..31 / 32..63, zero for
@@ -242,7 +248,27 @@ __device__ __forceinline__ void qm_store_codes(uint8_t *A, int row, int k_lo, in
     *reinterpret_cast<uint4 *>(A + ((size_t)((c1 + 1) * G + g) * 8 + r0) * 16) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
 }
 
-// grid (rows/128), block 288, dynamic smem kQmSmem.  One TMEM allocation of 512 columns.
+// Output of one row n for the first a.M tokens (all lanes of the warp call it).
+__device__ __forceinline__ void qm_epilogue(const QmArgs &a, const float (&acc)[kQmTok], int n, int lane) {
+    if (a.epi == EPI_SWIGLU) {
+        // rows 2i (gate) and 2i+1 (up) sit in adjacent lanes
+#pragma unroll
+        for (int t = 0; t < kQmTok; t++) {
+            const float other = __shfl_xor_sync(JDG_FULL, acc[t], 1);
+            if (!(lane & 1) && t < a.M && n + 1 < a.w.rows) a.C[(size_t)t * a.ldc + n / 2] = __fmul_rn(silu_ref(acc[t]), other);
+        }
+    } else if (n < a.w.rows) {
+#pragma unroll
+        for (int t = 0; t < kQmTok; t++) {
+            if (t >= a.M) break;
+            float *cp = a.C + (size_t)t * a.ldc + n;
+            if (a.epi == EPI_ADD) *cp = __fadd_rn(*cp, __fmul_rn(acc[t], a.alpha));
+            else *cp = acc[t];
+        }
+    }
+}
+
+// grid (rows/128, ksplit), block, dynamic smem kQmSmem.  One TMEM allocation of 512 columns.
 static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a) {
     extern __shared__ __align__(1024) uint8_t qsm[];
     uint64_t *full_a = reinterpret_cast<uint64_t *>(qsm);        // [S] producers done (128 arrivals)
@@ -255,6 +281,8 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a) {
     uint8_t *stages = qsm + 1024;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = a.w.cols, nsb = K / 256, n0 = blockIdx.x * kQmRows;
+    const int ks = a.ksplit > 1 ? a.ksplit : 1, kz = blockIdx.y, sb0 = (int)((long long)kz * nsb / ks);
+    const int nloc = (int)((long long)(kz + 1) * nsb / ks) - sb0;  // superblocks of this CTA
     if (tid == 0) {
         for (int s = 0; s < kQmStages; s++) {
             mbar_init(&full_a[s], kQmProd * 32);
@@ -288,28 +316,29 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a) {
         // one whole 128-byte core matrix (no bank conflicts).
         // raw loads of superblock sb+1 are issued before superblock sb is dequantised
         // (register double buffer), so the DRAM latency overlaps the conversion
-        auto load_sb = [&](int sb, uint4 (&qv)[kQmPasses], uint4 (&hv)[kQmPasses / 2]) {
+        auto load_sb = [&](int i, uint4 (&qv)[kQmPasses], uint4 (&hv)[kQmPasses / 2]) {
+            const int sb = sb0 + i;
 #pragma unroll
             for (int pass = 0; pass < kQmPasses; pass++) {
                 const int n = n0 + warp * kQmRowsPerProd + (pass >> 1) * 8 + (lane & 7), sub = (lane >> 3) + 4 * (pass & 1);
                 qv[pass] = make_uint4(0, 0, 0, 0);
-                if (sb < nsb && n < a.w.rows) qv[pass] = ld_stream_u4(a.w.q + (size_t)n * (K / 2) + (size_t)sb * 128 + sub * 16);
+                if (i < nloc && n < a.w.rows) qv[pass] = ld_stream_u4(a.w.q + (size_t)n * (K / 2) + (size_t)sb * 128 + sub * 16);
                 if (!(pass & 1)) {
                     hv[pass >> 1] = make_uint4(0, 0, 0, 0);
-                    if (sb < nsb && n < a.w.rows) hv[pass >> 1] = ld_nc_u4(a.w.s + ((size_t)n * nsb + sb) * 16);
+                    if (i < nloc && n < a.w.rows) hv[pass >> 1] = ld_nc_u4(a.w.s + ((size_t)n * nsb + sb) * 16);
                 }
             }
         };
-        auto produce = [&](int sb, const uint4 (&qv)[kQmPasses], const uint4 (&hv)[kQmPasses / 2]) -> bool {
-            const int s = sb % kQmStages;
-            if (sb >= kQmStages && !mbar_wait(&empty[s], (uint32_t)((sb / kQmStages) - 1) & 1u)) *abort_flag = 1;
+        auto produce = [&](int i, const uint4 (&qv)[kQmPasses], const uint4 (&hv)[kQmPasses / 2]) -> bool {
+            const int s = i % kQmStages;
+            if (i >= kQmStages && !mbar_wait(&empty[s], (uint32_t)((i / kQmStages) - 1) & 1u)) *abort_flag = 1;
             if (*abort_flag) return false;
             uint8_t *st = stages + (size_t)s * kQmStageBytes;
             uint8_t *Am = st, *An = st + kQmAMain, *Bm = An + kQmAMin;
             if (tid == 0) {
                 mbar_expect_tx(&full_b[s], kQmBBytes);
-                bulk_g2s(Bm, a.xprep + (size_t)sb * kQmBBytes, kQmBBytes, &full_b[s]);
-                issued_b = sb + 1;
+                bulk_g2s(Bm, a.xprep + (size_t)(sb0 + i) * kQmBBytes, kQmBBytes, &full_b[s]);
+                issued_b = i + 1;
             }
 #pragma unroll
             for (int pass = 0; pass < kQmPasses; pass++) {
@@ -342,22 +371,22 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a) {
         };
         uint4 qa[kQmPasses], ha[kQmPasses / 2], qb[kQmPasses], hb[kQmPasses / 2];
         load_sb(0, qa, ha);
-        for (int sb = 0; sb < nsb; sb += 2) {
-            load_sb(sb + 1, qb, hb);
-            if (!produce(sb, qa, ha)) break;
-            if (sb + 1 >= nsb) break;
-            load_sb(sb + 2, qa, ha);
-            if (!produce(sb + 1, qb, hb)) break;
+        for (int i = 0; i < nloc; i += 2) {
+            load_sb(i + 1, qb, hb);
+            if (!produce(i, qa, ha)) break;
+            if (i + 1 >= nloc) break;
+            load_sb(i + 2, qa, ha);
+            if (!produce(i + 1, qb, hb)) break;
         }
     } else if (warp == kQmMmaWarp) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             constexpr int GA = kQmRows / 8, GB = kQmN / 8;
-            for (int sb = 0; sb < nsb; sb++) {
-                const int s = sb % kQmStages, q = sb % kQmRegions;
-                const uint32_t ph = (uint32_t)(sb / kQmStages) & 1u;
+            for (int i = 0; i < nloc; i++) {
+                const int s = i % kQmStages, q = i % kQmRegions;
+                const uint32_t ph = (uint32_t)(i / kQmStages) & 1u;
                 bool ok = mbar_wait(&full_a[s], ph) && mbar_wait(&full_b[s], ph);
-                if (ok && sb >= kQmRegions) ok = mbar_wait(&tfree[q], (uint32_t)((sb / kQmRegions) - 1) & 1u);
+                if (ok && i >= kQmRegions) ok = mbar_wait(&tfree[q], (uint32_t)((i / kQmRegions) - 1) & 1u);
                 if (!ok || *abort_flag) {
                     *abort_flag = 1;
                     break;
@@ -372,7 +401,7 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a) {
                 qm_mma(dmin, qm_desc(an, GA * 128, 128), qm_desc(bn, GB * 128, 128), 0);
                 qm_commit(&empty[s]);
                 qm_commit(&ready[q]);
-                issued_mma = sb + 1;
+                issued_mma = i + 1;
             }
         }
         __syncwarp();
@@ -382,9 +411,9 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a) {
         float acc[kQmTok];
 #pragma unroll
         for (int t = 0; t < kQmTok; t++) acc[t] = 0.f;
-        for (int sb = 0; sb < nsb; sb++) {
-            const int q = sb % kQmRegions;
-            const bool ok = mbar_wait(&ready[q], (uint32_t)(sb / kQmRegions) & 1u);
+        for (int i = 0; i < nloc; i++) {
+            const int q = i % kQmRegions, sb = sb0 + i;
+            const bool ok = mbar_wait(&ready[q], (uint32_t)(i / kQmRegions) & 1u);
             if (!ok) *abort_flag = 1;
             // the TMEM loads below are warp-collective: leave the loop as a whole warp
             if (__any_sync(JDG_FULL, !ok || *abort_flag)) break;
@@ -411,26 +440,48 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a) {
             for (int t = 0; t < kQmTok; t++) acc[t] = fmaf(-dmin, mh[t] + ml[t], acc[t]);
         }
         if (!__any_sync(JDG_FULL, *abort_flag)) {
-            if (a.epi == EPI_SWIGLU) {
-                // rows 2i (gate) and 2i+1 (up) sit in adjacent lanes
-#pragma unroll
-                for (int t = 0; t < kQmTok; t++) {
-                    const float other = __shfl_xor_sync(JDG_FULL, acc[t], 1);
-                    if (!(lane & 1) && t < a.M && n + 1 < a.w.rows)
-                        a.C[(size_t)t * a.ldc + n / 2] = __fmul_rn(silu_ref(acc[t]), other);
-                }
+            if (ks == 1) {
+                qm_epilogue(a, acc, n, lane);
             } else if (n < a.w.rows) {
 #pragma unroll
                 for (int t = 0; t < kQmTok; t++) {
                     if (t >= a.M) break;
-                    float *cp = a.C + (size_t)t * a.ldc + n;
-                    if (a.epi == EPI_ADD) *cp = __fadd_rn(*cp, __fmul_rn(acc[t], a.alpha));
-                    else *cp = acc[t];
+                    a.part[((size_t)kz * kQmTok + t) * a.w.rows + n] = acc[t];
                 }
             }
         }
     }
     __syncthreads();
+    if (ks > 1 && !*abort_flag) {
+        // the last CTA of this row tile adds the partials in split order
+        __shared__ unsigned s_last;
+        if (tid == 0) {
+            __threadfence();
+            const unsigned t = atomicAdd(a.tickets + blockIdx.x, 1u);
+            s_last = t == (unsigned)ks - 1;
+            if (s_last) {
+                __threadfence();
+                a.tickets[blockIdx.x] = 0;
+            }
+        }
+        __syncthreads();
+        if (s_last && warp > kQmMmaWarp) {
+            const int row = (warp & 3) * 32 + lane, n = n0 + row;
+            float acc[kQmTok];
+#pragma unroll
+            for (int t = 0; t < kQmTok; t++) acc[t] = 0.f;
+            // split by split, all tokens' loads in flight at once (ks round trips in total)
+            for (int z = 0; z < ks; z++) {
+                float v[kQmTok];
+#pragma unroll
+                for (int t = 0; t < kQmTok; t++)
+                    v[t] = (t < a.M && n < a.w.rows) ? __ldcg(a.part + ((size_t)z * kQmTok + t) * a.w.rows + n) : 0.f;
+#pragma unroll
+                for (int t = 0; t < kQmTok; t++) acc[t] += v[t];
+            }
+            qm_epilogue(a, acc, n, lane);
+        }
+    }
     if (*abort_flag) {
         if (tid == 0) atomicOr(a.err, JDG_ERR_TIMEOUT);
         // let the issued MMAs and copies land before the memory goes away
