@@ -775,6 +775,21 @@ extern "C" int jdg_qmatvec(jdg_ctx *ctx, float *out, const void *W, int dt, cons
     QW w;
     float *dx = nullptr, *dy = nullptr;
     rc = upload_packed(e, p, w);
+    if (rc == JD_OK && dt == JD_Q4_K && B > 1) {
+        // batched Q4_K products run on the tensor cores, as in the engine
+        e->host_priv = new (std::nothrow) HostPriv();
+        HostPriv *hp = priv(e);
+        if (!hp) rc = JD_ENOMEM;
+        if (rc == JD_OK) {
+            int dev = 0;
+            cudaGetDevice(&dev);
+            cudaDeviceGetAttribute(&hp->n_sm, cudaDevAttrMultiProcessorCount, dev);
+            rc = dalloc(e, (void **)&hp->xprep, (size_t)(c / 256) * kQmBBytes);
+        }
+        if (rc == JD_OK) rc = dalloc(e, (void **)&hp->qm_part, (size_t)kQmMaxSplit * kQmTok * 160 * kQmRows * 4);
+        if (rc == JD_OK) rc = dalloc(e, (void **)&hp->qm_tickets, 1024 * 4);
+        if (rc == JD_OK && cudaMemset(hp->qm_tickets, 0, 1024 * 4) != cudaSuccess) rc = JD_ECUDA;
+    }
     if (rc == JD_OK) rc = dalloc(e, (void **)&dx, (size_t)B * c * 4);
     if (rc == JD_OK) rc = dalloc(e, (void **)&dy, (size_t)B * r * 4);
     if (rc == JD_OK) rc = jdg_host_set_attrs(e);

@@ -14,14 +14,17 @@
 //     A_min.B_min (K = 16, one MMA); the epilogue adds d_sb * (hi + lo) - dmin_sb * (hi + lo)
 //     of the two into f32 registers.  d and dmin stay f32 outside the tensor core.
 //
-// CTA = 128 weight rows x all K, 13 warps:
-//   warps 0-7   producers: dequantise the packed rows of a superblock into the fp16 A tile
-//               (core-matrix layout, no swizzle) and bulk-copy the prepared B tile
+// CTA = 128 weight rows x all K (or a split of K), 13 warps, 4 smem stages of half a
+// superblock:
+//   warps 0-7   producers: dequantise the packed rows of half a superblock into the fp16 A
+//               tile (core-matrix layout, no swizzle) and bulk-copy the prepared B tile
 //   warp 8      MMA issuer: one thread issues tcgen05.mma, commits to mbarriers
 //   warps 9-12  epilogue: tcgen05.ld of a region, scale, accumulate; then the output
 // Every mbarrier wait is bounded; on a timeout the CTA records JDG_ERR_TIMEOUT, waits
 // (bounded) for the copies and MMAs it issued, frees its tensor memory and returns.
 #pragma once
+#include <type_traits>
+
 #include "jdg_hb1.cuh"
 
 namespace jdg {
@@ -59,21 +62,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
 constexpr int kQmRows = 128;            // weight rows per CTA (MMA M)
 constexpr int kQmTok = 32;              // tokens (B rows 0..31 hi, 32..63 lo)
 constexpr int kQmN = 2 * kQmTok;        // MMA N
-constexpr int kQmStages = 2;            // smem stages (one superblock each)
+constexpr int kQmStages = 4;            // smem stages, half a superblock (128 K) each
 constexpr int kQmRegions = 4;           // TMEM regions (128 columns: 64 main + 64 min)
 constexpr int kQmMaxSplit = 8;          // split-K ways at most
 constexpr int kQmProd = 8;                      // producer warps
-constexpr int kQmRowsPerProd = kQmRows / kQmProd;  // 16
-constexpr int kQmPasses = kQmRowsPerProd / 4;      // 8 rows x 4 pieces per pass
+constexpr int kQmRowsPerProd = kQmRows / kQmProd;  // 16: two groups of 8 rows
 constexpr int kQmMmaWarp = kQmProd;
 constexpr int kQmThreads = (kQmProd + 5) * 32;
-// per stage: A main 128x256 fp16, A min 128x16, B main 64x256, B min 64x16
-constexpr int kQmAMain = kQmRows * 256 * 2;           // 65536
-constexpr int kQmAMin = kQmRows * 16 * 2;             // 4096
+// prepared B per superblock in global memory: main 64 x 256 fp16, min 64 x 16
 constexpr int kQmBMain = kQmN * 256 * 2;              // 32768
 constexpr int kQmBMin = kQmN * 16 * 2;                // 2048
-constexpr int kQmBBytes = kQmBMain + kQmBMin;         // one prepared B superblock in global memory
-constexpr int kQmStageBytes = kQmAMain + kQmAMin + kQmBBytes;
+constexpr int kQmBBytes = kQmBMain + kQmBMin;
+constexpr int kQmBHalf = kQmBMain / 2;                // the B main half a stage holds
+// per stage: A main 128 x 128 fp16, A min 128 x 16, B main half 64 x 128, B min 64 x 16
+constexpr int kQmAMain = kQmRows * 128 * 2;           // 32768
+constexpr int kQmAMin = kQmRows * 16 * 2;             // 4096
+constexpr int kQmStageBytes = kQmAMain + kQmAMin + kQmBHalf + kQmBMin;  // 55296
 constexpr int kQmSmem = 1024 + kQmStages * kQmStageBytes;
 
 // Core-matrix layout (K-major, no swizzle): 8 rows x 8 fp16 (16 bytes per row) = 128 bytes
@@ -131,6 +135,11 @@ struct QmArgs {
     int ksplit;
     float *part;
     unsigned *tickets;
+    // optional timeline of CTA (0,0) for tuning (%globaltimer ns): [0] entry, [1] exit,
+    // [2 + 3i] producers done with superblock i, [3 + 3i] its MMAs issued, [4 + 3i] its
+    // epilogue done, [194 + 2i] its B tile landed, [195 + 2i] its A tile complete (i < 64);
+    // 322 entries
+    unsigned long long *tl;
 };
 
 // X [M][K] f32 -> prepared B superblocks: fp16 hi/lo of x (rows 0..31 / 32..63, zero for
@@ -268,21 +277,33 @@ __device__ __forceinline__ void qm_epilogue(const QmArgs &a, const float (&acc)[
     }
 }
 
-// grid (rows/128, ksplit), block, dynamic smem kQmSmem.  One TMEM allocation of 512 columns.
+// grid (rows/128, ksplit), block kQmThreads, dynamic smem kQmSmem.  One TMEM allocation of
+// 512 columns.  Stage j holds half h = j % 2 of superblock i = j / 2 (K range 128h..128h+127);
+// superblock i accumulates in TMEM region i % 4 over its two stages.
 static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a) {
     extern __shared__ __align__(1024) uint8_t qsm[];
-    uint64_t *full_a = reinterpret_cast<uint64_t *>(qsm);        // [S] producers done (128 arrivals)
-    uint64_t *full_b = full_a + kQmStages;                         // [S] B bulk copy landed
+    uint64_t *full_a = reinterpret_cast<uint64_t *>(qsm);        // [S] producers done (256 arrivals)
+    uint64_t *full_b = full_a + kQmStages;                         // [S] B bulk copies landed
     uint64_t *empty = full_b + kQmStages;                          // [S] MMAs of the stage done
     uint64_t *ready = empty + kQmStages;                           // [R] region complete
     uint64_t *tfree = ready + kQmRegions;                          // [R] epilogue read the region (128 arrivals)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tfree + kQmRegions);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
     uint8_t *stages = qsm + 1024;
+    const bool tl_on = a.tl && blockIdx.x == 0 && blockIdx.y == 0;
+    auto tl_mark = [&](int slot) {
+        if (tl_on && slot < 2 + 5 * 64) {
+            unsigned long long t;
+            asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+            a.tl[slot] = t;
+        }
+    };
+    if (threadIdx.x == 0) tl_mark(0);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = a.w.cols, nsb = K / 256, n0 = blockIdx.x * kQmRows;
     const int ks = a.ksplit > 1 ? a.ksplit : 1, kz = blockIdx.y, sb0 = (int)((long long)kz * nsb / ks);
     const int nloc = (int)((long long)(kz + 1) * nsb / ks) - sb0;  // superblocks of this CTA
+    const int nst = 2 * nloc;                                       // stages of this CTA
     if (tid == 0) {
         for (int s = 0; s < kQmStages; s++) {
             mbar_init(&full_a[s], kQmProd * 32);
@@ -305,56 +326,65 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a) {
     __syncthreads();
     qm_fence_after();
     const uint32_t tmem = *tmem_slot;
-    int issued_mma = 0;  // superblocks whose MMAs warp 4 issued (lane 0 of warp 4)
-    int issued_b = 0;    // B copies issued (thread 0)
+    int issued_mma = 0;  // stages whose MMAs were issued (lane 0 of the MMA warp)
+    int issued_b = 0;    // stages whose B copies were issued (thread 0)
 
     if (warp < kQmProd) {
         // ---------------- producers ----------------
-        // warp w owns rows 32w..32w+31 (4 groups of 8).  Per superblock a row has 128 code
-        // bytes = 8 pieces of 16.  Pass p covers row group p/2 and pieces 4*(p%2)..+3: lane
-        // l takes row 8*(p/2) + l%8 and piece l/8 + 4*(p%2), so the 8 lanes of a piece store
-        // one whole 128-byte core matrix (no bank conflicts).
-        // raw loads of superblock sb+1 are issued before superblock sb is dequantised
-        // (register double buffer), so the DRAM latency overlaps the conversion
-        auto load_sb = [&](int i, uint4 (&qv)[kQmPasses], uint4 (&hv)[kQmPasses / 2]) {
-            const int sb = sb0 + i;
+        // warp w owns rows 16w..16w+15 (2 groups of 8).  A row's half superblock is 64 code
+        // bytes = 4 pieces of 16.  Pass p covers row group p: lane l takes row 8p + l%8 and
+        // piece l/8, so the 8 lanes of a piece store one whole 128-byte core matrix (no bank
+        // conflicts).  Raw loads run three stages ahead in a ring of register buffers.
+        auto load_st = [&](int j, uint4 (&qv)[2], uint4 (&hv)[2]) {
+            const int sb = sb0 + (j >> 1), piece = 4 * (j & 1) + (lane >> 3);
 #pragma unroll
-            for (int pass = 0; pass < kQmPasses; pass++) {
-                const int n = n0 + warp * kQmRowsPerProd + (pass >> 1) * 8 + (lane & 7), sub = (lane >> 3) + 4 * (pass & 1);
+            for (int pass = 0; pass < 2; pass++) {
+                const int n = n0 + warp * kQmRowsPerProd + pass * 8 + (lane & 7);
                 qv[pass] = make_uint4(0, 0, 0, 0);
-                if (i < nloc && n < a.w.rows) qv[pass] = ld_stream_u4(a.w.q + (size_t)n * (K / 2) + (size_t)sb * 128 + sub * 16);
-                if (!(pass & 1)) {
-                    hv[pass >> 1] = make_uint4(0, 0, 0, 0);
-                    if (i < nloc && n < a.w.rows) hv[pass >> 1] = ld_nc_u4(a.w.s + ((size_t)n * nsb + sb) * 16);
+                hv[pass] = make_uint4(0, 0, 0, 0);
+                if (j < nst && n < a.w.rows) {
+                    qv[pass] = ld_stream_u4(a.w.q + (size_t)n * (K / 2) + (size_t)sb * 128 + piece * 16);
+                    hv[pass] = ld_nc_u4(a.w.s + ((size_t)n * nsb + sb) * 16);
                 }
             }
         };
-        auto produce = [&](int i, const uint4 (&qv)[kQmPasses], const uint4 (&hv)[kQmPasses / 2]) -> bool {
-            const int s = i % kQmStages;
-            if (i >= kQmStages && !mbar_wait(&empty[s], (uint32_t)((i / kQmStages) - 1) & 1u)) *abort_flag = 1;
+        // H (the half, j % 2) is a compile-time constant: the scale bytes a lane needs then sit
+        // at fixed header positions, two candidates per lane chosen by lane / 16
+        auto produce = [&](int j, const uint4 (&qv)[2], const uint4 (&hv)[2], auto h_tag) -> bool {
+            constexpr int h = decltype(h_tag)::value;
+            const int s = j % kQmStages, sb = sb0 + (j >> 1);
+            if (j >= kQmStages && !mbar_wait(&empty[s], (uint32_t)((j / kQmStages) - 1) & 1u)) *abort_flag = 1;
             if (*abort_flag) return false;
+            if (tid == 0 && h == 1 && (j >> 1) < 64) tl_mark(2 + 3 * 64 + 2 * (j >> 1));  // producer starts half 1
             uint8_t *st = stages + (size_t)s * kQmStageBytes;
-            uint8_t *Am = st, *An = st + kQmAMain, *Bm = An + kQmAMin;
+            uint8_t *Am = st, *An = st + kQmAMain, *Bm = An + kQmAMin, *Bn = Bm + kQmBHalf;
             if (tid == 0) {
-                mbar_expect_tx(&full_b[s], kQmBBytes);
-                bulk_g2s(Bm, a.xprep + (size_t)(sb0 + i) * kQmBBytes, kQmBBytes, &full_b[s]);
-                issued_b = i + 1;
+                const uint8_t *src = a.xprep + (size_t)sb * kQmBBytes;
+                mbar_expect_tx(&full_b[s], kQmBHalf + (h == 0 ? kQmBMin : 0));
+                bulk_g2s(Bm, src + (size_t)h * kQmBHalf, kQmBHalf, &full_b[s]);
+                if (h == 0) bulk_g2s(Bn, src + kQmBMain, kQmBMin, &full_b[s]);
+                issued_b = j + 1;
             }
 #pragma unroll
-            for (int pass = 0; pass < kQmPasses; pass++) {
-                const int row = warp * kQmRowsPerProd + (pass >> 1) * 8 + (lane & 7), sub = (lane >> 3) + 4 * (pass & 1);
-                const int c = sub >> 1, l0 = (sub & 1) * 16;
-                int s0, m0, s1, m1;
-                smk4_reg(2 * c, hv[pass >> 1], s0, m0);
-                smk4_reg(2 * c + 1, hv[pass >> 1], s1, m1);
-                qm_store_codes(Am, row, 64 * c + l0, 64 * c + 32 + l0, qv[pass], s0, s1);
-                if (sub == 0) {
+            for (int pass = 0; pass < 2; pass++) {
+                const int row = warp * kQmRowsPerProd + pass * 8 + (lane & 7), piece = 4 * h + (lane >> 3);
+                const int c = piece >> 1, l0 = (piece & 1) * 16;
+                // sub-blocks 2c and 2c+1 with c = 2h + lane/16
+                int sa, sbb, sc_, sd, mm;
+                smk4_reg(4 * h, hv[pass], sa, mm);
+                smk4_reg(4 * h + 1, hv[pass], sbb, mm);
+                smk4_reg(4 * h + 2, hv[pass], sc_, mm);
+                smk4_reg(4 * h + 3, hv[pass], sd, mm);
+                const bool hiC = (lane >> 4) & 1;
+                const int s0 = hiC ? sc_ : sa, s1 = hiC ? sd : sbb;
+                qm_store_codes(Am, row, 64 * c + l0 - 128 * h, 64 * c + 32 + l0 - 128 * h, qv[pass], s0, s1);
+                if (h == 0 && (lane >> 3) == 0) {
                     // A_min row: m_0..m_7 in K columns 0..7, zeros in 8..15
                     int mj[8];
 #pragma unroll
-                    for (int j = 0; j < 8; j++) {
+                    for (int jj = 0; jj < 8; jj++) {
                         int sj;
-                        smk4_reg(j, hv[pass >> 1], sj, mj[j]);
+                        smk4_reg(jj, hv[pass], sj, mj[jj]);
                     }
                     constexpr int G = kQmRows / 8;
                     const int g = row >> 3, r0 = row & 7;
@@ -367,52 +397,80 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a) {
             // generic-proxy stores must be visible to the tensor core (async proxy)
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_arrive(&full_a[s]);
+            if (tid == 0 && h == 1) tl_mark(2 + 3 * (j >> 1));
             return true;
         };
-        uint4 qa[kQmPasses], ha[kQmPasses / 2], qb[kQmPasses], hb[kQmPasses / 2];
-        load_sb(0, qa, ha);
-        for (int i = 0; i < nloc; i += 2) {
-            load_sb(i + 1, qb, hb);
-            if (!produce(i, qa, ha)) break;
-            if (i + 1 >= nloc) break;
-            load_sb(i + 2, qa, ha);
-            if (!produce(i + 1, qb, hb)) break;
+        uint4 qa[2], ha[2], qb[2], hb[2], qc[2], hc[2], qd[2], hd[2];
+        // weights do not depend on the previous kernel: the first stages load before the
+        // dependency wait (Programmatic Dependent Launch)
+        load_st(0, qa, ha);
+        load_st(1, qb, hb);
+        load_st(2, qc, hc);
+        pdl_wait();
+        pdl_trigger();
+        using H0 = std::integral_constant<int, 0>;
+        using H1 = std::integral_constant<int, 1>;
+        for (int j = 0; j < nst; j += 4) {  // nst is even: j, j+2 are first halves
+            load_st(j + 3, qd, hd);
+            if (!produce(j, qa, ha, H0{}) || j + 1 >= nst) break;
+            load_st(j + 4, qa, ha);
+            if (!produce(j + 1, qb, hb, H1{}) || j + 2 >= nst) break;
+            load_st(j + 5, qb, hb);
+            if (!produce(j + 2, qc, hc, H0{}) || j + 3 >= nst) break;
+            load_st(j + 6, qc, hc);
+            if (!produce(j + 3, qd, hd, H1{})) break;
         }
     } else if (warp == kQmMmaWarp) {
         // ---------------- MMA issuer ----------------
+        pdl_trigger();
         if (lane == 0) {
             constexpr int GA = kQmRows / 8, GB = kQmN / 8;
-            for (int i = 0; i < nloc; i++) {
-                const int s = i % kQmStages, q = i % kQmRegions;
-                const uint32_t ph = (uint32_t)(i / kQmStages) & 1u;
-                bool ok = mbar_wait(&full_a[s], ph) && mbar_wait(&full_b[s], ph);
-                if (ok && i >= kQmRegions) ok = mbar_wait(&tfree[q], (uint32_t)((i / kQmRegions) - 1) & 1u);
+            for (int j = 0; j < nst; j++) {
+                const int s = j % kQmStages, h = j & 1, i = j >> 1, q = i % kQmRegions;
+                const uint32_t ph = (uint32_t)(j / kQmStages) & 1u;
+                bool ok = mbar_wait(&full_b[s], ph);
+                ok = ok && mbar_wait(&full_a[s], ph);
+                if (h == 1 && i < 64) tl_mark(2 + 3 * 64 + 2 * i + 1);
+                if (ok && h == 0 && i >= kQmRegions) ok = mbar_wait(&tfree[q], (uint32_t)((i / kQmRegions) - 1) & 1u);
                 if (!ok || *abort_flag) {
                     *abort_flag = 1;
                     break;
                 }
                 qm_fence_after();
                 const uint32_t st = smem_u32(stages + (size_t)s * kQmStageBytes);
-                const uint32_t am = st, an = st + kQmAMain, bm = an + kQmAMin, bn = bm + kQmBMain;
+                const uint32_t am = st, an = st + kQmAMain, bm = an + kQmAMin, bn = bm + kQmBHalf;
                 const uint32_t dmain = tmem + (uint32_t)(q * 128), dmin = dmain + 64;
-                for (int ks = 0; ks < 16; ks++)
-                    qm_mma(dmain, qm_desc(am + ks * 2 * GA * 128, GA * 128, 128), qm_desc(bm + ks * 2 * GB * 128, GB * 128, 128),
-                           ks > 0);
-                qm_mma(dmin, qm_desc(an, GA * 128, 128), qm_desc(bn, GB * 128, 128), 0);
+#pragma unroll
+                for (int k8 = 0; k8 < 8; k8++)
+                    qm_mma(dmain, qm_desc(am + k8 * 2 * GA * 128, GA * 128, 128), qm_desc(bm + k8 * 2 * GB * 128, GB * 128, 128),
+                           (h > 0 || k8 > 0) ? 1u : 0u);
+                if (h == 0) qm_mma(dmin, qm_desc(an, GA * 128, 128), qm_desc(bn, GB * 128, 128), 0);
                 qm_commit(&empty[s]);
-                qm_commit(&ready[q]);
-                issued_mma = i + 1;
+                if (h == 1) qm_commit(&ready[q]);
+                issued_mma = j + 1;
+                if (h == 1) tl_mark(3 + 3 * i);
             }
         }
         __syncwarp();
     } else {
-        // ---------------- epilogue: warps 5..8, TMEM lane quarter warp % 4 ----------------
+        // ---------------- epilogue: warps 9..12, TMEM lane quarter warp % 4 ----------------
         const int quarter = warp & 3, row = quarter * 32 + lane, n = n0 + row;
+        pdl_wait();  // the epilogue reads and writes C
+        pdl_trigger();
         float acc[kQmTok];
 #pragma unroll
         for (int t = 0; t < kQmTok; t++) acc[t] = 0.f;
+        // the superblock scales (d, dmin: the first 4 bytes of each header) are loaded one
+        // superblock ahead, so their latency hides behind the wait for the region
+        auto hdr_word = [&](int i) -> uint32_t {
+            return (i < nloc && n < a.w.rows) ? __ldg(reinterpret_cast<const uint32_t *>(a.w.s + ((size_t)n * nsb + sb0 + i) * 16))
+                                              : 0u;
+        };
+        uint32_t hw_next = hdr_word(0);
         for (int i = 0; i < nloc; i++) {
-            const int q = i % kQmRegions, sb = sb0 + i;
+            const int q = i % kQmRegions;
+            const uint32_t hw = hw_next;
+            hw_next = hdr_word(i + 1);
             const bool ok = mbar_wait(&ready[q], (uint32_t)(i / kQmRegions) & 1u);
             if (!ok) *abort_flag = 1;
             // the TMEM loads below are warp-collective: leave the loop as a whole warp
@@ -420,12 +478,7 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a) {
             qm_fence_after();
             const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(q * 128);
             float mh[32], ml[32];
-            float d = 0.f, dmin = 0.f;
-            if (n < a.w.rows) {
-                const uint32_t hw = *reinterpret_cast<const uint32_t *>(a.w.s + ((size_t)n * nsb + sb) * 16);
-                d = h2f((uint16_t)(hw & 0xFFFF));
-                dmin = h2f((uint16_t)(hw >> 16));
-            }
+            const float d = h2f((uint16_t)(hw & 0xFFFF)), dmin = h2f((uint16_t)(hw >> 16));
             qm_ld32(base, mh);
             qm_ld32(base + 32, ml);
             qm_ld_wait();
@@ -436,6 +489,7 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a) {
             qm_ld_wait();
             qm_fence_before();
             mbar_arrive(&tfree[q]);
+            if (warp == kQmMmaWarp + 1 && lane == 0) tl_mark(4 + 3 * i);
 #pragma unroll
             for (int t = 0; t < kQmTok; t++) acc[t] = fmaf(-dmin, mh[t] + ml[t], acc[t]);
         }
@@ -486,12 +540,12 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a) {
         if (tid == 0) atomicOr(a.err, JDG_ERR_TIMEOUT);
         // let the issued MMAs and copies land before the memory goes away
         if (warp == kQmMmaWarp && lane == 0 && issued_mma > 0) {
-            const int sb = issued_mma - 1;
-            mbar_wait(&ready[sb % kQmRegions], (uint32_t)(sb / kQmRegions) & 1u);
+            const int j = issued_mma - 1;
+            mbar_wait(&empty[j % kQmStages], (uint32_t)(j / kQmStages) & 1u);
         }
         if (tid == 0)
-            for (int sb = max(0, issued_b - kQmStages); sb < issued_b; sb++)
-                mbar_wait(&full_b[sb % kQmStages], (uint32_t)(sb / kQmStages) & 1u);
+            for (int j = max(0, issued_b - kQmStages); j < issued_b; j++)
+                mbar_wait(&full_b[j % kQmStages], (uint32_t)(j / kQmStages) & 1u);
     }
     qm_fence_before();
     __syncthreads();
@@ -499,6 +553,7 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a) {
         qm_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
     }
+    if (threadIdx.x == 0) tl_mark(1);
 }
 
 }  // namespace jdg
