@@ -2,6 +2,7 @@
 // rows losslessly, tensor-parallel sharding), the decode step (gguf_host_forward,
 // janusdoe.c:3160-3322, for a batch of independent sequences), NCCL all-reduce for the
 // tensor-parallel case, and the standalone packed GEMV entry point.
+#include <cudaTypedefs.h>
 #include <nccl.h>
 
 #include <algorithm>
@@ -58,9 +59,62 @@ struct HostPriv {
     uint8_t *xprep = nullptr;               // batched Q4_K GEMM: activations as fp16 hi/lo tiles
     float *qm_part = nullptr;               // split-K partials
     unsigned *qm_tickets = nullptr;         // split-K row-tile tickets
+    std::vector<QmMaps> qm_maps;            // TMA tensor maps of the Q4_K matrices the GEMM reads
 };
 
 HostPriv *priv(jdg_engine *e) { return (HostPriv *)e->host_priv; }
+
+// cuTensorMapEncodeTiled from the driver (through the runtime, no link-time dependency)
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// The two tensor maps k_qm_q4k reads a Q4_K matrix through: the code bytes [rows][cols/2]
+// in boxes of 128 bytes x 128 rows with the 128-byte swizzle, and the 16-byte superblock
+// headers [rows][cols/256 * 16] in boxes of 16 bytes x 128 rows.  Created once per matrix.
+int qm_add_maps(jdg_engine *e, const QW &w) {
+    HostPriv *hp = priv(e);
+    for (const QmMaps &m : hp->qm_maps)
+        if (m.q == w.q) return JD_OK;
+    auto enc = tensor_map_encoder();
+    if (!enc) {
+        jdg_set_err(e->ctx, "cuTensorMapEncodeTiled is not available from the driver");
+        return JD_ECUDA;
+    }
+    QmMaps m;
+    m.q = w.q;
+    const cuuint32_t es[2] = {1, 1};
+    const cuuint64_t gd[2] = {(cuuint64_t)w.cols / 2, (cuuint64_t)w.rows}, gs[1] = {(cuuint64_t)w.cols / 2};
+    const cuuint32_t box[2] = {128, 128};
+    CUresult r = enc(&m.codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(w.q), gd, gs, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const cuuint64_t hd[2] = {(cuuint64_t)(w.cols / 256) * 16, (cuuint64_t)w.rows}, hs[1] = {(cuuint64_t)(w.cols / 256) * 16};
+    const cuuint32_t hbox[2] = {16, 128};
+    if (r == CUDA_SUCCESS)
+        r = enc(&m.hdr, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(w.s), hd, hs, hbox, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        jdg_set_err(e->ctx, "cuTensorMapEncodeTiled failed (%d) for a %d x %d Q4_K matrix", (int)r, w.rows, w.cols);
+        return JD_ECUDA;
+    }
+    hp->qm_maps.push_back(m);
+    return JD_OK;
+}
+const QmMaps *qm_find_maps(jdg_engine *e, const QW &w) {
+    for (const QmMaps &m : priv(e)->qm_maps)
+        if (m.q == w.q) return &m;
+    return nullptr;
+}
 
 int block_elems(int dt) { return dt == JD_Q8_0 ? 32 : dt == JD_Q4_K ? 256 : dt == JD_F32 ? 1 : 0; }
 size_t block_bytes(int dt) { return dt == JD_Q8_0 ? 34 : dt == JD_Q4_K ? 144 : dt == JD_F32 ? 4 : 0; }
@@ -376,6 +430,20 @@ static int host_upload_impl(jdg_engine *e, const jd_host_model *h, int max_batch
             DALLOC(hp->qm_part, (size_t)kQmMaxSplit * kQmTok * 160 * kQmRows * 4);
             DALLOC(hp->qm_tickets, 1024 * 4);
             CK(cudaMemset(hp->qm_tickets, 0, 1024 * 4));
+            // tensor maps of every Q4_K matrix the batched GEMM reads
+            std::vector<const QW *> mats;
+            for (int l = 0; l < L; l++) {
+                mats.push_back(&hp->wqkv[l]);
+                mats.push_back(&hp->wo[l]);
+                mats.push_back(&hp->gu[l]);
+                mats.push_back(&hp->dn[l]);
+            }
+            mats.push_back(&hp->out);
+            for (const QW *w : mats)
+                if (w->dt == JD_Q4_K && w->cols % 256 == 0 && w->rows > 0) {
+                    const int rc = qm_add_maps(e, *w);
+                    if (rc != JD_OK) return rc;
+                }
         }
     }
     DALLOC(hp->votes, kMaxE * 4);
@@ -441,6 +509,13 @@ static void launch_q(jdg_engine *e, const QW &w, const float *X, int ldx, int M,
         }
     } else if (w.dt == JD_Q4_K && w.cols % 256 == 0 && priv(e) && priv(e)->xprep) {
         // tensor cores (tcgen05): 32 tokens per launch
+        const QmMaps *maps = qm_find_maps(e, w);
+        if (!maps) {
+            // the maps are made at upload for every matrix that can come here
+            jdg_set_err(e->ctx, "tensor-core GEMM: no tensor maps for a %d x %d matrix", w.rows, w.cols);
+            cudaMemsetAsync(e->err, 0xFF, sizeof(int), e->st);
+            return;
+        }
         for (int t0 = 0; t0 < M; t0 += kQmTok) {
             const int mt = std::min(kQmTok, M - t0);
             k_qm_prep_x<<<w.cols / 256, 256, 0, e->st>>>(X + (size_t)t0 * ldx, ldx, mt, w.cols, priv(e)->xprep);
@@ -461,7 +536,7 @@ static void launch_q(jdg_engine *e, const QW &w, const float *X, int ldx, int M,
             q.ksplit = ks;
             q.part = priv(e)->qm_part;
             q.tickets = priv(e)->qm_tickets;
-            k_qm_q4k<<<dim3(tiles, ks), kQmThreads, kQmSmem, e->st>>>(q);
+            k_qm_q4k<<<dim3(tiles, ks), kQmThreads, kQmSmem, e->st>>>(q, maps->codes, maps->hdr);
             e->launches += 2;
         }
         return;
@@ -789,6 +864,7 @@ extern "C" int jdg_qmatvec(jdg_ctx *ctx, float *out, const void *W, int dt, cons
         if (rc == JD_OK) rc = dalloc(e, (void **)&hp->qm_part, (size_t)kQmMaxSplit * kQmTok * 160 * kQmRows * 4);
         if (rc == JD_OK) rc = dalloc(e, (void **)&hp->qm_tickets, 1024 * 4);
         if (rc == JD_OK && cudaMemset(hp->qm_tickets, 0, 1024 * 4) != cudaSuccess) rc = JD_ECUDA;
+        if (rc == JD_OK) rc = qm_add_maps(e, w);
     }
     if (rc == JD_OK) rc = dalloc(e, (void **)&dx, (size_t)B * c * 4);
     if (rc == JD_OK) rc = dalloc(e, (void **)&dy, (size_t)B * r * 4);

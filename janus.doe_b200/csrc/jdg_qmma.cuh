@@ -1,28 +1,38 @@
 // jdg_qmma.cuh — batched host GEMM over Q4_K weights on the 5th-generation tensor cores
-// (tcgen05.mma, accumulators in tensor memory), for the host GGUF path at batch > 1.
+// (tcgen05.mma with the A operand in tensor memory), for the host GGUF path at batch > 1.
 //
 //   Y[t][n] (epi)= sum_k X[t][k] * W[n][k],   W in Q4_K (janusdoe.c:2573-2585):
 //   W[n][k] = d_sb * s_j * q - dmin_sb * m_j   (superblock sb of 256 weights, sub-block j of 32)
 //
 // Exact reformulation on fp16 tensor cores with f32 accumulation:
-//   * A = s_j * q is an integer <= 63 * 15 = 945: exact in fp16.  The sub-block minimum
-//     becomes a second product: A_min[n][j] = m_j (integer <= 63), against the sums of x over
-//     each sub-block.
+//   * A = s_j * q is an integer <= 63 * 15 = 945: exact in fp16.
 //   * X is split into x_hi = fp16(x) and x_lo = fp16(x - x_hi); together they carry ~22
 //     mantissa bits.  B stacks them as 64 "columns": tokens 0..31 hi, then 0..31 lo.
-//   * Per superblock one TMEM region receives A.B (K = 256, 16 MMAs of 128x64x16) and
+//   * The sub-block minimum becomes a second product: A_min[n][j] = m_j (integer <= 63),
+//     against the sums of x over each sub-block (hi/lo as well).
+//   * Per superblock one TMEM region receives A.B (K = 256: 16 MMAs of 128x64x16) and
 //     A_min.B_min (K = 16, one MMA); the epilogue adds d_sb * (hi + lo) - dmin_sb * (hi + lo)
 //     of the two into f32 registers.  d and dmin stay f32 outside the tensor core.
 //
-// CTA = 128 weight rows x all K (or a split of K), 13 warps, 4 smem stages of half a
-// superblock:
-//   warps 0-7   producers: dequantise the packed rows of half a superblock into the fp16 A
-//               tile (core-matrix layout, no swizzle) and bulk-copy the prepared B tile
-//   warp 8      MMA issuer: one thread issues tcgen05.mma, commits to mbarriers
-//   warps 9-12  epilogue: tcgen05.ld of a region, scale, accumulate; then the output
+// CTA = 128 weight rows x all K (or a split of K), 23 warps:
+//   warps 0-15   producers: warp w fills TMEM lanes 32(w%4).. (its 32 rows, one per lane) for
+//                the K quarter w/4 of each superblock: it reads the raw codes from shared
+//                memory, forms the fp16 s*q pairs and stores them with tcgen05.st; warps 0-3
+//                also write the A_min rows into shared memory
+//   warps 16-17  MMA issuers (one thread each): warp 16 the even superblocks, warp 17 the odd
+//                ones; their smem stages, A stages and accumulator regions are disjoint, so the
+//                two streams of MMAs need no ordering (one thread issues ~1 MMA per 50 cycles)
+//   warp 18      TMA issuer (one thread): per superblock the code bytes (128 rows x 128 B,
+//                128-byte swizzle), the headers (128 x 16 B) and the prepared B tile (34 KB)
+//   warps 19-22  epilogue (TMEM lane quarter warp % 4)
+// Shared memory: kQmStages stages of one superblock.  TMEM (512 columns): four A stages of
+// half a superblock (64 columns: K 128 as fp16 pairs; warps w/4 = 2h, 2h+1 fill half h) and
+// two accumulator regions of 128 columns (A.B 64, A_min.B_min 64).
 // Every mbarrier wait is bounded; on a timeout the CTA records JDG_ERR_TIMEOUT, waits
 // (bounded) for the copies and MMAs it issued, frees its tensor memory and returns.
 #pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
 #include <type_traits>
 
 #include "jdg_hb1.cuh"
@@ -30,7 +40,7 @@
 namespace jdg {
 
 // ---------------------------------------------------------------------------------
-// mbarriers and 1-D bulk async copies (TMA) into shared memory.  Every wait is bounded.
+// mbarriers and bulk async copies (TMA) into shared memory.  Every wait is bounded.
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
@@ -38,15 +48,33 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
 __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                      smem_u32(dst)),
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
+// tile (x, y) of a 2-D tensor map into shared memory (no multicast)
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
 // Wait for phase `parity` of bar with an iteration limit (try_wait also suspends for a
 // bounded time per call); false when the limit ran out.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    // the non-blocking test first: on a completed phase it costs ~13 cycles, try_wait ~150
+    uint32_t ready;
+    asm volatile("{ .reg .pred p; mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                 : "=r"(ready)
+                 : "r"(smem_u32(bar)), "r"(parity)
+                 : "memory");
+    if (ready) return true;
     for (int it = 0; it < (1 << 20); it++) {
         uint32_t done;
         asm volatile(
@@ -59,26 +87,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
     return false;
 }
 
-constexpr int kQmRows = 128;            // weight rows per CTA (MMA M)
-constexpr int kQmTok = 32;              // tokens (B rows 0..31 hi, 32..63 lo)
-constexpr int kQmN = 2 * kQmTok;        // MMA N
-constexpr int kQmStages = 4;            // smem stages, half a superblock (128 K) each
-constexpr int kQmRegions = 4;           // TMEM regions (128 columns: 64 main + 64 min)
-constexpr int kQmMaxSplit = 8;          // split-K ways at most
-constexpr int kQmProd = 8;                      // producer warps
-constexpr int kQmRowsPerProd = kQmRows / kQmProd;  // 16: two groups of 8 rows
-constexpr int kQmMmaWarp = kQmProd;
-constexpr int kQmThreads = (kQmProd + 5) * 32;
-// prepared B per superblock in global memory: main 64 x 256 fp16, min 64 x 16
-constexpr int kQmBMain = kQmN * 256 * 2;              // 32768
-constexpr int kQmBMin = kQmN * 16 * 2;                // 2048
-constexpr int kQmBBytes = kQmBMain + kQmBMin;
-constexpr int kQmBHalf = kQmBMain / 2;                // the B main half a stage holds
-// per stage: A main 128 x 128 fp16, A min 128 x 16, B main half 64 x 128, B min 64 x 16
-constexpr int kQmAMain = kQmRows * 128 * 2;           // 32768
-constexpr int kQmAMin = kQmRows * 16 * 2;             // 4096
-constexpr int kQmStageBytes = kQmAMain + kQmAMin + kQmBHalf + kQmBMin;  // 55296
+constexpr int kQmRows = 128;             // weight rows per CTA (MMA M)
+constexpr int kQmTok = 32;               // tokens (B rows 0..31 hi, 32..63 lo)
+constexpr int kQmN = 2 * kQmTok;         // MMA N
+constexpr int kQmStages = 4;             // shared-memory stages, one superblock each
+constexpr int kQmAStages = 4;            // TMEM A stages of half a superblock (64 columns)
+constexpr int kQmRegions = 2;            // TMEM accumulator regions (128 columns)
+constexpr int kQmMaxSplit = 8;           // split-K ways at most
+constexpr int kQmProd = 16;              // producer warps
+constexpr int kQmMmaWarp = 16, kQmTmaWarp = 18;  // MMA issuers: warps 16, 17
+constexpr int kQmThreads = 23 * 32;
+constexpr int kQmCodes = kQmRows * 128;  // code bytes of one superblock
+constexpr int kQmHdr = kQmRows * 16;     // headers of one superblock
+constexpr int kQmAMin = kQmRows * 16 * 2;    // A_min of one superblock (fp16, core-matrix layout)
+constexpr int kQmBMain = kQmN * 256 * 2;     // B tile of one superblock (fp16, core-matrix layout)
+constexpr int kQmBMin = kQmN * 16 * 2;       // B_min: hi/lo of the sub-block sums
+constexpr int kQmBBytes = kQmBMain + kQmBMin;  // prepared activations per superblock in global memory
+constexpr int kQmStageBytes = kQmCodes + kQmHdr + kQmAMin + kQmBBytes;  // 57344 = 56 KB
 constexpr int kQmSmem = 1024 + kQmStages * kQmStageBytes;
+constexpr uint32_t kQmRegionCol = kQmAStages * 64;  // first accumulator column
 
 // Core-matrix layout (K-major, no swizzle): 8 rows x 8 fp16 (16 bytes per row) = 128 bytes
 // contiguous; core matrix (row group g, K chunk c) at (c * G + g) * 128 bytes, G = rows/8.
@@ -90,6 +117,15 @@ __device__ __forceinline__ uint64_t qm_desc(uint32_t saddr, uint32_t lbo, uint32
 // kind::f16 instruction descriptor: D f32, A/B f16, both K-major, N = 64, M = 128
 constexpr uint32_t kQmIdesc = (1u << 4) | ((uint32_t)(kQmN >> 3) << 17) | ((uint32_t)(kQmRows >> 4) << 24);
 
+// tcgen05.mma with A in tensor memory (lane = row, K as fp16 pairs along the columns) and B
+// from a shared-memory descriptor
+__device__ __forceinline__ void qm_mma_ts(uint32_t dtmem, uint32_t atmem, uint64_t db, uint32_t acc) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p; }" ::"r"(dtmem),
+        "r"(atmem), "l"(db), "r"(kQmIdesc), "r"(acc));
+}
+// tcgen05.mma with A and B from shared-memory descriptors
 __device__ __forceinline__ void qm_mma(uint32_t dtmem, uint64_t da, uint64_t db, uint32_t acc) {
     asm volatile(
         "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
@@ -102,28 +138,37 @@ __device__ __forceinline__ void qm_commit(uint64_t *bar) {
 }
 __device__ __forceinline__ void qm_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void qm_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-// 32 consecutive f32 columns of this warp's 32 TMEM lanes
-__device__ __forceinline__ void qm_ld32(uint32_t taddr, float (&v)[32]) {
-    uint32_t r[32];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
+// 8 consecutive f32 columns of this warp's 32 TMEM lanes
+__device__ __forceinline__ void qm_ld8(uint32_t taddr, float (&v)[8]) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
 #pragma unroll
-    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
 }
 __device__ __forceinline__ void qm_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// 32 consecutive 32-bit TMEM columns of this warp's 32 lanes
+__device__ __forceinline__ void qm_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+        "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+        "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+// TMA tensor maps of one Q4_K matrix (made on the host with cuTensorMapEncodeTiled)
+struct QmMaps {
+    const uint8_t *q;  // the matrix's code bytes (identifies it)
+    CUtensorMap codes, hdr;
+};
 
 struct QmArgs {
     QW w;                  // Q4_K, rows x cols (cols % 256 == 0)
-    const uint8_t *xprep;  // prepared B: [cols/256][kQmBBytes]
+    const uint8_t *xprep;  // prepared activations: [cols/256][kQmBBytes]
     int M;                 // tokens (<= 32)
     float *C;              // C[t * ldc + n]
     int ldc;
@@ -135,17 +180,26 @@ struct QmArgs {
     int ksplit;
     float *part;
     unsigned *tickets;
-    // optional timeline of CTA (0,0) for tuning (%globaltimer ns): [0] entry, [1] exit,
-    // [2 + 3i] producers done with superblock i, [3 + 3i] its MMAs issued, [4 + 3i] its
-    // epilogue done, [194 + 2i] its B tile landed, [195 + 2i] its A tile complete (i < 64);
-    // 322 entries
-    unsigned long long *tl;
 };
 
-// X [M][K] f32 -> prepared B superblocks: fp16 hi/lo of x (rows 0..31 / 32..63, zero for
-// t >= M) in the core-matrix layout, and of the 8 sub-block sums in B_min (K columns 0..7,
-// the sums in f32 in index order).  grid (K/256), block 256: the 32 x 256 tile is staged in
-// shared memory first.
+// K order inside the tensor-core tiles: within every group of 4 consecutive K positions the
+// middle two are swapped (MMA position p holds source k = qm_kperm(p); the map is its own
+// inverse).  A 32-bit word of 4 code bytes then yields its fp16 pairs (byte 0, byte 2) and
+// (byte 1, byte 3) with one mask each, see qm_decode_word.
+__host__ __device__ __forceinline__ int qm_kperm(int p) { return (p & ~3) | ((p & 1) << 1) | ((p >> 1) & 1); }
+
+// fp16 hi/lo of an f32 pair, packed: the lo row of a B tile holds fp16(v - fp16(v))
+__device__ __forceinline__ uint32_t qm_split2(float v0, float v1, bool lo) {
+    const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+    const __half r0 = lo ? __float2half_rn(v0 - __half2float(h0)) : h0;
+    const __half r1 = lo ? __float2half_rn(v1 - __half2float(h1)) : h1;
+    return (uint32_t)__half_as_ushort(r0) | ((uint32_t)__half_as_ushort(r1) << 16);
+}
+
+// X [M][K] f32 -> prepared activations per superblock: B = fp16 hi/lo of x (rows 0..31 /
+// 32..63, zero for t >= M) in the core-matrix layout and tensor-core K order, then B_min =
+// fp16 hi/lo of the 8 sub-block sums (f32, index order) in K columns 0..7, zeros in 8..15.
+// grid (K/256), block 256: the 32 x 256 tile is staged in shared memory first.
 static __global__ __launch_bounds__(256) void k_qm_prep_x(const float *__restrict__ X, int ldx, int M, int K,
                                                           uint8_t *__restrict__ out) {
     __shared__ float xt[kQmTok][257];
@@ -153,45 +207,33 @@ static __global__ __launch_bounds__(256) void k_qm_prep_x(const float *__restric
     const int sb = blockIdx.x, tid = threadIdx.x;
     for (int t = 0; t < kQmTok; t++) xt[t][tid] = t < M ? X[(size_t)t * ldx + sb * 256 + tid] : 0.f;
     __syncthreads();
+    uint8_t *o = out + (size_t)sb * kQmBBytes;
     {
-        const int t = tid >> 3, j = tid & 7;
+        const int t = tid & 31, j = tid >> 5;
         float sm = 0.f;
         for (int i = 0; i < 32; i++) sm += xt[t][32 * j + i];
         sums[t][j] = sm;
     }
-    uint8_t *o = out + (size_t)sb * kQmBBytes;
-    // main: 64 rows x 32 chunks of 8
+    // 64 rows x 32 chunks of 8 (K positions 8c..8c+7 in tensor-core order)
     for (int idx = tid; idx < kQmN * 32; idx += 256) {
         const int row = idx % kQmN, c = idx / kQmN, t = row % kQmTok;
         const bool lo = row >= kQmTok;
         uint32_t v[4];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const float x0 = xt[t][c * 8 + 2 * i], x1 = xt[t][c * 8 + 2 * i + 1];
-            const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
-            const __half r0 = lo ? __float2half_rn(x0 - __half2float(h0)) : h0;
-            const __half r1 = lo ? __float2half_rn(x1 - __half2float(h1)) : h1;
-            v[i] = (uint32_t)__half_as_ushort(r0) | ((uint32_t)__half_as_ushort(r1) << 16);
-        }
+        for (int i = 0; i < 4; i++) v[i] = qm_split2(xt[t][qm_kperm(c * 8 + 2 * i)], xt[t][qm_kperm(c * 8 + 2 * i + 1)], lo);
         *reinterpret_cast<uint4 *>(o + ((size_t)(c * (kQmN / 8) + row / 8) * 8 + row % 8) * 16) = make_uint4(v[0], v[1], v[2], v[3]);
     }
     __syncthreads();
-    // min: 64 rows x 2 chunks; chunk 0 holds the 8 sub-block sums, chunk 1 zeros
-    uint8_t *om = o + kQmBMain;
+    // B_min: 64 rows x 2 chunks; chunk 0 holds the 8 sub-block sums, chunk 1 zeros
     if (tid < kQmN * 2) {
         const int row = tid % kQmN, c = tid / kQmN, t = row % kQmTok;
         const bool lo = row >= kQmTok;
         uint32_t v[4] = {0, 0, 0, 0};
         if (c == 0)
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const float s0 = sums[t][2 * i], s1 = sums[t][2 * i + 1];
-                const __half h0 = __float2half_rn(s0), h1 = __float2half_rn(s1);
-                const __half r0 = lo ? __float2half_rn(s0 - __half2float(h0)) : h0;
-                const __half r1 = lo ? __float2half_rn(s1 - __half2float(h1)) : h1;
-                v[i] = (uint32_t)__half_as_ushort(r0) | ((uint32_t)__half_as_ushort(r1) << 16);
-            }
-        *reinterpret_cast<uint4 *>(om + ((size_t)(c * (kQmN / 8) + row / 8) * 8 + row % 8) * 16) = make_uint4(v[0], v[1], v[2], v[3]);
+            for (int i = 0; i < 4; i++) v[i] = qm_split2(sums[t][2 * i], sums[t][2 * i + 1], lo);
+        *reinterpret_cast<uint4 *>(o + kQmBMain + ((size_t)(c * (kQmN / 8) + row / 8) * 8 + row % 8) * 16) =
+            make_uint4(v[0], v[1], v[2], v[3]);
     }
 }
 
@@ -217,44 +259,34 @@ __device__ __forceinline__ __half2 small_int_h2(uint32_t a, uint32_t b) {
     const uint32_t v = (0x6400u | a) | ((0x6400u | b) << 16);
     return __hsub2(*reinterpret_cast<const __half2 *>(&v), __half2half2(__ushort_as_half(0x6400)));
 }
-__device__ __forceinline__ uint32_t half2_bits(int a, int b) {
-    const __half2 h = small_int_h2((uint32_t)a, (uint32_t)b);
-    return *reinterpret_cast<const uint32_t *>(&h);
-}
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<const uint32_t *>(&h); }
+__device__ __forceinline__ uint32_t half2_bits(int a, int b) { return h2_bits(small_int_h2((uint32_t)a, (uint32_t)b)); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t v) { return *reinterpret_cast<const __half2 *>(&v); }
 
-// Two 4-bit codes as an fp16 pair times the integer scale s, exactly: 0x6400 | v is the
-// half 1024 + v, and fma((1024 + v), s, -1024 s) = v * s (<= 945) is exact in one rounding.
-__device__ __forceinline__ uint32_t nib2_scaled(uint32_t pair, __half2 s2, __half2 bias) {
-    const uint32_t hv = (pair & 0x000F000Fu) | 0x64006400u;
-    const __half2 r = __hfma2(*reinterpret_cast<const __half2 *>(&hv), s2, bias);
-    return *reinterpret_cast<const uint32_t *>(&r);
+// Scale constants of one sub-block for qm_decode_word.  Low nibbles: 0x6400 | q is the half
+// 1024 + q and fma(1024 + q, s, -1024 s) = q s exactly (<= 945).  High nibbles stay in bits
+// 4..7: 0x6400 | 16q is 1024 + 16 q and fma(1024 + 16 q, s / 16, -64 s) = q s exactly (s / 16
+// is exact in fp16).
+struct QmScale {
+    __half2 s, b;
+};
+__device__ __forceinline__ QmScale qm_scale_lo(int s) {
+    const __half2 s2 = small_int_h2((uint32_t)s, (uint32_t)s);
+    return {s2, __hmul2(s2, __half2half2(__ushort_as_half(0xE400)))};  // -1024 s
 }
-
-// Dequantise 16 code bytes (32 weights: 16 low nibbles of sub-block 2c at K positions
-// k_lo.., 16 high nibbles of sub-block 2c+1 at k_hi..) into fp16 s*q values and store them
-// as four 16-byte core-matrix rows.  Registers only.
-__device__ __forceinline__ void qm_store_codes(uint8_t *A, int row, int k_lo, int k_hi, uint4 q, int s_lo, int s_hi) {
-    const __half2 sl2 = small_int_h2((uint32_t)s_lo, (uint32_t)s_lo), sh2 = small_int_h2((uint32_t)s_hi, (uint32_t)s_hi);
-    const __half2 m1024 = __half2half2(__ushort_as_half(0xE400));  // -1024
-    const __half2 bl = __hmul2(sl2, m1024), bh = __hmul2(sh2, m1024);  // -1024 s, exact
-    const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
-    uint32_t lo[8], hi[8];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        // bytes (0,1) and (2,3) of the word into the two 16-bit halves
-        const uint32_t p01 = __byte_perm(wd[i], 0, 0x4140), p23 = __byte_perm(wd[i], 0, 0x4342);
-        lo[2 * i] = nib2_scaled(p01, sl2, bl);
-        lo[2 * i + 1] = nib2_scaled(p23, sl2, bl);
-        hi[2 * i] = nib2_scaled(p01 >> 4, sh2, bh);
-        hi[2 * i + 1] = nib2_scaled(p23 >> 4, sh2, bh);
-    }
-    const int g = row >> 3, r0 = row & 7;
-    constexpr int G = kQmRows / 8;
-    const int c0 = k_lo >> 3, c1 = k_hi >> 3;
-    *reinterpret_cast<uint4 *>(A + ((size_t)(c0 * G + g) * 8 + r0) * 16) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-    *reinterpret_cast<uint4 *>(A + ((size_t)((c0 + 1) * G + g) * 8 + r0) * 16) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
-    *reinterpret_cast<uint4 *>(A + ((size_t)(c1 * G + g) * 8 + r0) * 16) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    *reinterpret_cast<uint4 *>(A + ((size_t)((c1 + 1) * G + g) * 8 + r0) * 16) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+__device__ __forceinline__ QmScale qm_scale_hi(int s) {
+    const __half2 s2 = __hmul2(small_int_h2((uint32_t)s, (uint32_t)s), __half2half2(__ushort_as_half(0x2C00)));  // s/16
+    return {s2, __hmul2(s2, __half2half2(__ushort_as_half(0xE400)))};  // -64 s
+}
+// 4 code bytes (K positions l..l+3 of two sub-blocks) -> 4 fp16 pairs in tensor-core K order:
+// lo0 = (b0, b2), lo1 = (b1, b3) of the low nibbles, hi0, hi1 the same for the high nibbles.
+__device__ __forceinline__ void qm_decode_word(uint32_t w, const QmScale &sl, const QmScale &sh, uint32_t &lo0,
+                                               uint32_t &lo1, uint32_t &hi0, uint32_t &hi1) {
+    const uint32_t w8 = w >> 8;
+    lo0 = h2_bits(__hfma2(bits_h2((w & 0x000F000Fu) | 0x64006400u), sl.s, sl.b));
+    lo1 = h2_bits(__hfma2(bits_h2((w8 & 0x000F000Fu) | 0x64006400u), sl.s, sl.b));
+    hi0 = h2_bits(__hfma2(bits_h2((w & 0x00F000F0u) | 0x64006400u), sh.s, sh.b));
+    hi1 = h2_bits(__hfma2(bits_h2((w8 & 0x00F000F0u) | 0x64006400u), sh.s, sh.b));
 }
 
 // Output of one row n for the first a.M tokens (all lanes of the warp call it).
@@ -277,42 +309,45 @@ __device__ __forceinline__ void qm_epilogue(const QmArgs &a, const float (&acc)[
     }
 }
 
-// grid (rows/128, ksplit), block kQmThreads, dynamic smem kQmSmem.  One TMEM allocation of
-// 512 columns.  Stage j holds half h = j % 2 of superblock i = j / 2 (K range 128h..128h+127);
-// superblock i accumulates in TMEM region i % 4 over its two stages.
-static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a) {
+// grid (rows/128, ksplit), block kQmThreads, dynamic smem kQmSmem.  tm_codes: 2-D map over
+// the code bytes [rows][cols/2], box 128 bytes x 128 rows, 128-byte swizzle; tm_hdr: 2-D map
+// over the headers [rows][cols/256 * 16], box 16 bytes x 128 rows.  Rows past the end read
+// as zeros.  One TMEM allocation of 512 columns.
+static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a, const __grid_constant__ CUtensorMap tm_codes,
+                                                                const __grid_constant__ CUtensorMap tm_hdr) {
     extern __shared__ __align__(1024) uint8_t qsm[];
-    uint64_t *full_a = reinterpret_cast<uint64_t *>(qsm);        // [S] producers done (256 arrivals)
-    uint64_t *full_b = full_a + kQmStages;                         // [S] B bulk copies landed
-    uint64_t *empty = full_b + kQmStages;                          // [S] MMAs of the stage done
-    uint64_t *ready = empty + kQmStages;                           // [R] region complete
-    uint64_t *tfree = ready + kQmRegions;                          // [R] epilogue read the region (128 arrivals)
+    uint64_t *rawf = reinterpret_cast<uint64_t *>(qsm);  // [S] codes + headers landed
+    uint64_t *bf = rawf + kQmStages;                      // [S] B landed
+    uint64_t *empty = bf + kQmStages;                     // [S] MMAs of the stage done
+    uint64_t *a_full = empty + kQmStages;                 // [AS] A stage written (one arrival per producer warp of the half)
+    uint64_t *a_empty = a_full + kQmAStages;              // [AS] MMAs that read the A stage done
+    uint64_t *ready = a_empty + kQmAStages;               // [R] region complete
+    uint64_t *tfree = ready + kQmRegions;                 // [R] epilogue read the region (one arrival per warp)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tfree + kQmRegions);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
     uint8_t *stages = qsm + 1024;
-    const bool tl_on = a.tl && blockIdx.x == 0 && blockIdx.y == 0;
-    auto tl_mark = [&](int slot) {
-        if (tl_on && slot < 2 + 5 * 64) {
-            unsigned long long t;
-            asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-            a.tl[slot] = t;
-        }
-    };
-    if (threadIdx.x == 0) tl_mark(0);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // the 128-byte-swizzled TMA destinations need 1024-byte alignment
+    if (smem_u32(qsm) & 1023u) {
+        if (tid == 0) atomicOr(a.err, JDG_ERR_SHAPE);
+        return;
+    }
     const int K = a.w.cols, nsb = K / 256, n0 = blockIdx.x * kQmRows;
     const int ks = a.ksplit > 1 ? a.ksplit : 1, kz = blockIdx.y, sb0 = (int)((long long)kz * nsb / ks);
     const int nloc = (int)((long long)(kz + 1) * nsb / ks) - sb0;  // superblocks of this CTA
-    const int nst = 2 * nloc;                                       // stages of this CTA
     if (tid == 0) {
         for (int s = 0; s < kQmStages; s++) {
-            mbar_init(&full_a[s], kQmProd * 32);
-            mbar_init(&full_b[s], 1);
+            mbar_init(&rawf[s], 1);
+            mbar_init(&bf[s], 1);
             mbar_init(&empty[s], 1);
+        }
+        for (int s = 0; s < kQmAStages; s++) {
+            mbar_init(&a_full[s], kQmProd / 2);
+            mbar_init(&a_empty[s], 1);
         }
         for (int q = 0; q < kQmRegions; q++) {
             mbar_init(&ready[q], 1);
-            mbar_init(&tfree[q], 128);
+            mbar_init(&tfree[q], 4);
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -326,134 +361,147 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a) {
     __syncthreads();
     qm_fence_after();
     const uint32_t tmem = *tmem_slot;
-    int issued_mma = 0;  // stages whose MMAs were issued (lane 0 of the MMA warp)
-    int issued_b = 0;    // stages whose B copies were issued (thread 0)
+    int issued_mma = 0;  // A stages (half superblocks) whose MMAs were issued (MMA thread)
+    int issued_ld = 0;   // superblocks whose copies were issued (TMA thread)
 
     if (warp < kQmProd) {
         // ---------------- producers ----------------
-        // warp w owns rows 16w..16w+15 (2 groups of 8).  A row's half superblock is 64 code
-        // bytes = 4 pieces of 16.  Pass p covers row group p: lane l takes row 8p + l%8 and
-        // piece l/8, so the 8 lanes of a piece store one whole 128-byte core matrix (no bank
-        // conflicts).  Raw loads run three stages ahead in a ring of register buffers.
-        auto load_st = [&](int j, uint4 (&qv)[2], uint4 (&hv)[2]) {
-            const int sb = sb0 + (j >> 1), piece = 4 * (j & 1) + (lane >> 3);
+        pdl_trigger();
+        const int quarter = warp & 3, kq = warp >> 2, row = quarter * 32 + lane;
+        const uint32_t tlane = (uint32_t)(quarter * 32) << 16;
+        // K quarter kq of a superblock = code bytes 32kq..32kq+31 of the row (16-byte chunks
+        // 2kq, 2kq+1): low nibbles are sub-block 2kq, high nibbles sub-block 2kq+1.  It lies in
+        // half h = kq / 2, columns 32 (kq % 2) of that half's A stage.
+        auto body = [&](auto kq_tag) {
+            constexpr int KQ = decltype(kq_tag)::value, H = KQ >> 1;
+            for (int i = 0; i < nloc; i++) {
+                const int s = i % kQmStages, j = 2 * i + H, as = j % kQmAStages;
+                bool ok = mbar_wait(&rawf[s], (uint32_t)(i / kQmStages) & 1u);
+                if (ok && j >= kQmAStages) ok = mbar_wait(&a_empty[as], (uint32_t)((j / kQmAStages) - 1) & 1u);
+                if (!ok) *abort_flag = 1;
+                // tcgen05.st is warp-collective: leave as a whole warp
+                if (__any_sync(JDG_FULL, !ok || *abort_flag)) break;
+                uint8_t *st = stages + (size_t)s * kQmStageBytes;
+                const uint4 hv = *reinterpret_cast<const uint4 *>(st + kQmCodes + row * 16);
+                const uint8_t *crow = st + row * 128;
+                const uint4 c0 = *reinterpret_cast<const uint4 *>(crow + (((2 * KQ) ^ (row & 7)) << 4));
+                const uint4 c1 = *reinterpret_cast<const uint4 *>(crow + (((2 * KQ + 1) ^ (row & 7)) << 4));
+                int s_lo, s_hi, mm;
+                smk4_reg(2 * KQ, hv, s_lo, mm);
+                smk4_reg(2 * KQ + 1, hv, s_hi, mm);
+                const QmScale sl = qm_scale_lo(s_lo), sh = qm_scale_hi(s_hi);
+                // columns [0, 8) chunk 0 low, [8, 16) chunk 1 low, [16, 24) chunk 0 high,
+                // [24, 32) chunk 1 high
+                uint32_t r[32];
+                const uint32_t w0[4] = {c0.x, c0.y, c0.z, c0.w}, w1[4] = {c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
-            for (int pass = 0; pass < 2; pass++) {
-                const int n = n0 + warp * kQmRowsPerProd + pass * 8 + (lane & 7);
-                qv[pass] = make_uint4(0, 0, 0, 0);
-                hv[pass] = make_uint4(0, 0, 0, 0);
-                if (j < nst && n < a.w.rows) {
-                    qv[pass] = ld_stream_u4(a.w.q + (size_t)n * (K / 2) + (size_t)sb * 128 + piece * 16);
-                    hv[pass] = ld_nc_u4(a.w.s + ((size_t)n * nsb + sb) * 16);
+                for (int k = 0; k < 4; k++) {
+                    qm_decode_word(w0[k], sl, sh, r[2 * k], r[2 * k + 1], r[16 + 2 * k], r[16 + 2 * k + 1]);
+                    qm_decode_word(w1[k], sl, sh, r[8 + 2 * k], r[8 + 2 * k + 1], r[24 + 2 * k], r[24 + 2 * k + 1]);
                 }
-            }
-        };
-        // H (the half, j % 2) is a compile-time constant: the scale bytes a lane needs then sit
-        // at fixed header positions, two candidates per lane chosen by lane / 16
-        auto produce = [&](int j, const uint4 (&qv)[2], const uint4 (&hv)[2], auto h_tag) -> bool {
-            constexpr int h = decltype(h_tag)::value;
-            const int s = j % kQmStages, sb = sb0 + (j >> 1);
-            if (j >= kQmStages && !mbar_wait(&empty[s], (uint32_t)((j / kQmStages) - 1) & 1u)) *abort_flag = 1;
-            if (*abort_flag) return false;
-            if (tid == 0 && h == 1 && (j >> 1) < 64) tl_mark(2 + 3 * 64 + 2 * (j >> 1));  // producer starts half 1
-            uint8_t *st = stages + (size_t)s * kQmStageBytes;
-            uint8_t *Am = st, *An = st + kQmAMain, *Bm = An + kQmAMin, *Bn = Bm + kQmBHalf;
-            if (tid == 0) {
-                const uint8_t *src = a.xprep + (size_t)sb * kQmBBytes;
-                mbar_expect_tx(&full_b[s], kQmBHalf + (h == 0 ? kQmBMin : 0));
-                bulk_g2s(Bm, src + (size_t)h * kQmBHalf, kQmBHalf, &full_b[s]);
-                if (h == 0) bulk_g2s(Bn, src + kQmBMain, kQmBMin, &full_b[s]);
-                issued_b = j + 1;
-            }
-#pragma unroll
-            for (int pass = 0; pass < 2; pass++) {
-                const int row = warp * kQmRowsPerProd + pass * 8 + (lane & 7), piece = 4 * h + (lane >> 3);
-                const int c = piece >> 1, l0 = (piece & 1) * 16;
-                // sub-blocks 2c and 2c+1 with c = 2h + lane/16
-                int sa, sbb, sc_, sd, mm;
-                smk4_reg(4 * h, hv[pass], sa, mm);
-                smk4_reg(4 * h + 1, hv[pass], sbb, mm);
-                smk4_reg(4 * h + 2, hv[pass], sc_, mm);
-                smk4_reg(4 * h + 3, hv[pass], sd, mm);
-                const bool hiC = (lane >> 4) & 1;
-                const int s0 = hiC ? sc_ : sa, s1 = hiC ? sd : sbb;
-                qm_store_codes(Am, row, 64 * c + l0 - 128 * h, 64 * c + 32 + l0 - 128 * h, qv[pass], s0, s1);
-                if (h == 0 && (lane >> 3) == 0) {
-                    // A_min row: m_0..m_7 in K columns 0..7, zeros in 8..15
+                qm_st32(tmem + tlane + (uint32_t)(as * 64 + (KQ & 1) * 32), r);
+                if (KQ == 0) {
+                    // A_min row: m_0..m_7 in K columns 0..7, zeros in 8..15 (core-matrix layout)
                     int mj[8];
 #pragma unroll
                     for (int jj = 0; jj < 8; jj++) {
                         int sj;
-                        smk4_reg(jj, hv[pass], sj, mj[jj]);
+                        smk4_reg(jj, hv, sj, mj[jj]);
                     }
                     constexpr int G = kQmRows / 8;
+                    uint8_t *An = st + kQmCodes + kQmHdr;
                     const int g = row >> 3, r0 = row & 7;
                     *reinterpret_cast<uint4 *>(An + ((size_t)(0 * G + g) * 8 + r0) * 16) =
                         make_uint4(half2_bits(mj[0], mj[1]), half2_bits(mj[2], mj[3]), half2_bits(mj[4], mj[5]),
                                    half2_bits(mj[6], mj[7]));
                     *reinterpret_cast<uint4 *>(An + ((size_t)(1 * G + g) * 8 + r0) * 16) = make_uint4(0, 0, 0, 0);
+                    // generic-proxy stores must be visible to the tensor core (async proxy)
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                qm_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&a_full[as]);
             }
-            // generic-proxy stores must be visible to the tensor core (async proxy)
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive(&full_a[s]);
-            if (tid == 0 && h == 1) tl_mark(2 + 3 * (j >> 1));
-            return true;
         };
-        uint4 qa[2], ha[2], qb[2], hb[2], qc[2], hc[2], qd[2], hd[2];
-        // weights do not depend on the previous kernel: the first stages load before the
-        // dependency wait (Programmatic Dependent Launch)
-        load_st(0, qa, ha);
-        load_st(1, qb, hb);
-        load_st(2, qc, hc);
-        pdl_wait();
-        pdl_trigger();
-        using H0 = std::integral_constant<int, 0>;
-        using H1 = std::integral_constant<int, 1>;
-        for (int j = 0; j < nst; j += 4) {  // nst is even: j, j+2 are first halves
-            load_st(j + 3, qd, hd);
-            if (!produce(j, qa, ha, H0{}) || j + 1 >= nst) break;
-            load_st(j + 4, qa, ha);
-            if (!produce(j + 1, qb, hb, H1{}) || j + 2 >= nst) break;
-            load_st(j + 5, qb, hb);
-            if (!produce(j + 2, qc, hc, H0{}) || j + 3 >= nst) break;
-            load_st(j + 6, qc, hc);
-            if (!produce(j + 3, qd, hd, H1{})) break;
+        switch (kq) {
+        case 0: body(std::integral_constant<int, 0>{}); break;
+        case 1: body(std::integral_constant<int, 1>{}); break;
+        case 2: body(std::integral_constant<int, 2>{}); break;
+        default: body(std::integral_constant<int, 3>{}); break;
         }
-    } else if (warp == kQmMmaWarp) {
-        // ---------------- MMA issuer ----------------
+    } else if (warp < kQmTmaWarp) {
+        // ---------------- MMA issuers: superblocks i with i % 2 == warp - kQmMmaWarp ----------------
         pdl_trigger();
         if (lane == 0) {
             constexpr int GA = kQmRows / 8, GB = kQmN / 8;
-            for (int j = 0; j < nst; j++) {
-                const int s = j % kQmStages, h = j & 1, i = j >> 1, q = i % kQmRegions;
-                const uint32_t ph = (uint32_t)(j / kQmStages) & 1u;
-                bool ok = mbar_wait(&full_b[s], ph);
-                ok = ok && mbar_wait(&full_a[s], ph);
-                if (h == 1 && i < 64) tl_mark(2 + 3 * 64 + 2 * i + 1);
-                if (ok && h == 0 && i >= kQmRegions) ok = mbar_wait(&tfree[q], (uint32_t)((i / kQmRegions) - 1) & 1u);
+            for (int j = 2 * (warp - kQmMmaWarp); j < 2 * nloc; j += (j & 1) ? 3 : 1) {
+                const int i = j >> 1, h = j & 1, s = i % kQmStages, as = j % kQmAStages, q = i % kQmRegions;
+                bool ok = true;
+                if (h == 0) {
+                    ok = mbar_wait(&bf[s], (uint32_t)(i / kQmStages) & 1u);
+                    if (ok && i >= kQmRegions) ok = mbar_wait(&tfree[q], (uint32_t)((i / kQmRegions) - 1) & 1u);
+                }
+                ok = ok && mbar_wait(&a_full[as], (uint32_t)(j / kQmAStages) & 1u);
                 if (!ok || *abort_flag) {
                     *abort_flag = 1;
                     break;
                 }
                 qm_fence_after();
                 const uint32_t st = smem_u32(stages + (size_t)s * kQmStageBytes);
-                const uint32_t am = st, an = st + kQmAMain, bm = an + kQmAMin, bn = bm + kQmBHalf;
-                const uint32_t dmain = tmem + (uint32_t)(q * 128), dmin = dmain + 64;
+                const uint32_t an = st + kQmCodes + kQmHdr, bm = an + kQmAMin, bn = bm + kQmBMain;
+                const uint32_t at = tmem + (uint32_t)(as * 64), dmain = tmem + kQmRegionCol + (uint32_t)(q * 128);
 #pragma unroll
-                for (int k8 = 0; k8 < 8; k8++)
-                    qm_mma(dmain, qm_desc(am + k8 * 2 * GA * 128, GA * 128, 128), qm_desc(bm + k8 * 2 * GB * 128, GB * 128, 128),
-                           (h > 0 || k8 > 0) ? 1u : 0u);
-                if (h == 0) qm_mma(dmin, qm_desc(an, GA * 128, 128), qm_desc(bn, GB * 128, 128), 0);
-                qm_commit(&empty[s]);
-                if (h == 1) qm_commit(&ready[q]);
+                for (int k = 0; k < 8; k++)
+                    qm_mma_ts(dmain, at + (uint32_t)(8 * k), qm_desc(bm + (8 * h + k) * 2 * GB * 128, GB * 128, 128),
+                              (h > 0 || k > 0) ? 1u : 0u);
+                if (h == 0) qm_mma(dmain + 64, qm_desc(an, GA * 128, 128), qm_desc(bn, GB * 128, 128), 0);
+                if (h == 1) {
+                    qm_commit(&empty[s]);
+                    qm_commit(&ready[q]);
+                }
+                qm_commit(&a_empty[as]);
                 issued_mma = j + 1;
-                if (h == 1) tl_mark(3 + 3 * i);
+            }
+        }
+        __syncwarp();
+    } else if (warp == kQmTmaWarp) {
+        // ---------------- TMA issuer ----------------
+        pdl_trigger();
+        if (lane == 0) {
+            auto raw = [&](int i) {
+                const int s = i % kQmStages;
+                uint8_t *st = stages + (size_t)s * kQmStageBytes;
+                mbar_expect_tx(&rawf[s], kQmCodes + kQmHdr);
+                tma_load_2d(st, &tm_codes, (sb0 + i) * 128, n0, &rawf[s]);
+                tma_load_2d(st + kQmCodes, &tm_hdr, (sb0 + i) * 16, n0, &rawf[s]);
+            };
+            auto bload = [&](int i) {
+                const int s = i % kQmStages;
+                uint8_t *st = stages + (size_t)s * kQmStageBytes;
+                mbar_expect_tx(&bf[s], kQmBBytes);
+                bulk_g2s(st + kQmCodes + kQmHdr + kQmAMin, a.xprep + (size_t)(sb0 + i) * kQmBBytes, kQmBBytes, &bf[s]);
+            };
+            const int pre = nloc < kQmStages ? nloc : kQmStages;
+            // the weights do not depend on the previous kernel: they load before the wait
+            for (int i = 0; i < pre; i++) raw(i);
+            pdl_wait();
+            for (int i = 0; i < pre; i++) bload(i);
+            issued_ld = pre;
+            for (int i = pre; i < nloc; i++) {
+                const int s = i % kQmStages;
+                if (!mbar_wait(&empty[s], (uint32_t)((i / kQmStages) - 1) & 1u) || *abort_flag) {
+                    *abort_flag = 1;
+                    break;
+                }
+                raw(i);
+                bload(i);
+                issued_ld = i + 1;
             }
         }
         __syncwarp();
     } else {
-        // ---------------- epilogue: warps 9..12, TMEM lane quarter warp % 4 ----------------
+        // ---------------- epilogue: warps 19..22, TMEM lane quarter warp % 4 ----------------
         const int quarter = warp & 3, row = quarter * 32 + lane, n = n0 + row;
         pdl_wait();  // the epilogue reads and writes C
         pdl_trigger();
@@ -476,22 +524,24 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a) {
             // the TMEM loads below are warp-collective: leave the loop as a whole warp
             if (__any_sync(JDG_FULL, !ok || *abort_flag)) break;
             qm_fence_after();
-            const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(q * 128);
-            float mh[32], ml[32];
+            const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + kQmRegionCol + (uint32_t)(q * 128);
             const float d = h2f((uint16_t)(hw & 0xFFFF)), dmin = h2f((uint16_t)(hw >> 16));
-            qm_ld32(base, mh);
-            qm_ld32(base + 32, ml);
-            qm_ld_wait();
 #pragma unroll
-            for (int t = 0; t < kQmTok; t++) acc[t] = fmaf(d, mh[t] + ml[t], acc[t]);
-            qm_ld32(base + 64, mh);
-            qm_ld32(base + 96, ml);
-            qm_ld_wait();
+            for (int part = 0; part < 2; part++) {  // A.B, then A_min.B_min
+                const float sc = part == 0 ? d : -dmin;
+#pragma unroll
+                for (int qt = 0; qt < 4; qt++) {
+                    float vh[8], vl[8];
+                    qm_ld8(base + 64 * part + 8 * qt, vh);
+                    qm_ld8(base + 64 * part + 32 + 8 * qt, vl);
+                    qm_ld_wait();
+#pragma unroll
+                    for (int t = 0; t < 8; t++) acc[8 * qt + t] = fmaf(sc, vh[t] + vl[t], acc[8 * qt + t]);
+                }
+            }
             qm_fence_before();
-            mbar_arrive(&tfree[q]);
-            if (warp == kQmMmaWarp + 1 && lane == 0) tl_mark(4 + 3 * i);
-#pragma unroll
-            for (int t = 0; t < kQmTok; t++) acc[t] = fmaf(-dmin, mh[t] + ml[t], acc[t]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tfree[q]);
         }
         if (!__any_sync(JDG_FULL, *abort_flag)) {
             if (ks == 1) {
@@ -519,33 +569,39 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a) {
             }
         }
         __syncthreads();
-        if (s_last && warp > kQmMmaWarp) {
+        if (s_last && warp > kQmTmaWarp) {
             const int row = (warp & 3) * 32 + lane, n = n0 + row;
             float acc[kQmTok];
 #pragma unroll
             for (int t = 0; t < kQmTok; t++) acc[t] = 0.f;
-            // split by split, all tokens' loads in flight at once (ks round trips in total)
-            for (int z = 0; z < ks; z++) {
-                float v[kQmTok];
+            // split by split, half the tokens' loads in flight at once
+            for (int z = 0; z < ks; z++)
 #pragma unroll
-                for (int t = 0; t < kQmTok; t++)
-                    v[t] = (t < a.M && n < a.w.rows) ? __ldcg(a.part + ((size_t)z * kQmTok + t) * a.w.rows + n) : 0.f;
+                for (int hf = 0; hf < 2; hf++) {
+                    float v[16];
 #pragma unroll
-                for (int t = 0; t < kQmTok; t++) acc[t] += v[t];
-            }
+                    for (int t = 0; t < 16; t++)
+                        v[t] = (16 * hf + t < a.M && n < a.w.rows)
+                                   ? __ldcg(a.part + ((size_t)z * kQmTok + 16 * hf + t) * a.w.rows + n)
+                                   : 0.f;
+#pragma unroll
+                    for (int t = 0; t < 16; t++) acc[16 * hf + t] += v[t];
+                }
             qm_epilogue(a, acc, n, lane);
         }
     }
     if (*abort_flag) {
         if (tid == 0) atomicOr(a.err, JDG_ERR_TIMEOUT);
         // let the issued MMAs and copies land before the memory goes away
-        if (warp == kQmMmaWarp && lane == 0 && issued_mma > 0) {
-            const int j = issued_mma - 1;
-            mbar_wait(&empty[j % kQmStages], (uint32_t)(j / kQmStages) & 1u);
+        if (warp >= kQmMmaWarp && warp < kQmTmaWarp && lane == 0 && issued_mma > 0) {
+            const int j = issued_mma - 1;  // its commit follows every MMA issued before
+            mbar_wait(&a_empty[j % kQmAStages], (uint32_t)(j / kQmAStages) & 1u);
         }
-        if (tid == 0)
-            for (int j = max(0, issued_b - kQmStages); j < issued_b; j++)
-                mbar_wait(&full_b[j % kQmStages], (uint32_t)(j / kQmStages) & 1u);
+        if (warp == kQmTmaWarp && lane == 0)
+            for (int i = max(0, issued_ld - kQmStages); i < issued_ld; i++) {
+                mbar_wait(&rawf[i % kQmStages], (uint32_t)(i / kQmStages) & 1u);
+                mbar_wait(&bf[i % kQmStages], (uint32_t)(i / kQmStages) & 1u);
+            }
     }
     qm_fence_before();
     __syncthreads();
@@ -553,7 +609,6 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a) {
         qm_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
     }
-    if (threadIdx.x == 0) tl_mark(1);
 }
 
 }  // namespace jdg
