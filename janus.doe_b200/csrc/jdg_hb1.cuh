@@ -323,8 +323,10 @@ static __device__ void hb1_elect_serial(const HB1Args &a) {
         sel[0] = idx[0];
         w[0] = 1.0f;
     } else if (na >= 2) {
+        // all 16 votes in one pass (independent loads; dead experts' entries are not used)
         float v[kMaxE];
-        for (int i = 0; i < na; i++) v[idx[i]] = __ldcg(a.votes + idx[i]);
+#pragma unroll
+        for (int e = 0; e < kMaxE; e++) v[e] = __ldcg(a.votes + e);
         float mean = 0.f;
         for (int i = 0; i < na; i++) mean = __fadd_rn(mean, v[idx[i]]);
         mean = mean / (float)na;

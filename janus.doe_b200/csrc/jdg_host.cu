@@ -13,6 +13,7 @@
 
 #include "jdg_engine.h"
 #include "jdg_hb1.cuh"
+#include "jdg_hpar.cuh"
 #include "jdg_qmma.cuh"
 
 using namespace jdg;
@@ -60,6 +61,11 @@ struct HostPriv {
     float *qm_part = nullptr;               // split-K partials
     unsigned *qm_tickets = nullptr;         // split-K row-tile tickets
     std::vector<QmMaps> qm_maps;            // TMA tensor maps of the Q4_K matrices the GEMM reads
+    // batched LoRA parliament (jdg_hpar.cuh)
+    float *hpar_part = nullptr;             // [D/256][16][R+1][32] partial dots
+    unsigned *hpar_tickets = nullptr;       // [17]
+    float *hpar_votes = nullptr;            // [max_batch][16]
+    float *hpar_tall = nullptr;             // [max_batch][16][R]
 };
 
 HostPriv *priv(jdg_engine *e) { return (HostPriv *)e->host_priv; }
@@ -448,6 +454,13 @@ static int host_upload_impl(jdg_engine *e, const jd_host_model *h, int max_batch
     }
     DALLOC(hp->votes, kMaxE * 4);
     DALLOC(hp->tall, (size_t)kMaxE * R * 4);
+    if (max_batch > 1 && D % 256 == 0 && R % 4 == 0 && R <= 20) {
+        DALLOC(hp->hpar_part, (size_t)(D / 256) * kMaxE * (R + 1) * kHparTok * 4);
+        DALLOC(hp->hpar_tickets, (kMaxE + 1) * 4);
+        CK(cudaMemset(hp->hpar_tickets, 0, (kMaxE + 1) * 4));
+        DALLOC(hp->hpar_votes, (size_t)max_batch * kMaxE * 4);
+        DALLOC(hp->hpar_tall, (size_t)max_batch * kMaxE * R * 4);
+    }
     DALLOC(e->amax_v, 1024 * 4);
     DALLOC(e->amax_i, 1024 * 4);
     for (int l = 0; l < L; l++) {
@@ -495,8 +508,20 @@ static int host_upload_impl(jdg_engine *e, const jd_host_model *h, int max_batch
 }
 
 // ------------------------------------------------------------------------------------
+// C (epi)= W . X for M tokens.  do_norm: X is first RMS-normed with norm_w (null = ones,
+// janusdoe.c:504), the normed rows also going to xn_out when given.
 template <int EPI>
-static void launch_q(jdg_engine *e, const QW &w, const float *X, int ldx, int M, float *C, int ldc, float alpha) {
+static void launch_q(jdg_engine *e, const QW &w, const float *X, int ldx, int M, float *C, int ldc, float alpha,
+                     int do_norm = 0, const float *norm_w = nullptr, float *xn_out = nullptr) {
+    const bool tc = M > 1 && w.dt == JD_Q4_K && w.cols % 256 == 0 && priv(e) && priv(e)->xprep;
+    if (do_norm && !tc) {
+        // the other paths read a normed copy
+        float *dst = xn_out ? xn_out : e->xb;
+        k_rmsnorm<<<M, 256, 0, e->st>>>(X, norm_w, dst, w.cols, e->eps);
+        e->launches++;
+        X = dst;
+        ldx = w.cols;
+    }
     if (M == 1) {
         QGemvArgs a{w, X, C, alpha};
         const int units = EPI == EPI_SWIGLU ? w.rows / 2 : w.rows;  // one unit per warp, 8 warps
@@ -507,7 +532,7 @@ static void launch_q(jdg_engine *e, const QW &w, const float *X, int ldx, int M,
         case JD_Q4_K: k_qgemv<12, EPI><<<grid, 256, sm, e->st>>>(a); break;
         default: k_qgemv<0, EPI><<<grid, 256, sm, e->st>>>(a); break;
         }
-    } else if (w.dt == JD_Q4_K && w.cols % 256 == 0 && priv(e) && priv(e)->xprep) {
+    } else if (tc) {
         // tensor cores (tcgen05): 32 tokens per launch
         const QmMaps *maps = qm_find_maps(e, w);
         if (!maps) {
@@ -518,7 +543,8 @@ static void launch_q(jdg_engine *e, const QW &w, const float *X, int ldx, int M,
         }
         for (int t0 = 0; t0 < M; t0 += kQmTok) {
             const int mt = std::min(kQmTok, M - t0);
-            k_qm_prep_x<<<w.cols / 256, 256, 0, e->st>>>(X + (size_t)t0 * ldx, ldx, mt, w.cols, priv(e)->xprep);
+            k_qm_prep_tok<<<kQmTok, 256, 0, e->st>>>(X + (size_t)t0 * ldx, ldx, mt, w.cols, do_norm, norm_w, e->eps,
+                                                     xn_out ? xn_out + (size_t)t0 * ldx : nullptr, priv(e)->xprep);
             QmArgs q = {};
             q.w = w;
             q.xprep = priv(e)->xprep;
@@ -579,6 +605,13 @@ int jdg_host_set_attrs(jdg_engine *e) {
 #undef SETA
     if (cudaFuncSetAttribute(k_qm_q4k, cudaFuncAttributeMaxDynamicSharedMemorySize, kQmSmem) != cudaSuccess) {
         jdg_set_err(e->ctx, "cannot reserve %d bytes of shared memory for the tensor-core GEMM", kQmSmem);
+        return JD_ECUDA;
+    }
+    if (cudaFuncSetAttribute(k_hpar_dots, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hpar_dots_smem(20)) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(k_hpar_apply, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hpar_apply_smem(kMaxE, 20)) !=
+            cudaSuccess) {
+        jdg_set_err(e->ctx, "cannot reserve shared memory for the parliament kernel");
         return JD_ECUDA;
     }
     return JD_OK;
@@ -709,11 +742,10 @@ int jdg_enqueue_host_step(jdg_engine *e, int B) {
     const float scale = 1.0f / sqrtf((float)e->HD);
     k_embed<<<B, 256, 0, e->st>>>(e->tok_emb, e->V, D, e->tok, e->x, e->err);
     e->launches++;
+    const bool hpar = hp->hpar_part && B <= kHparTok;
     for (int l = 0; l < L; l++) {
         HostLayerDev &hl = e->hl[l];
-        k_rmsnorm<<<B, 256, 0, e->st>>>(e->x, hl.attn_norm, e->xn, D, e->eps);
-        e->launches++;
-        launch_q<EPI_STORE>(e, hp->wqkv[l], e->xn, D, B, e->qkv, e->qkvd, 1.f);
+        launch_q<EPI_STORE>(e, hp->wqkv[l], e->x, D, B, e->qkv, e->qkvd, 1.f, 1, hl.attn_norm, e->xn);
         jdg_launch_rope(e, l, B);
         jdg_launch_attention(e, l, B, scale, 1.0f + hl.attn_bias);
         if (!tp) {
@@ -724,9 +756,7 @@ int jdg_enqueue_host_step(jdg_engine *e, int B) {
             k_add<<<(unsigned)(((size_t)B * D + 255) / 256), 256, 0, e->st>>>(e->x, hp->partial, (size_t)B * D);
             e->launches++;
         }
-        k_rmsnorm<<<B, 256, 0, e->st>>>(e->x, hl.ffn_norm, e->xb, D, e->eps);
-        e->launches++;
-        launch_q<EPI_SWIGLU>(e, hp->gu[l], e->xb, D, B, e->hbuf, e->hidden, 1.f);
+        launch_q<EPI_SWIGLU>(e, hp->gu[l], e->x, D, B, e->hbuf, e->hidden, 1.f, 1, hl.ffn_norm);
         if (!tp) {
             launch_q<EPI_ADD>(e, hp->dn[l], e->hbuf, e->hidden, B, e->x, D, hl.focus);
         } else {
@@ -736,6 +766,21 @@ int jdg_enqueue_host_step(jdg_engine *e, int B) {
             e->launches++;
         }
         // LoRA parliament on xn (janusdoe.c:3281-3303)
+        if (hpar && e->n_alive[l] > 0) {
+            HParArgs pa;
+            pa.D = D; pa.R = e->lora_rank; pa.B = B; pa.L = L; pa.l = l;
+            pa.xn = e->xn; pa.w_vote = hl.w_vote; pa.lora_A = hp->lora_A[l]; pa.lora_B = hp->lora_B[l];
+            pa.alive = hl.alive; pa.alive_list = hp->alive_list[l]; pa.n_alive = e->n_alive[l];
+            pa.part = hp->hpar_part; pa.tickets = hp->hpar_tickets;
+            pa.votes = hp->hpar_votes; pa.tall = hp->hpar_tall;
+            pa.kcnt = e->kcnt; pa.sel = e->sel; pa.selw = e->selw; pa.consensus = e->consensus;
+            pa.tr_k = e->tr_k; pa.tr_sel = e->tr_sel; pa.tr_w = e->tr_w; pa.tr_ema = e->tr_ema;
+            pa.lora_alpha = e->lora_alpha; pa.x = e->x;
+            k_hpar_dots<<<dim3(D / 256, e->n_alive[l]), 256, hpar_dots_smem(pa.R), e->st>>>(pa);
+            k_hpar_apply<<<(D + 31) / 32, 256, hpar_apply_smem(e->n_alive[l], pa.R), e->st>>>(pa);
+            e->launches += 2;
+            continue;
+        }
         jdg_launch_elect(e, l, B, e->xn, nullptr, hl.w_vote, hl.alive, 0.f, 1);
         if (e->n_alive[l] > 0) {
             k_lora_t<<<dim3(e->lora_rank, e->n_alive[l], B), 256, 0, e->st>>>(hp->lora_B[l], e->lora_rank, D, e->kcnt,
@@ -745,13 +790,11 @@ int jdg_enqueue_host_step(jdg_engine *e, int B) {
             e->launches += 2;
         }
     }
-    k_rmsnorm<<<B, 256, 0, e->st>>>(e->x, e->output_norm, e->xb, D, e->eps);
-    e->launches++;
     if (!tp) {
-        launch_q<EPI_STORE>(e, hp->out, e->xb, D, B, e->logits, hp->V_loc, 1.f);
+        launch_q<EPI_STORE>(e, hp->out, e->x, D, B, e->logits, hp->V_loc, 1.f, 1, e->output_norm);
         jdg_launch_pick(e, B);
     } else {
-        launch_q<EPI_STORE>(e, hp->out, e->xb, D, B, e->logits, hp->V_loc, 1.f);
+        launch_q<EPI_STORE>(e, hp->out, e->x, D, B, e->logits, hp->V_loc, 1.f, 1, e->output_norm);
         k_argmax_part<<<B, 1024, 0, e->st>>>(e->logits, hp->V_loc, hp->V_loc, hp->V_off, hp->amx_v_loc, hp->amx_i_loc);
         ncclAllGather(hp->amx_v_loc, hp->amx_v, B, ncclFloat, hp->comm, e->st);
         ncclAllGather(hp->amx_i_loc, hp->amx_i, B, ncclInt32, hp->comm, e->st);

@@ -32,8 +32,19 @@ static __global__ void k_rmsnorm(const float *__restrict__ x, const float *__res
     __shared__ float red[32];
     int b = blockIdx.x;
     const float *xr = x + (size_t)b * D;
+    // elements tid, tid + blockDim, ... in order, eight loads in flight
     float ss = 0.f;
-    for (int i = threadIdx.x; i < D; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+    for (int base = 0; base < D; base += blockDim.x * 8) {
+        float v[8];
+#pragma unroll
+        for (int m = 0; m < 8; m++) {
+            const int i = base + threadIdx.x + blockDim.x * m;
+            v[m] = i < D ? xr[i] : 0.f;
+        }
+#pragma unroll
+        for (int m = 0; m < 8; m++)
+            if (base + threadIdx.x + blockDim.x * m < D) ss = fmaf(v[m], v[m], ss);
+    }
     ss = block_sum(ss, red);
     float inv = 1.0f / sqrtf(ss / (float)D + eps);
     float *o = out + (size_t)b * D;
@@ -529,8 +540,19 @@ static __global__ __launch_bounds__(256) void k_elect(ElectArgs a) {
     const int b = blockIdx.x, D = a.D;
     const float *xr = a.x + (size_t)b * D;
     if (!a.host) {
+        // elements tid, tid + blockDim, ... in order, eight loads in flight
         float ss = 0.f;
-        for (int i = threadIdx.x; i < D; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+        for (int base = 0; base < D; base += blockDim.x * 8) {
+            float v[8];
+#pragma unroll
+            for (int m = 0; m < 8; m++) {
+                const int i = base + threadIdx.x + blockDim.x * m;
+                v[m] = i < D ? xr[i] : 0.f;
+            }
+#pragma unroll
+            for (int m = 0; m < 8; m++)
+                if (base + threadIdx.x + blockDim.x * m < D) ss = fmaf(v[m], v[m], ss);
+        }
         ss = block_sum(ss, red);
         float inv = 1.0f / sqrtf(ss / (float)D + a.eps);
         for (int i = threadIdx.x; i < D; i += blockDim.x) {
@@ -547,7 +569,19 @@ static __global__ __launch_bounds__(256) void k_elect(ElectArgs a) {
         if (!a.alive[e]) continue;
         const float *wr = a.w_vote + (size_t)e * D;
         float d = 0.f;
-        for (int i = lane; i < D; i += 32) d = fmaf(wr[i], xs[i], d);
+        for (int base = 0; base < D; base += 32 * 8) {  // in order, eight loads in flight
+            float v[8];
+#pragma unroll
+            for (int m = 0; m < 8; m++) {
+                const int i = base + lane + 32 * m;
+                v[m] = i < D ? wr[i] : 0.f;
+            }
+#pragma unroll
+            for (int m = 0; m < 8; m++) {
+                const int i = base + lane + 32 * m;
+                if (i < D) d = fmaf(v[m], xs[i], d);
+            }
+        }
         d = warp_sum(d);
         if (lane == 0) votes[e] = d;
     }

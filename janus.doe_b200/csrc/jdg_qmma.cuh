@@ -196,47 +196,6 @@ __device__ __forceinline__ uint32_t qm_split2(float v0, float v1, bool lo) {
     return (uint32_t)__half_as_ushort(r0) | ((uint32_t)__half_as_ushort(r1) << 16);
 }
 
-// X [M][K] f32 -> prepared activations per superblock: B = fp16 hi/lo of x (rows 0..31 /
-// 32..63, zero for t >= M) in the core-matrix layout and tensor-core K order, then B_min =
-// fp16 hi/lo of the 8 sub-block sums (f32, index order) in K columns 0..7, zeros in 8..15.
-// grid (K/256), block 256: the 32 x 256 tile is staged in shared memory first.
-static __global__ __launch_bounds__(256) void k_qm_prep_x(const float *__restrict__ X, int ldx, int M, int K,
-                                                          uint8_t *__restrict__ out) {
-    __shared__ float xt[kQmTok][257];
-    __shared__ float sums[kQmTok][9];
-    const int sb = blockIdx.x, tid = threadIdx.x;
-    for (int t = 0; t < kQmTok; t++) xt[t][tid] = t < M ? X[(size_t)t * ldx + sb * 256 + tid] : 0.f;
-    __syncthreads();
-    uint8_t *o = out + (size_t)sb * kQmBBytes;
-    {
-        const int t = tid & 31, j = tid >> 5;
-        float sm = 0.f;
-        for (int i = 0; i < 32; i++) sm += xt[t][32 * j + i];
-        sums[t][j] = sm;
-    }
-    // 64 rows x 32 chunks of 8 (K positions 8c..8c+7 in tensor-core order)
-    for (int idx = tid; idx < kQmN * 32; idx += 256) {
-        const int row = idx % kQmN, c = idx / kQmN, t = row % kQmTok;
-        const bool lo = row >= kQmTok;
-        uint32_t v[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) v[i] = qm_split2(xt[t][qm_kperm(c * 8 + 2 * i)], xt[t][qm_kperm(c * 8 + 2 * i + 1)], lo);
-        *reinterpret_cast<uint4 *>(o + ((size_t)(c * (kQmN / 8) + row / 8) * 8 + row % 8) * 16) = make_uint4(v[0], v[1], v[2], v[3]);
-    }
-    __syncthreads();
-    // B_min: 64 rows x 2 chunks; chunk 0 holds the 8 sub-block sums, chunk 1 zeros
-    if (tid < kQmN * 2) {
-        const int row = tid % kQmN, c = tid / kQmN, t = row % kQmTok;
-        const bool lo = row >= kQmTok;
-        uint32_t v[4] = {0, 0, 0, 0};
-        if (c == 0)
-#pragma unroll
-            for (int i = 0; i < 4; i++) v[i] = qm_split2(sums[t][2 * i], sums[t][2 * i + 1], lo);
-        *reinterpret_cast<uint4 *>(o + kQmBMain + ((size_t)(c * (kQmN / 8) + row / 8) * 8 + row % 8) * 16) =
-            make_uint4(v[0], v[1], v[2], v[3]);
-    }
-}
-
 // Byte i (0..15) of a 16-byte Q4_K superblock header held in registers.
 __device__ __forceinline__ uint32_t hdr_byte(const uint4 &h, int i) {
     const uint32_t w = i < 4 ? h.x : i < 8 ? h.y : i < 12 ? h.z : h.w;
