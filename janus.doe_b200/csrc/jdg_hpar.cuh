@@ -10,105 +10,112 @@ namespace jdg {
 // x -> (optionally RMS-normed, janusdoe.c:504 / 3196-3199) -> prepared activations of
 // k_qm_q4k: the fp16 hi/lo rows t and 32 + t of every superblock's B tile (tensor-core K
 // order) and of its B_min tile (the 8 sub-block sums).  grid 32: CTA t handles token slot t
-// (slots >= M write zeros), block 256.  The norm matches k_rmsnorm bit for bit: the same
-// thread-strided sum of squares and block reduction, then (x * inv) * w; norm_w null = ones.
-// xn_out (optional) receives the normed rows.
+// (slots >= M write zeros), block 256.  Norm: inv = 1/sqrt(mean(x^2) + eps) (each thread sums
+// its 8-element groups in order, then the block), v = (x * inv) * w; norm_w null = ones.
+// xn_out (optional) receives the normed rows.  Thread tid owns the groups g = tid + 256 m of
+// 8 consecutive K positions (one 16-byte core-matrix row piece); a warp covers the 32 groups
+// of one superblock, lanes 4j..4j+3 its sub-block j.  Loads go out in batches of 8 groups.
+constexpr int kPrepBatch = 8;
 static __global__ __launch_bounds__(256) void k_qm_prep_tok(const float *__restrict__ X, int ldx, int M, int K, int do_norm,
                                                             const float *__restrict__ norm_w, float eps,
                                                             float *__restrict__ xn_out, uint8_t *__restrict__ out) {
     __shared__ float red[32];
-    const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
+    const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, ng = K / 8;
     const bool live = t < M;
     const float *xr = X + (size_t)t * ldx;
     float inv = 1.f;
     if (live && do_norm) {
-        // elements tid, tid + 256, ... in order (as k_rmsnorm), eight loads in flight
         float ss = 0.f;
-        for (int base = 0; base < K; base += 256 * 8) {
-            float v[8];
+        for (int g0 = tid; g0 < ng; g0 += 256 * kPrepBatch) {
+            float4 xa[kPrepBatch], xb[kPrepBatch];
 #pragma unroll
-            for (int m = 0; m < 8; m++) {
-                const int i = base + tid + 256 * m;
-                v[m] = i < K ? xr[i] : 0.f;
+            for (int m = 0; m < kPrepBatch; m++) {
+                const int g = g0 + 256 * m;
+                if (g < ng) {
+                    xa[m] = *reinterpret_cast<const float4 *>(xr + 8 * g);
+                    xb[m] = *reinterpret_cast<const float4 *>(xr + 8 * g + 4);
+                }
             }
 #pragma unroll
-            for (int m = 0; m < 8; m++)
-                if (base + tid + 256 * m < K) ss = fmaf(v[m], v[m], ss);
+            for (int m = 0; m < kPrepBatch; m++)
+                if (g0 + 256 * m < ng) {
+                    ss = fmaf(xa[m].x, xa[m].x, ss); ss = fmaf(xa[m].y, xa[m].y, ss);
+                    ss = fmaf(xa[m].z, xa[m].z, ss); ss = fmaf(xa[m].w, xa[m].w, ss);
+                    ss = fmaf(xb[m].x, xb[m].x, ss); ss = fmaf(xb[m].y, xb[m].y, ss);
+                    ss = fmaf(xb[m].z, xb[m].z, ss); ss = fmaf(xb[m].w, xb[m].w, ss);
+                }
         }
         ss = block_sum(ss, red);
         inv = 1.0f / sqrtf(ss / (float)K + eps);
     }
-    // group g = 8 consecutive K positions = one 16-byte core-matrix row piece; a warp covers
-    // the 32 groups of one superblock, lanes 4j..4j+3 its sub-block j.  The next group's loads
-    // are issued before this one is processed.
-    float4 na = make_float4(0.f, 0.f, 0.f, 0.f), nb = na, nwa = make_float4(1.f, 1.f, 1.f, 1.f), nwb = nwa;
-    auto fetch = [&](int g) {
-        if (live && g < K / 8) {
-            na = *reinterpret_cast<const float4 *>(xr + 8 * g);
-            nb = *reinterpret_cast<const float4 *>(xr + 8 * g + 4);
-            if (do_norm && norm_w) {
-                nwa = *reinterpret_cast<const float4 *>(norm_w + 8 * g);
-                nwb = *reinterpret_cast<const float4 *>(norm_w + 8 * g + 4);
+    for (int g0 = tid; g0 < ng; g0 += 256 * kPrepBatch) {
+        float4 xa[kPrepBatch], xb[kPrepBatch], wa[kPrepBatch], wb[kPrepBatch];
+#pragma unroll
+        for (int m = 0; m < kPrepBatch; m++) {
+            const int g = g0 + 256 * m;
+            xa[m] = xb[m] = make_float4(0.f, 0.f, 0.f, 0.f);
+            wa[m] = wb[m] = make_float4(1.f, 1.f, 1.f, 1.f);
+            if (live && g < ng) {
+                xa[m] = *reinterpret_cast<const float4 *>(xr + 8 * g);
+                xb[m] = *reinterpret_cast<const float4 *>(xr + 8 * g + 4);
+                if (do_norm && norm_w) {
+                    wa[m] = *reinterpret_cast<const float4 *>(norm_w + 8 * g);
+                    wb[m] = *reinterpret_cast<const float4 *>(norm_w + 8 * g + 4);
+                }
             }
         }
-    };
-    fetch(tid);
-    for (int g = tid; g < K / 8; g += blockDim.x) {
-        const int sb = g / 32, c = g % 32;
-        float v[8];
-        const float4 a = na, b = nb, wa = nwa, wb = nwb;
-        fetch(g + blockDim.x);
-        if (live) {
-            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-            if (do_norm) {
-                const float w8[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+        for (int m = 0; m < kPrepBatch; m++) {
+            const int g = g0 + 256 * m;
+            if (g >= ng) break;  // warp-uniform: ng is a multiple of 32
+            const int sb = g / 32, c = g % 32;
+            float v[8] = {xa[m].x, xa[m].y, xa[m].z, xa[m].w, xb[m].x, xb[m].y, xb[m].z, xb[m].w};
+            if (live && do_norm) {
+                const float w8[8] = {wa[m].x, wa[m].y, wa[m].z, wa[m].w, wb[m].x, wb[m].y, wb[m].z, wb[m].w};
 #pragma unroll
                 for (int i = 0; i < 8; i++) {
                     v[i] = __fmul_rn(v[i], inv);
                     if (norm_w) v[i] = __fmul_rn(v[i], w8[i]);
                 }
             }
-            if (xn_out) {
+            if (live && xn_out) {
                 float *o = xn_out + (size_t)t * ldx + 8 * g;
                 *reinterpret_cast<float4 *>(o) = make_float4(v[0], v[1], v[2], v[3]);
                 *reinterpret_cast<float4 *>(o + 4) = make_float4(v[4], v[5], v[6], v[7]);
             }
-        } else {
-#pragma unroll
-            for (int i = 0; i < 8; i++) v[i] = 0.f;
-        }
-        uint8_t *tile = out + (size_t)sb * kQmBBytes;
-        uint32_t hi[4], lo[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const float a0 = v[qm_kperm(2 * i)], a1 = v[qm_kperm(2 * i + 1)];
-            hi[i] = qm_split2(a0, a1, false);
-            lo[i] = qm_split2(a0, a1, true);
-        }
-        *reinterpret_cast<uint4 *>(tile + ((size_t)(c * (kQmN / 8) + t / 8) * 8 + t % 8) * 16) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        const int tl = kQmTok + t;
-        *reinterpret_cast<uint4 *>(tile + ((size_t)(c * (kQmN / 8) + tl / 8) * 8 + tl % 8) * 16) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-        // sub-block sums: 8 values here, then the 4 lanes of the sub-block
-        float s = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; i++) s += v[i];
-        s += __shfl_xor_sync(JDG_FULL, s, 1);
-        s += __shfl_xor_sync(JDG_FULL, s, 2);
-        float sj[8];
-#pragma unroll
-        for (int j = 0; j < 8; j++) sj[j] = __shfl_sync(JDG_FULL, s, 4 * j);
-        if (lane == 0) {
-            uint8_t *bm = tile + kQmBMain;
-            uint32_t h[4], l[4];
+            uint8_t *tile = out + (size_t)sb * kQmBBytes;
+            uint32_t hi[4], lo[4];
 #pragma unroll
             for (int i = 0; i < 4; i++) {
-                h[i] = qm_split2(sj[2 * i], sj[2 * i + 1], false);
-                l[i] = qm_split2(sj[2 * i], sj[2 * i + 1], true);
+                const float a0 = v[qm_kperm(2 * i)], a1 = v[qm_kperm(2 * i + 1)];
+                hi[i] = qm_split2(a0, a1, false);
+                lo[i] = qm_split2(a0, a1, true);
             }
-            *reinterpret_cast<uint4 *>(bm + ((size_t)(0 * (kQmN / 8) + t / 8) * 8 + t % 8) * 16) = make_uint4(h[0], h[1], h[2], h[3]);
-            *reinterpret_cast<uint4 *>(bm + ((size_t)(0 * (kQmN / 8) + tl / 8) * 8 + tl % 8) * 16) = make_uint4(l[0], l[1], l[2], l[3]);
-            *reinterpret_cast<uint4 *>(bm + ((size_t)(1 * (kQmN / 8) + t / 8) * 8 + t % 8) * 16) = make_uint4(0, 0, 0, 0);
-            *reinterpret_cast<uint4 *>(bm + ((size_t)(1 * (kQmN / 8) + tl / 8) * 8 + tl % 8) * 16) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4 *>(tile + ((size_t)(c * (kQmN / 8) + t / 8) * 8 + t % 8) * 16) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            const int tl = kQmTok + t;
+            *reinterpret_cast<uint4 *>(tile + ((size_t)(c * (kQmN / 8) + tl / 8) * 8 + tl % 8) * 16) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            // sub-block sums: 8 values here, then the 4 lanes of the sub-block
+            float s = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; i++) s += v[i];
+            s += __shfl_xor_sync(JDG_FULL, s, 1);
+            s += __shfl_xor_sync(JDG_FULL, s, 2);
+            float sj[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) sj[j] = __shfl_sync(JDG_FULL, s, 4 * j);
+            if (lane == 0) {
+                uint8_t *bm = tile + kQmBMain;
+                uint32_t h[4], l[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    h[i] = qm_split2(sj[2 * i], sj[2 * i + 1], false);
+                    l[i] = qm_split2(sj[2 * i], sj[2 * i + 1], true);
+                }
+                *reinterpret_cast<uint4 *>(bm + ((size_t)(0 * (kQmN / 8) + t / 8) * 8 + t % 8) * 16) = make_uint4(h[0], h[1], h[2], h[3]);
+                *reinterpret_cast<uint4 *>(bm + ((size_t)(0 * (kQmN / 8) + tl / 8) * 8 + tl % 8) * 16) = make_uint4(l[0], l[1], l[2], l[3]);
+                *reinterpret_cast<uint4 *>(bm + ((size_t)(1 * (kQmN / 8) + t / 8) * 8 + t % 8) * 16) = make_uint4(0, 0, 0, 0);
+                *reinterpret_cast<uint4 *>(bm + ((size_t)(1 * (kQmN / 8) + tl / 8) * 8 + tl % 8) * 16) = make_uint4(0, 0, 0, 0);
+            }
         }
     }
 }
@@ -153,14 +160,33 @@ static __global__ __launch_bounds__(256) void k_hpar_dots(HParArgs a) {
     __shared__ unsigned s_last;
     const int kc = blockIdx.x, ei = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int e = a.alive_list[ei], R = a.R, nrow = R + 1, k0 = kc * 256;
-    for (int i = tid; i < a.B * 64; i += 256) {
-        const int b = i / 64, q = i % 64;
-        *reinterpret_cast<float4 *>(&xs[b][4 * q]) = *reinterpret_cast<const float4 *>(a.xn + (size_t)b * a.D + k0 + 4 * q);
-    }
-    for (int i = tid; i < nrow * 64; i += 256) {
-        const int r = i / 64, q = i % 64;
-        const float *src = r == 0 ? a.w_vote + (size_t)e * a.D : a.lora_B + ((size_t)e * R + (r - 1)) * a.D;
-        *reinterpret_cast<float4 *>(&ws[r][4 * q]) = *reinterpret_cast<const float4 *>(src + k0 + 4 * q);
+    {
+        // every load of the staging issued before the first store (B <= 32: 8 float4 of
+        // activations per thread; R + 1 <= 21: 6 float4 of weight rows)
+        float4 xv[8], wv[6];
+#pragma unroll
+        for (int m = 0; m < 8; m++) {
+            const int i = tid + 256 * m, b = i / 64, q = i % 64;
+            if (i < a.B * 64) xv[m] = *reinterpret_cast<const float4 *>(a.xn + (size_t)b * a.D + k0 + 4 * q);
+        }
+#pragma unroll
+        for (int m = 0; m < 6; m++) {
+            const int i = tid + 256 * m, r = i / 64, q = i % 64;
+            if (i < nrow * 64) {
+                const float *src = r == 0 ? a.w_vote + (size_t)e * a.D : a.lora_B + ((size_t)e * R + (r - 1)) * a.D;
+                wv[m] = *reinterpret_cast<const float4 *>(src + k0 + 4 * q);
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < 8; m++) {
+            const int i = tid + 256 * m;
+            if (i < a.B * 64) *reinterpret_cast<float4 *>(&xs[i / 64][4 * (i % 64)]) = xv[m];
+        }
+#pragma unroll
+        for (int m = 0; m < 6; m++) {
+            const int i = tid + 256 * m;
+            if (i < nrow * 64) *reinterpret_cast<float4 *>(&ws[i / 64][4 * (i % 64)]) = wv[m];
+        }
     }
     __syncthreads();
     // lane = sequence, warp w takes rows w, w + 8, w + 16
@@ -250,16 +276,31 @@ static __global__ __launch_bounds__(256) void k_hpar_apply(HParArgs a) {
     if (tid < kMaxE) slot[tid] = -1;
     __syncthreads();
     if (tid < na) slot[a.alive_list[tid]] = tid;
-    for (int idx = tid; idx < na * 8 * R; idx += 256) {  // float4 units
-        const int ei = idx / (8 * R), rem = idx % (8 * R);
-        if (i0 + (4 * rem) / R < a.D)
-            reinterpret_cast<float4 *>(as)[idx] =
-                *reinterpret_cast<const float4 *>(a.lora_A + ((size_t)a.alive_list[ei] * a.D + i0) * R + 4 * rem);
-    }
-    for (int idx = tid; idx < a.B * na * (R / 4); idx += 256) {
-        const int b = idx / (na * (R / 4)), rem = idx % (na * (R / 4)), ei = rem / (R / 4), q = rem % (R / 4);
-        reinterpret_cast<float4 *>(ts)[idx] =
-            __ldcg(reinterpret_cast<const float4 *>(a.tall + ((size_t)b * kMaxE + a.alive_list[ei]) * R) + q);
+    // staging in float4 units, eight loads in flight per thread before their stores
+    const int nA = na * 8 * R, nT = a.B * na * (R / 4);
+    for (int base = 0; base < nA + nT; base += 256 * 8) {
+        float4 v[8];
+#pragma unroll
+        for (int m = 0; m < 8; m++) {
+            const int idx = base + tid + 256 * m;
+            if (idx < nA) {
+                const int ei = idx / (8 * R), rem = idx % (8 * R);
+                if (i0 + (4 * rem) / R < a.D)
+                    v[m] = *reinterpret_cast<const float4 *>(a.lora_A + ((size_t)a.alive_list[ei] * a.D + i0) * R + 4 * rem);
+            } else if (idx < nA + nT) {
+                const int j = idx - nA, b = j / (na * (R / 4)), rem = j % (na * (R / 4)), ei = rem / (R / 4), q = rem % (R / 4);
+                v[m] = __ldcg(reinterpret_cast<const float4 *>(a.tall + ((size_t)b * kMaxE + a.alive_list[ei]) * R) + q);
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < 8; m++) {
+            const int idx = base + tid + 256 * m;
+            if (idx < nA) {
+                if (i0 + (4 * (idx % (8 * R))) / R < a.D) reinterpret_cast<float4 *>(as)[idx] = v[m];
+            } else if (idx < nA + nT) {
+                reinterpret_cast<float4 *>(ts)[idx - nA] = v[m];
+            }
+        }
     }
     __syncthreads();
     const int b = tid >> 3, q = tid & 7;
