@@ -310,31 +310,47 @@ static __global__ __launch_bounds__(128) void k_hb1_attn(B1Args ab, HB1Args a) {
 // The host election (janusdoe.c:3054-3087) on one thread: alive list ascending; na == 1
 // takes that expert with weight 1 and leaves the EMA alone; top-k by strict '>' with the
 // next unused alive expert when none beats -1e30; softmax without temperature, uniform
-// weights when the sum is not finite and positive.
+// weights when the sum is not finite and positive.  Every loop runs over the 16 expert
+// slots unrolled with the alive mask (ascending order, the reference's operation order), so
+// the votes, selection and weights stay in registers.
 static __device__ void hb1_elect_serial(const HB1Args &a) {
-    int idx[kMaxE], na = 0;
+    unsigned alive = 0;
+    int na = 0, first = -1;
+#pragma unroll
     for (int e = 0; e < kMaxE; e++)
-        if (a.alive[e]) idx[na++] = e;
+        if (a.alive[e]) {
+            alive |= 1u << e;
+            if (first < 0) first = e;
+            na++;
+        }
     float *cons = a.consensus + a.l;
     int k = 0, sel[kMaxE];
     float w[kMaxE];
+#pragma unroll
+    for (int i = 0; i < kMaxE; i++) {
+        sel[i] = -1;
+        w[i] = 0.f;
+    }
     if (na == 1) {
         k = 1;
-        sel[0] = idx[0];
+        sel[0] = first;
         w[0] = 1.0f;
     } else if (na >= 2) {
-        // all 16 votes in one pass (independent loads; dead experts' entries are not used)
         float v[kMaxE];
 #pragma unroll
         for (int e = 0; e < kMaxE; e++) v[e] = __ldcg(a.votes + e);
         float mean = 0.f;
-        for (int i = 0; i < na; i++) mean = __fadd_rn(mean, v[idx[i]]);
+#pragma unroll
+        for (int e = 0; e < kMaxE; e++)
+            if (alive >> e & 1u) mean = __fadd_rn(mean, v[e]);
         mean = mean / (float)na;
         float var = 0.f;
-        for (int i = 0; i < na; i++) {
-            const float dd = __fsub_rn(v[idx[i]], mean);
-            var = __fadd_rn(var, __fmul_rn(dd, dd));
-        }
+#pragma unroll
+        for (int e = 0; e < kMaxE; e++)
+            if (alive >> e & 1u) {
+                const float dd = __fsub_rn(v[e], mean);
+                var = __fadd_rn(var, __fmul_rn(dd, dd));
+            }
         var = var / (float)na;
         const float cs = fminf(1.0f, sqrtf(__fadd_rn(var, 1e-8f)) / __fadd_rn(fabsf(mean), 1.0f));
         const float ema = __fadd_rn(__fmul_rn(0.9f, *cons), __fmul_rn(0.1f, cs));
@@ -343,42 +359,46 @@ static __device__ void hb1_elect_serial(const HB1Args &a) {
         if (k < 2) k = 2;
         if (k > na) k = na;
         unsigned used = 0;
-        for (int ki = 0; ki < k; ki++) {
-            float bv = -1e30f;
-            int bi = -1;
-            for (int i = 0; i < na; i++) {
-                const int e = idx[i];
-                if (!(used >> e & 1u) && v[e] > bv) {
-                    bv = v[e];
-                    bi = e;
-                }
-            }
-            if (bi < 0)
-                for (int i = 0; i < na; i++)
-                    if (!(used >> idx[i] & 1u)) {
-                        bi = idx[i];
-                        break;
+#pragma unroll
+        for (int ki = 0; ki < kMaxE; ki++) {
+            if (ki < k) {
+                float bv = -1e30f, bw = 0.f;
+                int bi = -1;
+#pragma unroll
+                for (int e = 0; e < kMaxE; e++)
+                    if ((alive & ~used) >> e & 1u && v[e] > bv) {
+                        bv = v[e];
+                        bi = e;
                     }
-            sel[ki] = bi;
-            w[ki] = v[bi];
-            used |= 1u << bi;
+                if (bi < 0) bi = __ffs(alive & ~used) - 1;  // the next unused alive expert
+#pragma unroll
+                for (int e = 0; e < kMaxE; e++)
+                    if (e == bi) bw = v[e];
+                sel[ki] = bi;
+                w[ki] = bw;
+                used |= 1u << bi;
+            }
         }
         float mx = w[0];
-        for (int i = 1; i < k; i++)
-            if (w[i] > mx) mx = w[i];
+#pragma unroll
+        for (int i = 1; i < kMaxE; i++)
+            if (i < k && w[i] > mx) mx = w[i];
         float sum = 0.f;
-        for (int i = 0; i < k; i++) {
-            w[i] = expf(__fsub_rn(w[i], mx));
-            sum = __fadd_rn(sum, w[i]);
-        }
-        if (sum > 0.0f && isfinite(sum))
-            for (int i = 0; i < k; i++) w[i] = w[i] / sum;
-        else
-            for (int i = 0; i < k; i++) w[i] = 1.0f / (float)k;
+#pragma unroll
+        for (int i = 0; i < kMaxE; i++)
+            if (i < k) {
+                w[i] = expf(__fsub_rn(w[i], mx));
+                sum = __fadd_rn(sum, w[i]);
+            }
+        const bool ok = sum > 0.0f && isfinite(sum);
+#pragma unroll
+        for (int i = 0; i < kMaxE; i++)
+            if (i < k) w[i] = ok ? w[i] / sum : 1.0f / (float)k;
     }
     a.kcnt[0] = k;
     a.tr_k[a.l] = k;
     a.tr_ema[a.l] = *cons;
+#pragma unroll
     for (int i = 0; i < kMaxE; i++) {
         a.sel[i] = i < k ? sel[i] : -1;
         a.selw[i] = i < k ? w[i] : 0.f;

@@ -9,7 +9,7 @@ namespace jdg {
 // ---------------------------------------------------------------------------------
 // x -> (optionally RMS-normed, janusdoe.c:504 / 3196-3199) -> prepared activations of
 // k_qm_q4k: the fp16 hi/lo rows t and 32 + t of every superblock's B tile (tensor-core K
-// order) and of its B_min tile (the 8 sub-block sums).  grid 32: CTA t handles token slot t
+// order) and row t of its B_min tile (the 8 sub-block sums, hi then lo along K).  grid 32: CTA t handles token slot t
 // (slots >= M write zeros), block 256.  Norm: inv = 1/sqrt(mean(x^2) + eps) (each thread sums
 // its 8-element groups in order, then the block), v = (x * inv) * w; norm_w null = ones.
 // xn_out (optional) receives the normed rows.  Thread tid owns the groups g = tid + 256 m of
@@ -111,10 +111,9 @@ static __global__ __launch_bounds__(256) void k_qm_prep_tok(const float *__restr
                     h[i] = qm_split2(sj[2 * i], sj[2 * i + 1], false);
                     l[i] = qm_split2(sj[2 * i], sj[2 * i + 1], true);
                 }
-                *reinterpret_cast<uint4 *>(bm + ((size_t)(0 * (kQmN / 8) + t / 8) * 8 + t % 8) * 16) = make_uint4(h[0], h[1], h[2], h[3]);
-                *reinterpret_cast<uint4 *>(bm + ((size_t)(0 * (kQmN / 8) + tl / 8) * 8 + tl % 8) * 16) = make_uint4(l[0], l[1], l[2], l[3]);
-                *reinterpret_cast<uint4 *>(bm + ((size_t)(1 * (kQmN / 8) + t / 8) * 8 + t % 8) * 16) = make_uint4(0, 0, 0, 0);
-                *reinterpret_cast<uint4 *>(bm + ((size_t)(1 * (kQmN / 8) + tl / 8) * 8 + tl % 8) * 16) = make_uint4(0, 0, 0, 0);
+                // B_min row t: K columns 0..7 the hi parts, 8..15 the lo parts
+                *reinterpret_cast<uint4 *>(bm + ((size_t)(0 * (kQmTok / 8) + t / 8) * 8 + t % 8) * 16) = make_uint4(h[0], h[1], h[2], h[3]);
+                *reinterpret_cast<uint4 *>(bm + ((size_t)(1 * (kQmTok / 8) + t / 8) * 8 + t % 8) * 16) = make_uint4(l[0], l[1], l[2], l[3]);
             }
         }
     }
@@ -272,8 +271,33 @@ static __global__ __launch_bounds__(256) void k_hpar_apply(HParArgs a) {
     float *as = hsm_apply;                     // [na][32][R]
     float *ts = hsm_apply + (size_t)na * 32 * R;  // [32][na][R]
     __shared__ int slot[kMaxE];                // expert id -> index in alive_list
+    __shared__ int s_sel[kHparTok][kMaxE], s_k[kHparTok];
+    __shared__ float s_w[kHparTok][kMaxE];
     const int i0 = blockIdx.x * 32, tid = threadIdx.x;
     if (tid < kMaxE) slot[tid] = -1;
+    {
+        // the elections of all sequences (2 entries per thread, loads before stores)
+        int sv[2] = {-1, -1}, kv = 0;
+        float wv[2] = {0.f, 0.f};
+#pragma unroll
+        for (int m = 0; m < 2; m++) {
+            const int i = tid + 256 * m;
+            if (i < a.B * kMaxE) {
+                sv[m] = a.sel[i];
+                wv[m] = a.selw[i];
+            }
+        }
+        if (tid < a.B) kv = a.kcnt[tid];
+#pragma unroll
+        for (int m = 0; m < 2; m++) {
+            const int i = tid + 256 * m;
+            if (i < a.B * kMaxE) {
+                s_sel[i / kMaxE][i % kMaxE] = sv[m];
+                s_w[i / kMaxE][i % kMaxE] = wv[m];
+            }
+        }
+        if (tid < a.B) s_k[tid] = kv;
+    }
     __syncthreads();
     if (tid < na) slot[a.alive_list[tid]] = tid;
     // staging in float4 units, eight loads in flight per thread before their stores
@@ -311,11 +335,11 @@ static __global__ __launch_bounds__(256) void k_hpar_apply(HParArgs a) {
         const int i = i0 + 4 * q + m;
         xi[m] = i < a.D ? a.x[(size_t)b * a.D + i] : 0.f;
     }
-    const int k = a.kcnt[b];
+    const int k = s_k[b];
     for (int ki = 0; ki < k; ki++) {
-        const int e = a.sel[b * kMaxE + ki], si = (e >= 0 && e < kMaxE) ? slot[e] : -1;
+        const int e = s_sel[b][ki], si = (e >= 0 && e < kMaxE) ? slot[e] : -1;
         if (si < 0) continue;  // the election only picks alive experts
-        const float w = __fmul_rn(a.lora_alpha, a.selw[b * kMaxE + ki]);
+        const float w = __fmul_rn(a.lora_alpha, s_w[b][ki]);
         const float *tr = ts + ((size_t)b * na + si) * R;
         float s[4] = {0.f, 0.f, 0.f, 0.f};
         for (int r = 0; r < R; r += 4) {

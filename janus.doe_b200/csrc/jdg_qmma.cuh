@@ -8,11 +8,12 @@
 //   * A = s_j * q is an integer <= 63 * 15 = 945: exact in fp16.
 //   * X is split into x_hi = fp16(x) and x_lo = fp16(x - x_hi); together they carry ~22
 //     mantissa bits.  B stacks them as 64 "columns": tokens 0..31 hi, then 0..31 lo.
-//   * The sub-block minimum becomes a second product: A_min[n][j] = m_j (integer <= 63),
-//     against the sums of x over each sub-block (hi/lo as well).
+//   * The sub-block minimum becomes a second product against the sums of x over each
+//     sub-block, split hi/lo along K: A_min[n] = (m_0..m_7, m_0..m_7) (integers <= 63),
+//     B_min[t] = (sum_hi_0..7, sum_lo_0..7), one 128x32x16 MMA.
 //   * Per superblock one TMEM region receives A.B (K = 256: 16 MMAs of 128x64x16) and
-//     A_min.B_min (K = 16, one MMA); the epilogue adds d_sb * (hi + lo) - dmin_sb * (hi + lo)
-//     of the two into f32 registers.  d and dmin stay f32 outside the tensor core.
+//     A_min.B_min; the epilogue adds d_sb * (hi + lo) - dmin_sb * min into f32 registers.
+//     d and dmin stay f32 outside the tensor core.
 //
 // CTA = 128 weight rows x all K (or a split of K), 23 warps:
 //   warps 0-15   producers: warp w fills TMEM lanes 32(w%4).. (its 32 rows, one per lane) for
@@ -25,9 +26,9 @@
 //   warp 18      TMA issuer (one thread): per superblock the code bytes (128 rows x 128 B,
 //                128-byte swizzle), the headers (128 x 16 B) and the prepared B tile (34 KB)
 //   warps 19-22  epilogue (TMEM lane quarter warp % 4)
-// Shared memory: kQmStages stages of one superblock.  TMEM (512 columns): four A stages of
+// Shared memory: kQmStages stages of one superblock.  TMEM (512 columns): five A stages of
 // half a superblock (64 columns: K 128 as fp16 pairs; warps w/4 = 2h, 2h+1 fill half h) and
-// two accumulator regions of 128 columns (A.B 64, A_min.B_min 64).
+// two accumulator regions of 96 columns (A.B 64, A_min.B_min 32).
 // Every mbarrier wait is bounded; on a timeout the CTA records JDG_ERR_TIMEOUT, waits
 // (bounded) for the copies and MMAs it issued, frees its tensor memory and returns.
 #pragma once
@@ -57,7 +58,7 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
-// tile (x, y) of a 2-D tensor map into shared memory (no multicast)
+// tile (x, y) of a 2-D tensor map into this CTA's shared memory
 __device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int x, int y, uint64_t *bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
@@ -91,8 +92,9 @@ constexpr int kQmRows = 128;             // weight rows per CTA (MMA M)
 constexpr int kQmTok = 32;               // tokens (B rows 0..31 hi, 32..63 lo)
 constexpr int kQmN = 2 * kQmTok;         // MMA N
 constexpr int kQmStages = 4;             // shared-memory stages, one superblock each
-constexpr int kQmAStages = 4;            // TMEM A stages of half a superblock (64 columns)
-constexpr int kQmRegions = 2;            // TMEM accumulator regions (128 columns)
+constexpr int kQmAStages = 5;            // TMEM A stages of half a superblock (64 columns)
+constexpr int kQmRegions = 2;            // TMEM accumulator regions (96 columns)
+constexpr int kQmRegionCols = 96;
 constexpr int kQmMaxSplit = 8;           // split-K ways at most
 constexpr int kQmProd = 16;              // producer warps
 constexpr int kQmMmaWarp = 16, kQmTmaWarp = 18;  // MMA issuers: warps 16, 17
@@ -101,11 +103,12 @@ constexpr int kQmCodes = kQmRows * 128;  // code bytes of one superblock
 constexpr int kQmHdr = kQmRows * 16;     // headers of one superblock
 constexpr int kQmAMin = kQmRows * 16 * 2;    // A_min of one superblock (fp16, core-matrix layout)
 constexpr int kQmBMain = kQmN * 256 * 2;     // B tile of one superblock (fp16, core-matrix layout)
-constexpr int kQmBMin = kQmN * 16 * 2;       // B_min: hi/lo of the sub-block sums
+constexpr int kQmBMin = kQmTok * 16 * 2;     // B_min: hi/lo of the sub-block sums along K
 constexpr int kQmBBytes = kQmBMain + kQmBMin;  // prepared activations per superblock in global memory
-constexpr int kQmStageBytes = kQmCodes + kQmHdr + kQmAMin + kQmBBytes;  // 57344 = 56 KB
+constexpr int kQmStageBytes = kQmCodes + kQmHdr + kQmAMin + kQmBBytes;  // 56320 = 55 KB
 constexpr int kQmSmem = 1024 + kQmStages * kQmStageBytes;
 constexpr uint32_t kQmRegionCol = kQmAStages * 64;  // first accumulator column
+static_assert(kQmRegionCol + kQmRegions * kQmRegionCols <= 512, "TMEM columns");
 
 // Core-matrix layout (K-major, no swizzle): 8 rows x 8 fp16 (16 bytes per row) = 128 bytes
 // contiguous; core matrix (row group g, K chunk c) at (c * G + g) * 128 bytes, G = rows/8.
@@ -114,8 +117,10 @@ __device__ __forceinline__ uint64_t qm_desc(uint32_t saddr, uint32_t lbo, uint32
     return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
            ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46);  // version 1, no swizzle
 }
-// kind::f16 instruction descriptor: D f32, A/B f16, both K-major, N = 64, M = 128
+// kind::f16 instruction descriptors: D f32, A/B f16, both K-major, M = 128, N = 64 (main) or
+// 32 (minimum)
 constexpr uint32_t kQmIdesc = (1u << 4) | ((uint32_t)(kQmN >> 3) << 17) | ((uint32_t)(kQmRows >> 4) << 24);
+constexpr uint32_t kQmIdescMin = (1u << 4) | ((uint32_t)(kQmTok >> 3) << 17) | ((uint32_t)(kQmRows >> 4) << 24);
 
 // tcgen05.mma with A in tensor memory (lane = row, K as fp16 pairs along the columns) and B
 // from a shared-memory descriptor
@@ -125,12 +130,12 @@ __device__ __forceinline__ void qm_mma_ts(uint32_t dtmem, uint32_t atmem, uint64
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p; }" ::"r"(dtmem),
         "r"(atmem), "l"(db), "r"(kQmIdesc), "r"(acc));
 }
-// tcgen05.mma with A and B from shared-memory descriptors
-__device__ __forceinline__ void qm_mma(uint32_t dtmem, uint64_t da, uint64_t db, uint32_t acc) {
+// tcgen05.mma with A and B from shared-memory descriptors (the 128x32x16 minimum product)
+__device__ __forceinline__ void qm_mma_min(uint32_t dtmem, uint64_t da, uint64_t db) {
     asm volatile(
-        "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(dtmem),
-        "l"(da), "l"(db), "r"(kQmIdesc), "r"(acc));
+        "{ .reg .pred p; setp.ne.b32 p, %3, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %4, p; }" ::"r"(dtmem),
+        "l"(da), "l"(db), "r"(0), "r"(kQmIdescMin));
 }
 __device__ __forceinline__ void qm_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -360,7 +365,7 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a, const
                 }
                 qm_st32(tmem + tlane + (uint32_t)(as * 64 + (KQ & 1) * 32), r);
                 if (KQ == 0) {
-                    // A_min row: m_0..m_7 in K columns 0..7, zeros in 8..15 (core-matrix layout)
+                    // A_min row: m_0..m_7 in K columns 0..7 and again in 8..15 (core-matrix layout)
                     int mj[8];
 #pragma unroll
                     for (int jj = 0; jj < 8; jj++) {
@@ -370,10 +375,10 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a, const
                     constexpr int G = kQmRows / 8;
                     uint8_t *An = st + kQmCodes + kQmHdr;
                     const int g = row >> 3, r0 = row & 7;
-                    *reinterpret_cast<uint4 *>(An + ((size_t)(0 * G + g) * 8 + r0) * 16) =
-                        make_uint4(half2_bits(mj[0], mj[1]), half2_bits(mj[2], mj[3]), half2_bits(mj[4], mj[5]),
-                                   half2_bits(mj[6], mj[7]));
-                    *reinterpret_cast<uint4 *>(An + ((size_t)(1 * G + g) * 8 + r0) * 16) = make_uint4(0, 0, 0, 0);
+                    const uint4 mrow = make_uint4(half2_bits(mj[0], mj[1]), half2_bits(mj[2], mj[3]),
+                                                  half2_bits(mj[4], mj[5]), half2_bits(mj[6], mj[7]));
+                    *reinterpret_cast<uint4 *>(An + ((size_t)(0 * G + g) * 8 + r0) * 16) = mrow;
+                    *reinterpret_cast<uint4 *>(An + ((size_t)(1 * G + g) * 8 + r0) * 16) = mrow;
                     // generic-proxy stores must be visible to the tensor core (async proxy)
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 }
@@ -393,7 +398,7 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a, const
         // ---------------- MMA issuers: superblocks i with i % 2 == warp - kQmMmaWarp ----------------
         pdl_trigger();
         if (lane == 0) {
-            constexpr int GA = kQmRows / 8, GB = kQmN / 8;
+            constexpr int GA = kQmRows / 8, GB = kQmN / 8, GBM = kQmTok / 8;
             for (int j = 2 * (warp - kQmMmaWarp); j < 2 * nloc; j += (j & 1) ? 3 : 1) {
                 const int i = j >> 1, h = j & 1, s = i % kQmStages, as = j % kQmAStages, q = i % kQmRegions;
                 bool ok = true;
@@ -409,12 +414,12 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a, const
                 qm_fence_after();
                 const uint32_t st = smem_u32(stages + (size_t)s * kQmStageBytes);
                 const uint32_t an = st + kQmCodes + kQmHdr, bm = an + kQmAMin, bn = bm + kQmBMain;
-                const uint32_t at = tmem + (uint32_t)(as * 64), dmain = tmem + kQmRegionCol + (uint32_t)(q * 128);
+                const uint32_t at = tmem + (uint32_t)(as * 64), dmain = tmem + kQmRegionCol + (uint32_t)(q * kQmRegionCols);
 #pragma unroll
                 for (int k = 0; k < 8; k++)
                     qm_mma_ts(dmain, at + (uint32_t)(8 * k), qm_desc(bm + (8 * h + k) * 2 * GB * 128, GB * 128, 128),
                               (h > 0 || k > 0) ? 1u : 0u);
-                if (h == 0) qm_mma(dmain + 64, qm_desc(an, GA * 128, 128), qm_desc(bn, GB * 128, 128), 0);
+                if (h == 0) qm_mma_min(dmain + 64, qm_desc(an, GA * 128, 128), qm_desc(bn, GBM * 128, 128));
                 if (h == 1) {
                     qm_commit(&empty[s]);
                     qm_commit(&ready[q]);
@@ -483,19 +488,19 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a, const
             // the TMEM loads below are warp-collective: leave the loop as a whole warp
             if (__any_sync(JDG_FULL, !ok || *abort_flag)) break;
             qm_fence_after();
-            const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + kQmRegionCol + (uint32_t)(q * 128);
+            const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + kQmRegionCol + (uint32_t)(q * kQmRegionCols);
             const float d = h2f((uint16_t)(hw & 0xFFFF)), dmin = h2f((uint16_t)(hw >> 16));
 #pragma unroll
-            for (int part = 0; part < 2; part++) {  // A.B, then A_min.B_min
-                const float sc = part == 0 ? d : -dmin;
+            for (int qt = 0; qt < 4; qt++) {  // A.B: tokens 8qt.. hi and lo, then A_min.B_min
+                float vh[8], vl[8], vm[8];
+                qm_ld8(base + 8 * qt, vh);
+                qm_ld8(base + 32 + 8 * qt, vl);
+                qm_ld8(base + 64 + 8 * qt, vm);
+                qm_ld_wait();
 #pragma unroll
-                for (int qt = 0; qt < 4; qt++) {
-                    float vh[8], vl[8];
-                    qm_ld8(base + 64 * part + 8 * qt, vh);
-                    qm_ld8(base + 64 * part + 32 + 8 * qt, vl);
-                    qm_ld_wait();
-#pragma unroll
-                    for (int t = 0; t < 8; t++) acc[8 * qt + t] = fmaf(sc, vh[t] + vl[t], acc[8 * qt + t]);
+                for (int t = 0; t < 8; t++) {
+                    acc[8 * qt + t] = fmaf(d, vh[t] + vl[t], acc[8 * qt + t]);
+                    acc[8 * qt + t] = fmaf(-dmin, vm[t], acc[8 * qt + t]);
                 }
             }
             qm_fence_before();
