@@ -218,13 +218,13 @@ static __global__ __launch_bounds__(256) void k_hpar_dots(HParArgs a) {
     for (int i = tid; i < nrow * a.B; i += 256) {
         const int r = i / a.B, b = i % a.B;
         float s = 0.f;
-        for (int c0 = 0; c0 < nkc; c0 += 8) {  // chunks in order, eight loads in flight
-            float v[8];
+        for (int c0 = 0; c0 < nkc; c0 += 16) {  // chunks in order, sixteen loads in flight
+            float v[16];
 #pragma unroll
-            for (int m = 0; m < 8; m++)
+            for (int m = 0; m < 16; m++)
                 v[m] = c0 + m < nkc ? __ldcg(a.part + (((size_t)(c0 + m) * a.n_alive + ei) * nrow + r) * kHparTok + b) : 0.f;
 #pragma unroll
-            for (int m = 0; m < 8; m++)
+            for (int m = 0; m < 16; m++)
                 if (c0 + m < nkc) s += v[m];
         }
         if (r == 0) a.votes[b * kMaxE + e] = isfinite(s) ? s : -1e30f;
@@ -260,16 +260,19 @@ static __global__ __launch_bounds__(256) void k_hpar_dots(HParArgs a) {
 
 // x[b][i] += (alpha * w_ki) * (A_e[i] . t_e[b]) for the elected experts in election order
 // (janusdoe.c:3294-3302).  grid (D/32), block 256, dynamic smem hpar_apply_smem: CTA takes rows
-// i0..i0+31 of every alive expert's A and the projections t of all sequences into shared
-// memory; thread (b, q) updates rows i0+4q..i0+4q+3 of sequence b (B <= 32, R % 4 == 0).
+// i0..i0+31 of every alive expert's A (rows padded to R + 4 floats: the 8 lanes of a
+// shared-memory phase read 8 consecutive rows from 8 distinct bank groups) and the
+// projections t of all sequences into shared memory; thread (b, q) updates rows i0+q+8m
+// (m < 4) of sequence b (B <= 32, R % 4 == 0).
 __host__ __device__ constexpr size_t hpar_apply_smem(int n_alive, int R) {
-    return ((size_t)n_alive * 32 * R + (size_t)kHparTok * n_alive * R) * 4;
+    return ((size_t)n_alive * 32 * (R + 4) + (size_t)kHparTok * n_alive * R) * 4;
 }
 static __global__ __launch_bounds__(256) void k_hpar_apply(HParArgs a) {
     extern __shared__ __align__(16) float hsm_apply[];
     const int R = a.R, na = a.n_alive;
-    float *as = hsm_apply;                     // [na][32][R]
-    float *ts = hsm_apply + (size_t)na * 32 * R;  // [32][na][R]
+    const int RP = R + 4;                      // padded row of A
+    float *as = hsm_apply;                     // [na][32][RP]
+    float *ts = hsm_apply + (size_t)na * 32 * RP;  // [32][na][R]
     __shared__ int slot[kMaxE];                // expert id -> index in alive_list
     __shared__ int s_sel[kHparTok][kMaxE], s_k[kHparTok];
     __shared__ float s_w[kHparTok][kMaxE];
@@ -320,7 +323,8 @@ static __global__ __launch_bounds__(256) void k_hpar_apply(HParArgs a) {
         for (int m = 0; m < 8; m++) {
             const int idx = base + tid + 256 * m;
             if (idx < nA) {
-                if (i0 + (4 * (idx % (8 * R))) / R < a.D) reinterpret_cast<float4 *>(as)[idx] = v[m];
+                const int ei = idx / (8 * R), rem = idx % (8 * R), row = (4 * rem) / R, col = (4 * rem) % R;
+                if (i0 + row < a.D) *reinterpret_cast<float4 *>(as + ((size_t)ei * 32 + row) * RP + col) = v[m];
             } else if (idx < nA + nT) {
                 reinterpret_cast<float4 *>(ts)[idx - nA] = v[m];
             }
@@ -332,7 +336,7 @@ static __global__ __launch_bounds__(256) void k_hpar_apply(HParArgs a) {
     float xi[4];
 #pragma unroll
     for (int m = 0; m < 4; m++) {
-        const int i = i0 + 4 * q + m;
+        const int i = i0 + q + 8 * m;
         xi[m] = i < a.D ? a.x[(size_t)b * a.D + i] : 0.f;
     }
     const int k = s_k[b];
@@ -342,11 +346,12 @@ static __global__ __launch_bounds__(256) void k_hpar_apply(HParArgs a) {
         const float w = __fmul_rn(a.lora_alpha, s_w[b][ki]);
         const float *tr = ts + ((size_t)b * na + si) * R;
         float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
         for (int r = 0; r < R; r += 4) {
             const float4 tv = *reinterpret_cast<const float4 *>(tr + r);
 #pragma unroll
             for (int m = 0; m < 4; m++) {
-                const float4 av = *reinterpret_cast<const float4 *>(as + ((size_t)si * 32 + 4 * q + m) * R + r);
+                const float4 av = *reinterpret_cast<const float4 *>(as + ((size_t)si * 32 + q + 8 * m) * RP + r);
                 s[m] = fmaf(av.x, tv.x, s[m]);
                 s[m] = fmaf(av.y, tv.y, s[m]);
                 s[m] = fmaf(av.z, tv.z, s[m]);
@@ -358,7 +363,7 @@ static __global__ __launch_bounds__(256) void k_hpar_apply(HParArgs a) {
     }
 #pragma unroll
     for (int m = 0; m < 4; m++) {
-        const int i = i0 + 4 * q + m;
+        const int i = i0 + q + 8 * m;
         if (i < a.D) a.x[(size_t)b * a.D + i] = xi[m];
     }
 }

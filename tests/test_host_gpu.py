@@ -164,6 +164,29 @@ def test_host_batched_parity(jd, orc, gpu_ctx, tmp_path):
         hm.close()
 
 
+def test_host_batched_parity_wide(jd, orc, gpu_ctx, tmp_path):
+    """A full 32-sequence tile of the 8B Q4_K layer shape (dim 4096, ffn 14336): every slot of
+    the tensor-core GEMM's token tile, the batched prep and the batched parliament."""
+    hm, om, V = _models(jd, orc, "q4k_c5_layer", tmp_path)
+    L = hm.h.n_layers
+    B, P, G = 32, 3, 2
+    prompts = np.random.default_rng(11).integers(0, V, (B, P)).astype(np.int32)
+    ref = [_oracle_stream(om, prompts[b], G) for b in range(B)]
+    eng = jd.Engine.host(gpu_ctx, hm, B, 96)
+    try:
+        eng.reset()
+        for pos in range(P + G - 1):
+            tok = np.array([ref[b][0][pos] for b in range(B)], np.int32)
+            nxt, _, lg, tr = eng.step(tok, np.full(B, pos, np.int32), logits=True, trace=True)
+            for b in range(B):
+                assert logit_err(lg[b], ref[b][1][pos]) <= LOGIT_TOL, (b, pos)
+                assert not compare_trace(tr, ref[b][2][pos], L, b=b), (b, pos)
+    finally:
+        eng.close()
+        om.close()
+        hm.close()
+
+
 def test_host_lora_sidecar_roundtrip(jd, orc, gpu_ctx, tmp_path):
     """A LoRA parliament saved to the sidecar and loaded back gives identical logits."""
     hm, om, V = _models(jd, orc, "q8_neox", tmp_path)
