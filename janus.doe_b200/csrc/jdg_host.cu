@@ -66,6 +66,10 @@ struct HostPriv {
     unsigned *hpar_tickets = nullptr;       // [17]
     float *hpar_votes = nullptr;            // [max_batch][16]
     float *hpar_tall = nullptr;             // [max_batch][16][R]
+    // the votes/projections/elections of a layer run on a second stream, forked after the
+    // q/k/v GEMM (they read only the normed layer input) and joined before the LoRA apply
+    cudaStream_t st2 = nullptr;
+    std::vector<cudaEvent_t> ev_fork, ev_join;  // one pair per layer
 };
 
 HostPriv *priv(jdg_engine *e) { return (HostPriv *)e->host_priv; }
@@ -460,6 +464,13 @@ static int host_upload_impl(jdg_engine *e, const jd_host_model *h, int max_batch
         CK(cudaMemset(hp->hpar_tickets, 0, (kMaxE + 1) * 4));
         DALLOC(hp->hpar_votes, (size_t)max_batch * kMaxE * 4);
         DALLOC(hp->hpar_tall, (size_t)max_batch * kMaxE * R * 4);
+        CK(cudaStreamCreateWithFlags(&hp->st2, cudaStreamNonBlocking));
+        hp->ev_fork.assign(L, nullptr);
+        hp->ev_join.assign(L, nullptr);
+        for (int l = 0; l < L; l++) {
+            CK(cudaEventCreateWithFlags(&hp->ev_fork[l], cudaEventDisableTiming));
+            CK(cudaEventCreateWithFlags(&hp->ev_join[l], cudaEventDisableTiming));
+        }
     }
     DALLOC(e->amax_v, 1024 * 4);
     DALLOC(e->amax_i, 1024 * 4);
@@ -745,7 +756,28 @@ int jdg_enqueue_host_step(jdg_engine *e, int B) {
     const bool hpar = hp->hpar_part && B <= kHparTok;
     for (int l = 0; l < L; l++) {
         HostLayerDev &hl = e->hl[l];
+        const bool hpar_l = hpar && e->n_alive[l] > 0;
+        HParArgs pa = {};
+        if (hpar_l) {
+            pa.D = D; pa.R = e->lora_rank; pa.B = B; pa.L = L; pa.l = l;
+            pa.xn = e->xn; pa.w_vote = hl.w_vote; pa.lora_A = hp->lora_A[l]; pa.lora_B = hp->lora_B[l];
+            pa.alive = hl.alive; pa.alive_list = hp->alive_list[l]; pa.n_alive = e->n_alive[l];
+            pa.part = hp->hpar_part; pa.tickets = hp->hpar_tickets;
+            pa.votes = hp->hpar_votes; pa.tall = hp->hpar_tall;
+            pa.kcnt = e->kcnt; pa.sel = e->sel; pa.selw = e->selw; pa.consensus = e->consensus;
+            pa.tr_k = e->tr_k; pa.tr_sel = e->tr_sel; pa.tr_w = e->tr_w; pa.tr_ema = e->tr_ema;
+            pa.lora_alpha = e->lora_alpha; pa.x = e->x;
+        }
         launch_q<EPI_STORE>(e, hp->wqkv[l], e->x, D, B, e->qkv, e->qkvd, 1.f, 1, hl.attn_norm, e->xn);
+        if (hpar_l) {
+            // LoRA parliament, first half (janusdoe.c:3281-3293): votes, projections and
+            // elections from xn, beside the rest of the layer
+            CK(cudaEventRecord(hp->ev_fork[l], e->st));
+            CK(cudaStreamWaitEvent(hp->st2, hp->ev_fork[l], 0));
+            k_hpar_dots<<<dim3(D / 256, e->n_alive[l]), 256, hpar_dots_smem(pa.R), hp->st2>>>(pa);
+            CK(cudaEventRecord(hp->ev_join[l], hp->st2));
+            e->launches++;
+        }
         jdg_launch_rope(e, l, B);
         jdg_launch_attention(e, l, B, scale, 1.0f + hl.attn_bias);
         if (!tp) {
@@ -766,19 +798,10 @@ int jdg_enqueue_host_step(jdg_engine *e, int B) {
             e->launches++;
         }
         // LoRA parliament on xn (janusdoe.c:3281-3303)
-        if (hpar && e->n_alive[l] > 0) {
-            HParArgs pa;
-            pa.D = D; pa.R = e->lora_rank; pa.B = B; pa.L = L; pa.l = l;
-            pa.xn = e->xn; pa.w_vote = hl.w_vote; pa.lora_A = hp->lora_A[l]; pa.lora_B = hp->lora_B[l];
-            pa.alive = hl.alive; pa.alive_list = hp->alive_list[l]; pa.n_alive = e->n_alive[l];
-            pa.part = hp->hpar_part; pa.tickets = hp->hpar_tickets;
-            pa.votes = hp->hpar_votes; pa.tall = hp->hpar_tall;
-            pa.kcnt = e->kcnt; pa.sel = e->sel; pa.selw = e->selw; pa.consensus = e->consensus;
-            pa.tr_k = e->tr_k; pa.tr_sel = e->tr_sel; pa.tr_w = e->tr_w; pa.tr_ema = e->tr_ema;
-            pa.lora_alpha = e->lora_alpha; pa.x = e->x;
-            k_hpar_dots<<<dim3(D / 256, e->n_alive[l]), 256, hpar_dots_smem(pa.R), e->st>>>(pa);
+        if (hpar_l) {
+            CK(cudaStreamWaitEvent(e->st, hp->ev_join[l], 0));
             k_hpar_apply<<<(D + 31) / 32, 256, hpar_apply_smem(e->n_alive[l], pa.R), e->st>>>(pa);
-            e->launches += 2;
+            e->launches++;
             continue;
         }
         jdg_launch_elect(e, l, B, e->xn, nullptr, hl.w_vote, hl.alive, 0.f, 1);
@@ -808,6 +831,11 @@ void jdg_host_release(jdg_engine *e) {
     HostPriv *hp = priv(e);
     if (!hp) return;
     if (hp->comm) ncclCommDestroy(hp->comm);
+    for (cudaEvent_t ev : hp->ev_fork)
+        if (ev) cudaEventDestroy(ev);
+    for (cudaEvent_t ev : hp->ev_join)
+        if (ev) cudaEventDestroy(ev);
+    if (hp->st2) cudaStreamDestroy(hp->st2);
     delete hp;
     e->host_priv = nullptr;
 }
