@@ -573,7 +573,20 @@ static void launch_q(jdg_engine *e, const QW &w, const float *X, int ldx, int M,
             q.ksplit = ks;
             q.part = priv(e)->qm_part;
             q.tickets = priv(e)->qm_tickets;
-            k_qm_q4k<<<dim3(tiles, ks), kQmThreads, kQmSmem, e->st>>>(q, maps->codes, maps->hdr);
+            // programmatic dependent launch: the GEMM's CTAs start while the prep kernel runs
+            // (it triggers at once) and stream their first weight stages; they wait for it
+            // before reading the prepared activations or C
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(tiles, ks);
+            cfg.blockDim = dim3(kQmThreads);
+            cfg.dynamicSmemBytes = kQmSmem;
+            cfg.stream = e->st;
+            cudaLaunchAttribute at[1];
+            at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            at[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = at;
+            cfg.numAttrs = 1;
+            cudaLaunchKernelEx(&cfg, k_qm_q4k, q, maps->codes, maps->hdr);
             e->launches += 2;
         }
         return;
