@@ -554,8 +554,21 @@ static void launch_q(jdg_engine *e, const QW &w, const float *X, int ldx, int M,
         }
         for (int t0 = 0; t0 < M; t0 += kQmTok) {
             const int mt = std::min(kQmTok, M - t0);
-            k_qm_prep_tok<<<kQmTok, 256, 0, e->st>>>(X + (size_t)t0 * ldx, ldx, mt, w.cols, do_norm, norm_w, e->eps,
-                                                     xn_out ? xn_out + (size_t)t0 * ldx : nullptr, priv(e)->xprep);
+            {
+                // programmatic dependent launch: queued behind the previous kernel, it waits
+                // for that grid before reading X
+                cudaLaunchConfig_t pc = {};
+                pc.gridDim = dim3(kQmTok);
+                pc.blockDim = dim3(256);
+                pc.stream = e->st;
+                cudaLaunchAttribute pa[1];
+                pa[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+                pa[0].val.programmaticStreamSerializationAllowed = 1;
+                pc.attrs = pa;
+                pc.numAttrs = 1;
+                cudaLaunchKernelEx(&pc, k_qm_prep_tok, X + (size_t)t0 * ldx, ldx, mt, w.cols, do_norm, norm_w, e->eps,
+                                   xn_out ? xn_out + (size_t)t0 * ldx : (float *)nullptr, priv(e)->xprep);
+            }
             QmArgs q = {};
             q.w = w;
             q.xprep = priv(e)->xprep;

@@ -20,8 +20,10 @@ static __global__ __launch_bounds__(256) void k_qm_prep_tok(const float *__restr
                                                             const float *__restrict__ norm_w, float eps,
                                                             float *__restrict__ xn_out, uint8_t *__restrict__ out) {
     __shared__ float red[32];
-    // the GEMM that follows (programmatic dependent launch) may start its weight stream now;
-    // it waits for this grid to finish before reading the prepared activations
+    // launched as a dependent of the previous kernel: wait for it before reading X; the GEMM
+    // that follows (also a dependent launch) may start its weight stream now and waits for
+    // this grid to finish before reading the prepared activations
+    pdl_wait();
     pdl_trigger();
     const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, ng = K / 8;
     const bool live = t < M;
