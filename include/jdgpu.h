@@ -225,16 +225,25 @@ int jdg_qmatvec(jdg_ctx *ctx, float *out, const void *W, int dt, const float *x,
 /* No counterpart in the reference.  Greedy vocabulary pick for callers that cannot allocate
  * device memory (all their buffers come from another allocator or a preallocated pool):
  * logits_dev[r] = W_dev[r][:] . x_dev (W f32 row-major [rows][cols], cols a multiple of 4)
- * and *argmax_dev = the first index of the maximum, enqueued on `stream` (a cudaStream_t,
- * NULL for the default stream); returns once enqueued.  It calls no allocator: its scratch
- * (per-CTA partial maxima and a completion ticket) is a fixed device array of about 64 KB
- * per GPU, held until the process exits, which limits a call to 131072 rows and 16384
- * columns (larger sizes return JD_EINVAL, message in jdg_last_error(NULL)).  The first call
- * on a device looks up that array's address, so make the first call before any stream
- * capture.  All calls share the array: calls that overlap on the GPU (other streams, other
- * host threads) race and must be serialised by the caller. */
+ * and *argmax_dev = the first index of the maximum, enqueued on `stream` (a cudaStream_t of
+ * the current device, NULL for the default stream); returns once enqueued.  W_dev and x_dev
+ * must be 16-byte aligned (rows and x are read as 16-byte vectors); logits_dev and argmax_dev
+ * are written as scalars.  NaN logits are never picked; if no logit is greater than -inf the
+ * pick is 0.  It calls no allocator: its scratch (per-CTA partial maxima and a completion
+ * ticket) is a fixed device array of about 64 KB per GPU, held until the process exits,
+ * which limits a call to 131072 rows and 16384 columns (larger sizes return JD_EINVAL,
+ * message in jdg_last_error(NULL)).  The first call on a device looks up that array's
+ * address, so make the first call before any stream capture.  All calls share the array:
+ * calls that overlap on the GPU (other streams, other host threads) race and must be
+ * serialised by the caller. */
 int jdg_logits_argmax_noalloc(const float *W_dev, const float *x_dev, int rows, int cols, float *logits_dev,
                               int *argmax_dev, void *stream);
+/* The argument check that jdg_logits_argmax_noalloc runs before it touches the GPU: null
+ * pointers, shape, 16-byte alignment of W_dev and x_dev, and the scratch limits.  Pure host
+ * arithmetic (no CUDA call, nothing dereferenced); JD_OK or JD_EINVAL with the message in
+ * jdg_last_error(NULL). */
+int jdg_logits_argmax_noalloc_check(const void *W_dev, const void *x_dev, int rows, int cols, const void *logits_dev,
+                                    const void *argmax_dev);
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

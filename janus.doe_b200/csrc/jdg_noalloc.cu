@@ -10,6 +10,7 @@
 // instead of a cudaMalloc'd buffer.
 #include <cuda_runtime.h>
 
+#include <cstdint>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -157,23 +158,48 @@ int na_scratch(NoAllocScratch **out) {
 
 }  // namespace
 
-extern "C" int jdg_logits_argmax_noalloc(const float *W_dev, const float *x_dev, int rows, int cols, float *logits_dev,
-                                         int *argmax_dev, void *stream) {
+extern "C" int jdg_logits_argmax_noalloc_check(const void *W_dev, const void *x_dev, int rows, int cols,
+                                               const void *logits_dev, const void *argmax_dev) {
+    // Pure host arithmetic on the arguments: no CUDA call, no dereference.
     if (!W_dev || !x_dev || !logits_dev || !argmax_dev || rows < 1 || cols < 4 || cols % 4) {
         jdg_set_err(nullptr, "jdg_logits_argmax_noalloc: bad arguments (rows %d, cols %d)", rows, cols);
         return JD_EINVAL;
     }
-    const int ctas = (rows + kNaRowsPerCta - 1) / kNaRowsPerCta;
-    if (ctas > kNaMaxCtas || cols > kNaMaxCols) {
-        jdg_set_err(nullptr,
-                 "jdg_logits_argmax_noalloc: %d x %d exceeds the fixed scratch (at most %d rows and %d columns)", rows,
-                 cols, kNaMaxCtas * kNaRowsPerCta, kNaMaxCols);
+    // W rows and x are read as 16-byte vectors: a misaligned view would fault on the GPU
+    if (((uintptr_t)W_dev | (uintptr_t)x_dev) & 15u) {
+        jdg_set_err(nullptr, "jdg_logits_argmax_noalloc: W_dev and x_dev must be 16-byte aligned (%p, %p)", W_dev,
+                    x_dev);
         return JD_EINVAL;
     }
+    const long ctas = ((long)rows + kNaRowsPerCta - 1) / kNaRowsPerCta;
+    if (ctas > kNaMaxCtas || cols > kNaMaxCols) {
+        jdg_set_err(nullptr,
+                    "jdg_logits_argmax_noalloc: %d x %d exceeds the fixed scratch (at most %d rows and %d columns)",
+                    rows, cols, kNaMaxCtas * kNaRowsPerCta, kNaMaxCols);
+        return JD_EINVAL;
+    }
+    return JD_OK;
+}
+
+extern "C" int jdg_logits_argmax_noalloc(const float *W_dev, const float *x_dev, int rows, int cols, float *logits_dev,
+                                         int *argmax_dev, void *stream) {
+    int rc = jdg_logits_argmax_noalloc_check(W_dev, x_dev, rows, cols, logits_dev, argmax_dev);
+    if (rc != JD_OK) return rc;
+    const int ctas = (rows + kNaRowsPerCta - 1) / kNaRowsPerCta;
     NoAllocScratch *scr = nullptr;
-    int rc = na_scratch(&scr);
+    rc = na_scratch(&scr);
     if (rc != JD_OK) return rc;
     cudaStream_t st = (cudaStream_t)stream;
+    if (st) {  // the scratch address belongs to the current device: so must the stream
+        int cur = -1, sdev = -1;
+        cudaError_t ge = cudaGetDevice(&cur);
+        if (ge == cudaSuccess) ge = cudaStreamGetDevice(st, &sdev);
+        if (ge != cudaSuccess || sdev != cur) {
+            jdg_set_err(nullptr, "jdg_logits_argmax_noalloc: the stream is not on the current device (%d vs %d%s%s)",
+                        sdev, cur, ge != cudaSuccess ? ": " : "", ge != cudaSuccess ? cudaGetErrorString(ge) : "");
+            return JD_EINVAL;
+        }
+    }
     // the ticket must start at zero; a memset allocates nothing
     cudaError_t e = cudaMemsetAsync(&scr->ticket, 0, sizeof(unsigned), st);
     if (e == cudaSuccess) {

@@ -146,3 +146,30 @@ def test_open_without_gpu_reports(jd):
         pytest.skip("a GPU is present")
     with pytest.raises(jd.JdError):
         jd.Context(0)
+
+
+def _na_check(jd):
+    f = jd.lib().jdg_logits_argmax_noalloc_check
+    f.argtypes = [C.c_void_p] * 2 + [C.c_int] * 2 + [C.c_void_p] * 2
+    f.restype = C.c_int
+    return f
+
+
+@pytest.mark.parametrize("W,x,rows,cols,code,msg", [
+    (256, 512, 8256, 768, 0, None),                      # aligned, within the scratch
+    (256, 512, 131072, 16384, 0, None),                  # the largest accepted call
+    (256, 512, 131072 + 16, 64, -1, b"exceeds"),         # one CTA of rows past the scratch
+    (256, 512, 64, 16384 + 4, -1, b"exceeds"),           # x no longer fits shared memory
+    (256 + 4, 512, 64, 64, -1, b"16-byte aligned"),      # W view offset by one float
+    (256, 512 + 8, 64, 64, -1, b"16-byte aligned"),      # x view offset by two floats
+    (256, 512, 64, 66, -1, b"bad arguments"),            # cols not a multiple of 4
+    (256, 512, 0, 64, -1, b"bad arguments"),             # no rows
+    (0, 512, 64, 64, -1, b"bad arguments"),              # null W
+])
+def test_noalloc_argument_check(jd, W, x, rows, cols, code, msg):
+    """Argument checks of the allocation-free pick, run on the host only: the values are
+    plain integers standing in for device addresses and nothing is dereferenced."""
+    rc = _na_check(jd)(W, x, rows, cols, 1024, 2048)
+    assert rc == code
+    if msg:
+        assert msg in jd.lib().jdg_last_error(None)
