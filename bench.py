@@ -3,15 +3,21 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
 
 One "step" is one decode step of the whole batch (one token per sequence) after a
-sequential prefill of the prompt.  Workloads (synthetic seeded weights, uniform-random
-prompts):
+sequential prefill of the prompt.  Without --workload the run measures depth12_bs256, then
+host_q4k_bs32, then depth12_bs1, and prints one JSON line per workload, the depth12_bs1
+headline last (K and W apply to the headline; the others take at most their own defaults).
+Workloads (synthetic seeded weights, uniform-random prompts):
   depth12_bs1    (default) own model depth 12 (dim 768, 12/4 heads, 8 experts with 5-8 alive
                  per layer, vocab 8256, ctx 1024), 512-token prompt, greedy, batch 1 per GPU
   depth12_bs256  same model, 256 sequences per GPU
   depth4_bs1     depth 4 (dim 256, 4 experts, vocab 2256), 32-token prompt, greedy
   depth8_bs64    depth 8 (dim 512, 8/4 heads, 6 experts, vocab 4256), 64 sequences,
                  64-token prompt, temperature 0.8 / top-k 40
-Sequences are independent, so N GPUs each run their own batch (weak scaling, no collective).
+  host_q8_bs1    host GGUF, Q8_0, 1.1B llama shape (dim 2048, 22 layers), batch 1
+  host_q4k_bs32  host GGUF, Q4_K, 8B llama shape (dim 4096, 32 layers, vocab 128256), 32 sequences
+Own-model sequences are independent, so N GPUs each run their own batch (weak scaling, no
+collective); the host model's 32 sequences are split over N GPUs by tensor parallelism with
+NCCL all-reduces (strong scaling).
 `value` is device-timed (CUDA events on the engine's stream, max over ranks); `e2e` goes
 through the public step call with host buffers (pinned H2D of token/position, D2H of the
 next token every step).
@@ -37,7 +43,8 @@ WORKLOADS = {
     "depth12_bs256": dict(depth=12, over=dict(n_kv_heads=4, vocab_size=8256, seq_len=1024), masks=True, seed=2,
                           B=256, prompt=512, temp=0.0, top_k=0, steps=32, warmup=4, ref_decode=8),
     "depth4_bs1": dict(depth=4, over=dict(vocab_size=2256, seq_len=256), masks=False, seed=0,
-                       B=1, prompt=32, temp=0.0, top_k=0, steps=128, warmup=8, ref_decode=128),
+                       B=1, prompt=32, temp=0.0, top_k=0, steps=128, warmup=8, ref_decode=128,
+                       l2="model L2-resident (16 MB of weights): tok/s and latency, no HBM claim"),
     "depth8_bs64": dict(depth=8, over=dict(n_kv_heads=4, vocab_size=4256, seq_len=512), masks=False, seed=1,
                         B=64, prompt=64, temp=0.8, top_k=40, steps=128, warmup=8, ref_decode=32),
     # host GGUF mode: synthetic llama-family models, weights N(0, 0.02) quantised per block
@@ -207,19 +214,19 @@ def own_bytes(cfg, alive_counts, B, steps, stats):
 def cpu_reference(w, n_decode, threads):
     """Time the reference's own decode (janusdoe.c forward_token + greedy/sample, OpenBLAS
     build from oracle/_ref) on the host cores: one sequence, prefill untimed, n_decode
-    decode tokens timed."""
+    decode tokens timed.  Returns (tok/s, kind, sample text, alive experts per layer)."""
     os.environ["OPENBLAS_NUM_THREADS"] = str(threads)
     sys.path.insert(0, ROOT)
     from oracle.oracle import Reference
     try:
         ref = Reference("_blas")
-        kind = "reference"
     except RuntimeError:
         ref = Reference("")
-        kind = "reference"
+    kind = "reference"
     ov = w["over"]
     ref.own_setup(w["depth"], ov.get("n_kv_heads", 0), ov["vocab_size"], ov.get("seq_len", 256), w["seed"], 0.02,
                   w["masks"])
+    alive = [int(sum(ref.own_alive(l))) for l in range(w["depth"])]
     pr, rngs = prompts_for(dict(w, B=1), 0)
     pos, lg = 0, None
     for t in pr[0]:
@@ -236,7 +243,7 @@ def cpu_reference(w, n_decode, threads):
         pos += 1
     dt = time.perf_counter() - t0
     return n_decode / dt, kind, "1 sequence, %d-token prefill untimed, %d decode tokens timed (positions %d-%d)" % (
-        w["prompt"], n_decode, w["prompt"], w["prompt"] + n_decode - 1)
+        w["prompt"], n_decode, w["prompt"], w["prompt"] + n_decode - 1), alive
 
 
 def host_gguf_path(w):
@@ -286,31 +293,50 @@ def cpu_reference_host(w, n_prompt, n_decode):
     return n_decode / dt, threads, "1 sequence, %d-token prompt untimed, %d greedy tokens timed" % (n_prompt, n_decode)
 
 
-def run_reference_arm(args, w):
-    dist, world, rank, local = dist_setup()
-    if rank != 0:
-        return
+def own_config(name, w, world, alive, steps, warmup):
+    """The workload description printed by both arms (identical for the same command line)."""
+    ov = w["over"]
+    P = w["prompt"]
+    # config_from_depth: dim = 64 * depth, heads of 64
+    return {"workload": name, "depth": w["depth"], "dim": 64 * w["depth"], "heads": w["depth"],
+            "kv_heads": ov.get("n_kv_heads") or w["depth"], "experts_alive": alive, "vocab": ov["vocab_size"],
+            "ctx": ov.get("seq_len"), "batch_per_gpu": w["B"], "global_batch": w["B"] * world, "prompt": P,
+            "positions": [P + warmup, P + warmup + steps - 1],
+            "sampling": "greedy" if w["temp"] <= 0 else "temp %.1f top-k %d" % (w["temp"], w["top_k"]),
+            "parallelism": "dp%d (independent sequences)" % world,
+            "l2": w.get("l2", "inputs larger than L2 (weights + KV read per step > 126 MB)")}
+
+
+def host_config(name, w, world):
+    return {"workload": name, "arch": w["arch"], "layers": w["L"], "dim": w["D"], "heads": w["H"],
+            "kv_heads": w["KV"], "ffn": w["FF"], "vocab": w["V"], "dtype": {8: "Q8_0", 12: "Q4_K"}[w["dtype"]],
+            "lora": "%d x rank %d" % (w["adapters"], w["rank"]), "global_batch": w["B"], "prompt": w["prompt"],
+            "parallelism": "tp%d" % world if world > 1 else "1 GPU",
+            "l2": "inputs larger than L2 (packed weights read per step > 126 MB)"}
+
+
+def scaling_of(w):
+    # own model: every GPU decodes its own batch (weak); host model: one batch of 32 sequences
+    # split by tensor parallelism over the GPUs (strong)
+    return "strong" if w.get("host") else "weak"
+
+
+def reference_line(args, name, w, steps, warmup):
+    """The reference arm for one workload: the reference's own CPU decode (rank 0 only)."""
     threads = os.cpu_count() or 1
     if w.get("host"):
         tps, threads, sample = cpu_reference_host(w, w["ref_prompt"], w["ref_decode"])
-        kind, n = "reference", w["ref_decode"]
-        line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": args.gpus,
-                "steps": n, "warmup": 0, "ms_per_step": 1000.0 / tps, "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                "config": {"workload": args.workload, "batch": 1},
-                "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": kind, "sample": sample},
-                "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-        print(json.dumps(line), flush=True)
-        return
-    n = max(1, min(args.steps, w["ref_decode"] * 4))
-    tps, kind, sample = cpu_reference(w, n, threads)
-    line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": args.gpus,
-            "steps": n, "warmup": args.warmup, "ms_per_step": 1000.0 / tps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": args.workload, "batch_per_gpu": 1, "prompt": w["prompt"]},
-            "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": kind, "sample": sample},
+        cfg = host_config(name, w, args.gpus)
+    else:
+        n = max(1, min(steps, w["ref_decode"] * 4))
+        tps, _, sample, alive = cpu_reference(w, n, threads)
+        cfg = own_config(name, w, args.gpus, alive, steps, warmup)
+    return {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": steps, "warmup": warmup, "ms_per_step": 1000.0 / tps, "higher_is_better": True,
+            "scaling": scaling_of(w), "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": cfg,
+            "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": threads, "kind": "reference", "sample": sample},
             "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
 
 
 def packed_bytes(w):
@@ -322,7 +348,7 @@ def packed_bytes(w):
     return bpw * (L * per_layer + V * D)
 
 
-def run_host(args, w, dist, world, rank, local):
+def run_host(args, name, w, steps, warmup, dist, world, rank, local):
     jd = load_pkg()
     B, P, S = w["B"], w["prompt"], w["max_seq"]
     if rank == 0:
@@ -333,7 +359,6 @@ def run_host(args, w, dist, world, rank, local):
     hm.lora_seed(*lora_args(w))
     ctx = jd.Context(local)
     if world > 1:
-        import torch
         ids = [None]
         if rank == 0:
             buf = C.create_string_buffer(128)
@@ -346,20 +371,20 @@ def run_host(args, w, dist, world, rank, local):
     prompts, _ = prompts_for(dict(w, over=dict(vocab_size=w["V"])), 0)
     eng.set_prompt(prompts, [P] * B)
     prefill_ms = eng.run(B, P - 1)
-    eng.run(B, args.warmup)
+    eng.run(B, warmup)
     clocks = Clocks(local)
     barrier(dist)
     eng.reset_stats()
     l0 = eng.launches()
     clocks.start()
-    ms = eng.run(B, args.steps)
+    ms = eng.run(B, steps)
     ck = clocks.stop()
     n_launch = eng.launches() - l0
     stats = eng.stats()
     ms = allmax(dist, ms)
     barrier(dist)
-    value = B * args.steps / (ms / 1000.0)
-    n_e2e = min(args.steps, 16)
+    value = B * steps / (ms / 1000.0)
+    n_e2e = min(steps, 16)
     tok_h, pos_h = eng.state(B)
     barrier(dist)
     t0 = time.perf_counter()
@@ -379,23 +404,19 @@ def run_host(args, w, dist, world, rank, local):
         used = {int(e) for b in range(B) for e in tr["sel"][b, l] if e >= 0}
         lora += len(used) * 2 * D * R * 4 + w["adapters"] * D * 4
     per_step = packed_bytes(w) + B * D * 4 + world * lora + 4 * D * (2 * L + 1)
-    bytes_run = args.steps * per_step + stats[1] * L * 2 * kd * 4 + args.steps * B * L * 2 * kd * 4
+    bytes_run = steps * per_step + stats[1] * L * 2 * kd * 4 + steps * B * L * 2 * kd * 4
     peak, peak_kind = peaks()
     achieved = bytes_run / (ms / 1000.0) / 1e9
     roof = {"bound": "hbm", "achieved": achieved, "peak": peak * world, "unit": "GB/s",
-            "frac": achieved / (peak * world), "traffic": dram_traffic(args.workload, bytes_run / args.steps),
+            "frac": achieved / (peak * world), "traffic": dram_traffic(name, bytes_run / steps),
             "peak_source": peak_kind,
-            "kernel": "whole decode step (CUDA graph of %d launches)" % (n_launch // max(1, args.steps)),
-            "algorithmic_bytes_per_step": bytes_run / args.steps}
-    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32",
+            "kernel": "whole decode step (CUDA graph of %d launches)" % (n_launch // max(1, steps)),
+            "algorithmic_bytes_per_step": bytes_run / steps}
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms / steps, "higher_is_better": True,
+            "scaling": scaling_of(w), "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (GGUF of N(0,0.02) weights quantised per block, uniform prompts)",
-            "config": {"workload": args.workload, "arch": w["arch"], "layers": L, "dim": D, "heads": w["H"],
-                       "kv_heads": w["KV"], "ffn": w["FF"], "vocab": w["V"], "dtype": {8: "Q8_0", 12: "Q4_K"}[w["dtype"]],
-                       "lora": "%d x rank %d" % (w["adapters"], R), "global_batch": B, "prompt": P,
-                       "parallelism": "tp%d" % world if world > 1 else "1 GPU",
-                       "l2": "inputs larger than L2: %.0f MB per step" % (per_step / 1e6)},
+            "config": host_config(name, w, world),
             "roofline": roof, "prefill_ms": prefill_ms, "clocks": ck, "gpu_launches": n_launch,
             "e2e": {"value": B * n_e2e / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 8 * B,
                     "d2h_bytes_per_step": 4 * B, "steps": n_e2e}}
@@ -403,42 +424,16 @@ def run_host(args, w, dist, world, rank, local):
         tps, threads, sample = cpu_reference_host(w, w["ref_prompt"], w["ref_decode"])
         line["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": threads, "kind": "reference",
                                 "sample": sample}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
     eng.close()
     hm.close()
     ctx.close()
-    if dist is not None:
-        dist.destroy_process_group()
+    return line if rank == 0 else None
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=None)
-    ap.add_argument("--warmup", type=int, default=None)
-    ap.add_argument("--workload", default="depth12_bs1", choices=sorted(WORKLOADS))
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--prompt", type=int, default=None, help="override the prompt length (profiling runs)")
-    args = ap.parse_args()
-    w = dict(WORKLOADS[args.workload])
-    if args.prompt:
-        w["prompt"] = max(2, args.prompt)
-    args.steps = w["steps"] if args.steps is None else args.steps
-    args.warmup = w["warmup"] if args.warmup is None else max(3, args.warmup)
-    if args.impl == "reference":
-        run_reference_arm(args, w)
-        return
-    dist, world, rank, local = dist_setup()
-    if w.get("host"):
-        run_host(args, w, dist, world, rank, local)
-        return
+def run_own(args, name, w, steps, warmup, dist, world, rank, local):
     jd = load_pkg()
     B, P = w["B"], w["prompt"]
     cfg = jd.config_from_depth(w["depth"], **w["over"])
-    if P + args.warmup + args.steps + min(args.steps, 64) + 1 > cfg.seq_len:
-        args.steps = max(1, (cfg.seq_len - P - args.warmup - 2) * 2 // 3)
     ctx = jd.Context(local)
     model = jd.Model.seeded(cfg, w["seed"], 0.02, w["masks"])
     alive = [sum(model.alive(l)) for l in range(cfg.depth)]
@@ -449,23 +444,23 @@ def main():
     eng.set_prompt(prompts, [P] * B, rngs)
     prefill_ms = eng.run(B, P - 1)
     # warm-up decode steps
-    eng.run(B, args.warmup)
+    eng.run(B, warmup)
     # timed decode steps
     clocks = Clocks(local)
     barrier(dist)
     eng.reset_stats()
     l0 = eng.launches()
     clocks.start()
-    ms = eng.run(B, args.steps)
+    ms = eng.run(B, steps)
     ck = clocks.stop()
     n_launch = eng.launches() - l0
     stats = eng.stats()
     ms = allmax(dist, ms)
     barrier(dist)
-    tok = B * args.steps * world
+    tok = B * steps * world
     value = tok / (ms / 1000.0)
     # e2e through the public step call with host buffers
-    n_e2e = min(args.steps, 64)
+    n_e2e = min(steps, 64)
     tok_h, pos_h = eng.state(B)
     rng_h = None if w["temp"] <= 0 else np.array(rngs, np.uint64)
     barrier(dist)
@@ -478,37 +473,81 @@ def main():
     barrier(dist)
     e2e = B * n_e2e * world / e2e_s
     # roofline: algorithmic bytes per step / device time per step (the decode step graph)
-    bytes_run = own_bytes(cfg, alive, B, args.steps, stats)
+    bytes_run = own_bytes(cfg, alive, B, steps, stats)
     peak, peak_kind = peaks()
     achieved = bytes_run / (ms / 1000.0) / 1e9
-    traffic = dram_traffic(args.workload, bytes_run / args.steps)
+    traffic = dram_traffic(name, bytes_run / steps)
     roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
             "traffic": traffic, "peak_source": peak_kind,
-            "kernel": "whole decode step (CUDA graph of %d launches)" % (n_launch // max(1, args.steps)),
-            "algorithmic_bytes_per_step": bytes_run / args.steps}
-    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "kernel": "whole decode step (CUDA graph of %d launches)" % (n_launch // max(1, steps)),
+            "algorithmic_bytes_per_step": bytes_run / steps}
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms / steps, "higher_is_better": True, "scaling": scaling_of(w),
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,0.02) weights, uniform prompts)",
-            "config": {"workload": args.workload, "depth": cfg.depth, "dim": cfg.dim, "heads": cfg.n_heads,
-                       "kv_heads": cfg.n_kv_heads, "experts_alive": alive, "vocab": cfg.vocab_size,
-                       "ctx": cfg.seq_len, "batch_per_gpu": B, "global_batch": B * world, "prompt": P,
-                       "positions": [P + args.warmup, P + args.warmup + args.steps - 1],
-                       "sampling": "greedy" if w["temp"] <= 0 else "temp %.1f top-k %d" % (w["temp"], w["top_k"]),
-                       "parallelism": "dp%d (independent sequences)" % world,
-                       "l2": "inputs larger than L2: %.0f MB of weights+KV per step vs 126 MB L2" % (
-                           bytes_run / args.steps / 1e6)},
+            "config": own_config(name, w, world, alive, steps, warmup),
             "roofline": roof, "prefill_ms": prefill_ms, "clocks": ck, "gpu_launches": n_launch,
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B,
                     "steps": n_e2e}}
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        tps, kind, sample = cpu_reference(w, w["ref_decode"], threads)
+        tps, kind, sample, _ = cpu_reference(w, w["ref_decode"], threads)
         line["cpu_baseline"] = {"value": tps, "unit": "tok/s", "cores": threads, "kind": kind, "sample": sample}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
     eng.close()
     model.close()
     ctx.close()
+    return line if rank == 0 else None
+
+
+# The default run (no --workload) measures the three workloads the metric names and prints
+# one JSON line each; the batch-1 depth-12 line, the headline, comes last.
+DEFAULT_RUN = ["depth12_bs256", "host_q4k_bs32", "depth12_bs1"]
+
+
+def steps_for(args, name, w, headline):
+    """Timed steps and warm-up steps of one workload: the command line's K and W for the
+    headline workload, at most the workload's own defaults for the others; bounded so that
+    prompt + warm-up + timed + end-to-end steps fit the context."""
+    if headline:
+        steps = w["steps"] if args.steps is None else args.steps
+        warmup = w["warmup"] if args.warmup is None else max(3, args.warmup)
+    else:
+        steps = w["steps"] if args.steps is None else min(args.steps, w["steps"])
+        warmup = w["warmup"] if args.warmup is None else max(3, min(args.warmup, w["warmup"]))
+    ctx = w["max_seq"] if w.get("host") else w["over"]["seq_len"]
+    e2e = 16 if w.get("host") else 64
+    if w["prompt"] + warmup + steps + min(steps, e2e) + 1 > ctx:
+        steps = max(1, (ctx - w["prompt"] - warmup - 2) * 2 // 3)
+    return steps, warmup
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
+    ap.add_argument("--workload", default=None, choices=sorted(WORKLOADS),
+                    help="one workload only (default: %s, the last being the headline)" % ", ".join(DEFAULT_RUN))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prompt", type=int, default=None, help="override the prompt length (profiling runs)")
+    args = ap.parse_args()
+    names = [args.workload] if args.workload else DEFAULT_RUN
+    dist, world, rank, local = (None, 1, int(os.environ.get("RANK", "0")), 0) if args.impl == "reference" \
+        else dist_setup()
+    for i, name in enumerate(names):
+        w = dict(WORKLOADS[name])
+        if args.prompt:
+            w["prompt"] = max(2, args.prompt)
+        steps, warmup = steps_for(args, name, w, i == len(names) - 1)
+        if args.impl == "reference":
+            # the reference is one CPU process: rank 0 runs it, other ranks exit without work
+            line = reference_line(args, name, w, steps, warmup) if rank == 0 else None
+        elif w.get("host"):
+            line = run_host(args, name, w, steps, warmup, dist, world, rank, local)
+        else:
+            line = run_own(args, name, w, steps, warmup, dist, world, rank, local)
+        if line is not None:
+            print(json.dumps(line), flush=True)
     if dist is not None:
         dist.destroy_process_group()
 

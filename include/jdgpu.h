@@ -134,6 +134,11 @@ int jd_host_lora_seed(jd_host_model *h, uint64_t seed, int n_alive, float ab_std
  * The reference re-draws its LoRA at every load; the sidecar lets runs share one. */
 int jd_host_lora_save(const jd_host_model *h, const char *path);
 int jd_host_lora_load(jd_host_model *h, const char *path);
+/* Decode n weights of GGUF type dt (JD_F16, JD_Q4_0, JD_Q5_0, JD_Q8_0, JD_Q4_K, JD_Q6_K; n a
+ * whole number of blocks) to f32, bit-identical to the reference's dequantisation
+ * (jd_f16_to_f32 and jd_dequant_q4_0/q5_0/q8_0/q4_k/q6_k, janusdoe.c:2545-2596).
+ * Returns JD_OK, or JD_EUNSUPPORTED for another type. */
+int jd_dequant(const void *src, float *out, uint64_t n, int dt);
 /* Write a synthetic llama-family GGUF v3 (the format gguf_host_load reads): weights
  * N(0, std) quantised per block to dtype (JD_Q8_0 or JD_Q4_K; norms f32 = 1), metadata
  * keys as the loader matches them.  Tensors are generated in parallel blocks from

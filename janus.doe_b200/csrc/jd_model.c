@@ -6,6 +6,7 @@
  */
 #define _GNU_SOURCE
 #include "../../include/jdgpu.h"
+#include "jd_quant.h"
 #include <fcntl.h>
 #include <math.h>
 #include <pthread.h>
@@ -338,16 +339,7 @@ done:
 }
 
 /* ============================= packed formats =========================== */
-/* janusdoe.c:2545-2553: exact half -> float */
-static float jd_h2f(uint16_t h) {
-    uint32_t sign = (h >> 15) & 1, ex = (h >> 10) & 0x1F, mant = h & 0x3FF, f;
-    if (ex == 0) {
-        if (mant == 0) f = sign << 31;
-        else { ex = 1; while (!(mant & 0x400)) { mant <<= 1; ex--; } mant &= 0x3FF; f = (sign << 31) | ((ex + 112) << 23) | (mant << 13); }
-    } else if (ex == 31) f = (sign << 31) | 0x7F800000 | (mant << 13);
-    else f = (sign << 31) | ((ex + 112) << 23) | (mant << 13);
-    float r; memcpy(&r, &f, 4); return r;
-}
+/* Block layouts, field extraction and the whole-tensor decoder: jd_quant.h */
 /* float -> half, round to nearest even (IEEE 754 binary16) */
 static uint16_t jd_f2h(float v) {
     uint32_t x; memcpy(&x, &v, 4);
@@ -367,68 +359,13 @@ static uint16_t jd_f2h(float v) {
     if (rem > 0x1000 || (rem == 0x1000 && (h & 1))) h++;
     return (uint16_t)(sign | h);
 }
-static float jd_hb(const uint8_t *b) { return jd_h2f((uint16_t)(b[0] | (b[1] << 8))); }
-
-/* janusdoe.c:2597-2601 jd_quant_bytes */
-static uint64_t jd_qbytes(int dt, uint64_t n) {
-    switch (dt) {
-    case JD_F32: return n * 4; case JD_F16: return n * 2; case JD_Q4_0: return (n / 32) * 18;
-    case JD_Q5_0: return (n / 32) * 22; case JD_Q8_0: return (n / 32) * 34;
-    case JD_Q4_K: return (n / 256) * 144; case JD_Q6_K: return (n / 256) * 210; default: return 0;
-    }
-}
 /* janusdoe.c:2674-2680 jd_pq_for: dtypes with a row kernel (here: a GPU kernel) */
 static int jd_has_rows(int dt, int c) {
     return (dt == JD_Q8_0 && c % 32 == 0) || (dt == JD_Q4_K && c % 256 == 0);
 }
-/* janusdoe.c:2559-2561 jd_smk4 */
-static void jd_smk4(int j, const uint8_t *sc, int *s, int *m) {
-    if (j < 4) { *s = sc[j] & 63; *m = sc[j + 4] & 63; }
-    else { *s = (sc[j + 4] & 0x0F) | ((sc[j - 4] >> 6) << 4); *m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4); }
-}
-/* janusdoe.c:2563-2610 jd_dequant_*: whole-tensor dequantisation (tok_emb and norms) */
-static int jd_dequant(const uint8_t *src, float *out, uint64_t n, int dt) {
-    if (dt == JD_F16) { for (uint64_t i = 0; i < n; i++) out[i] = jd_h2f((uint16_t)(src[2 * i] | (src[2 * i + 1] << 8))); return 0; }
-    if (dt == JD_Q4_0) {
-        for (uint64_t i = 0; i < n / 32; i++) { const uint8_t *b = src + i * 18; float d = jd_hb(b);
-            for (int j = 0; j < 16; j++) { out[i * 32 + j] = (float)((b[2 + j] & 0x0F) - 8) * d; out[i * 32 + j + 16] = (float)((b[2 + j] >> 4) - 8) * d; } }
-        return 0;
-    }
-    if (dt == JD_Q5_0) {
-        for (uint64_t i = 0; i < n / 32; i++) { const uint8_t *b = src + i * 22; float d = jd_hb(b);
-            uint32_t qh = b[2] | (b[3] << 8) | (b[4] << 16) | ((uint32_t)b[5] << 24); const uint8_t *qs = b + 6;
-            for (int j = 0; j < 16; j++) { int lo = qs[j] & 0x0F, hi = qs[j] >> 4, h0 = (qh >> j) & 1, h1 = (qh >> (j + 16)) & 1;
-                out[i * 32 + j] = (float)((lo | (h0 << 4)) - 16) * d; out[i * 32 + j + 16] = (float)((hi | (h1 << 4)) - 16) * d; } }
-        return 0;
-    }
-    if (dt == JD_Q8_0) {
-        for (uint64_t i = 0; i < n / 32; i++) { const uint8_t *b = src + i * 34; float d = jd_hb(b);
-            for (int j = 0; j < 32; j++) out[i * 32 + j] = (float)((int8_t)b[2 + j]) * d; }
-        return 0;
-    }
-    if (dt == JD_Q4_K) {
-        for (uint64_t i = 0; i < n / 256; i++) { const uint8_t *b = src + i * 144; float d = jd_hb(b), dmin = jd_hb(b + 2);
-            const uint8_t *sc = b + 4, *qs = b + 16; uint64_t oi = i * 256;
-            for (int c = 0; c < 4; c++) { int s0, m0, s1, m1; jd_smk4(2 * c, sc, &s0, &m0); jd_smk4(2 * c + 1, sc, &s1, &m1);
-                float d1 = d * s0, mm1 = dmin * m0, d2 = d * s1, mm2 = dmin * m1;
-                for (int l = 0; l < 32; l++) out[oi + 64 * c + l] = d1 * (float)(qs[32 * c + l] & 0x0F) - mm1;
-                for (int l = 0; l < 32; l++) out[oi + 64 * c + 32 + l] = d2 * (float)(qs[32 * c + l] >> 4) - mm2; } }
-        return 0;
-    }
-    if (dt == JD_Q6_K) {
-        for (uint64_t i = 0; i < n / 256; i++) { const uint8_t *b = src + i * 210, *ql = b, *qh = b + 128, *sc = b + 192;
-            float d = jd_h2f((uint16_t)(b[208] | (b[209] << 8))); uint64_t oi = i * 256;
-            for (int h = 0; h < 2; h++) { const uint8_t *qlp = ql + h * 64, *qhp = qh + h * 32, *scp = sc + h * 8; uint64_t yo = oi + h * 128;
-                for (int l = 0; l < 32; l++) { int is = l / 16;
-                    int q1 = (qlp[l] & 0x0F) | ((qhp[l] >> 0) & 3) << 4, q2 = (qlp[l + 32] & 0x0F) | ((qhp[l] >> 2) & 3) << 4;
-                    int q3 = (qlp[l] >> 4) | ((qhp[l] >> 4) & 3) << 4, q4 = (qlp[l + 32] >> 4) | ((qhp[l] >> 6) & 3) << 4;
-                    out[yo + l] = d * (float)((int8_t)scp[is]) * (float)(q1 - 32);
-                    out[yo + l + 32] = d * (float)((int8_t)scp[is + 2]) * (float)(q2 - 32);
-                    out[yo + l + 64] = d * (float)((int8_t)scp[is + 4]) * (float)(q3 - 32);
-                    out[yo + l + 96] = d * (float)((int8_t)scp[is + 6]) * (float)(q4 - 32); } } }
-        return 0;
-    }
-    return -1;
+int jd_dequant(const void *src, float *out, uint64_t n, int dt) {
+    if (!src || !out) return JD_EINVAL;
+    return jdq_decode((const uint8_t *)src, out, n, dt) == 0 ? JD_OK : JD_EUNSUPPORTED;
 }
 
 /* ============================== host model ============================== */
@@ -456,7 +393,7 @@ static int jd_rope_norm_for_arch(const char *arch) {
 static const void *jd_resolve(jd_host_priv *pv, const uint8_t *raw, const uint8_t *pend, int dt, uint64_t ne, int c,
                               int want_f32, int *out_dt) {
     *out_dt = 0;
-    uint64_t bytes = jd_qbytes(dt, ne);
+    uint64_t bytes = jdq_bytes(dt, ne);
     if (dt != 0 && bytes == 0) return NULL;
     if (bytes == 0) bytes = ne * 4;
     if (raw > pend || bytes > (uint64_t)(pend - raw)) return NULL;
@@ -464,7 +401,7 @@ static const void *jd_resolve(jd_host_priv *pv, const uint8_t *raw, const uint8_
     if (!want_f32 && jd_has_rows(dt, c)) { *out_dt = dt; return raw; }
     float *buf = malloc(ne * 4);
     if (!buf) return NULL;
-    if (jd_dequant(raw, buf, ne, dt) != 0 || jd_priv_own(pv, buf) != JD_OK) { free(buf); return NULL; }
+    if (jdq_decode(raw, buf, ne, dt) != 0 || jd_priv_own(pv, buf) != JD_OK) { free(buf); return NULL; }
     return buf;
 }
 
@@ -752,7 +689,7 @@ static void jd_quant_q4_k(const float *x, uint8_t *b) {
         if (mn[j] > maxmn) maxmn = mn[j];
     }
     uint16_t hd = jd_f2h(maxsc / 63.0f), hm = jd_f2h(maxmn / 63.0f);
-    float d = jd_h2f(hd), dmin = jd_h2f(hm);
+    float d = jdq_half(hd), dmin = jdq_half(hm);
     int s6[8], m6[8];
     for (int j = 0; j < 8; j++) {
         int s = d > 0 ? (int)lrintf(sc[j] / d) : 0, m = dmin > 0 ? (int)lrintf(mn[j] / dmin) : 0;
@@ -860,7 +797,7 @@ int jd_gguf_write_synthetic(const char *path, const char *arch, int n_layers, in
     uint64_t off = 0;
     for (int i = 0; i < n; i++) {
         t[i].off = off;
-        t[i].bytes = jd_qbytes(t[i].dt, t[i].d0 * t[i].d1);
+        t[i].bytes = jdq_bytes(t[i].dt, t[i].d0 * t[i].d1);
         off += (t[i].bytes + 31) / 32 * 32;
     }
     FILE *f = fopen(path, "wb");

@@ -10,6 +10,7 @@
 // The value of a weight is exactly the reference's dequantisation (janusdoe.c:2566-2585):
 //   Q8_0: d * q;   Q4_K: (d*s_j) * q - (dmin*m_j) for sub-block j.
 #pragma once
+#include "jd_quant.h"
 #include "jdg_kernels.cuh"
 
 namespace jdg {
@@ -21,16 +22,8 @@ struct QW {
     const uint8_t *s;
 };
 
-// janusdoe.c:2559-2561 jd_smk4: 6-bit scale and min of sub-block j from the 12 packed bytes
-__device__ __forceinline__ void smk4(int j, const uint8_t *sc, int &s, int &m) {
-    if (j < 4) {
-        s = sc[j] & 63;
-        m = sc[j + 4] & 63;
-    } else {
-        s = (sc[j + 4] & 0x0F) | ((sc[j - 4] >> 6) << 4);
-        m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
-    }
-}
+// 6-bit scale and minimum of Q4_K sub-block j from the 12 packed header bytes (jd_quant.h)
+__device__ __forceinline__ void smk4(int j, const uint8_t *sc, int &s, int &m) { jdq_q4k_scale_min(sc, j, &s, &m); }
 // exact small non-negative integer -> float (no I2F): 2^23 + n, then subtract 2^23
 __device__ __forceinline__ float u2f_small(uint32_t n) { return __uint_as_float(0x4B000000u | n) - 8388608.0f; }
 __device__ __forceinline__ float s8f(uint32_t word, int byte) {

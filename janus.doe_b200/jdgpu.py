@@ -93,6 +93,7 @@ def lib():
         "jd_host_lora_load": [C.POINTER(JdHostModel), C.c_char_p],
         "jd_gguf_write_synthetic": [C.c_char_p, C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                     C.c_float, C.c_float, C.c_int, C.c_uint64, C.c_float, C.c_int],
+        "jd_dequant": [C.c_void_p, F32P, C.c_uint64, C.c_int],
         "jdg_open": [C.c_int, C.POINTER(C.c_void_p)],
         "jdg_close": [C.c_void_p],
         "jdg_last_error": [C.c_void_p],
@@ -227,6 +228,14 @@ def write_synthetic_gguf(path, arch, n_layers, dim, hidden, n_heads, n_kv_heads,
                          seed, std=0.02, threads=0):
     check(lib().jd_gguf_write_synthetic(path.encode(), arch.encode(), n_layers, dim, hidden, n_heads, n_kv_heads,
                                         vocab, rope_theta, rms_eps, dtype, seed, std, threads))
+
+
+def dequant(W, n, dt):
+    """n weights of GGUF type dt (packed bytes W) decoded to f32 on the host."""
+    W = np.ascontiguousarray(W)
+    out = np.zeros(n, np.float32)
+    check(lib().jd_dequant(W.ctypes.data_as(C.c_void_p), _p(out, F32P), n, dt))
+    return out
 
 
 # --------------------------------------------------------------------------- GPU engine

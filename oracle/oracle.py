@@ -86,7 +86,9 @@ def trace_to_arrays(tr, L):
             sel[l, i] = tr[l].sel[i]
             w[l, i] = tr[l].w[i]
     ema = np.array([tr[l].ema for l in range(L)], np.float32)
-    return {"k": k, "sel": sel, "w": w, "ema": ema}
+    votes = np.array([[tr[l].votes[e] for e in range(MAXE)] for l in range(L)], np.float32)
+    n_alive = np.array([tr[l].n_alive for l in range(L)], np.int32)
+    return {"k": k, "sel": sel, "w": w, "ema": ema, "votes": votes, "n_alive": n_alive}
 
 
 class Oracle:
@@ -205,6 +207,34 @@ class OwnModel:
         if self.m.tok_emb:
             self.lib.jdo_own_state_free(C.byref(self.s))
             self.lib.jdo_own_free(C.byref(self.m))
+
+
+class OwnSeq:
+    """One more decode state (KV, per-layer EMA, scratch) over an OwnModel's weights, so that
+    several sequences can run on the oracle at once (one state per thread; the ctypes call
+    releases the GIL and the forward touches only its own state)."""
+
+    def __init__(self, om):
+        self.om, self.lib, self.c = om, om.lib, om.c
+        self.s = JdoOwnState()
+        if self.lib.jdo_own_state_alloc(C.byref(om.m), C.byref(self.s)) != 0:
+            raise MemoryError("oracle state alloc failed")
+        self.tr = (JdoElect * MAXL)()
+
+    def reset(self):
+        self.lib.jdo_own_state_reset(C.byref(self.om.m), C.byref(self.s))
+
+    def forward(self, tok, pos, trace=False):
+        p = self.lib.jdo_own_forward(C.byref(self.om.m), C.byref(self.s), int(tok), int(pos),
+                                     self.tr if trace else None)
+        lg = np.ctypeslib.as_array(p, shape=(self.c.vocab_size,)).copy()
+        if trace:
+            return lg, trace_to_arrays(self.tr, self.c.active_depth or self.c.depth)
+        return lg
+
+    def close(self):
+        if self.s.x:
+            self.lib.jdo_own_state_free(C.byref(self.s))
 
 
 class HostModel:
