@@ -127,6 +127,14 @@ typedef struct {
  * The LoRA parliament is allocated with lora_rank and 4 alive zero experts, consensus 0.5. */
 int jd_host_load_gguf(jd_host_model *h, const char *path, int rope_override, int lora_rank);
 void jd_host_free(jd_host_model *h); /* gguf_host_free (janusdoe.c:3449-3467) */
+/* host_tokenize (janusdoe.c:3329-3347): words split at spaces, each looked up as
+ * "\xc4\xa0word" then "word" (first 120 bytes), else byte by byte; at most max ids.
+ * Returns the number of ids (0 when the file has no vocabulary) or JD_EINVAL. */
+int jd_host_tokenize(const jd_host_model *h, const char *text, int *out, int max);
+/* host_decode_print (janusdoe.c:3348-3356) into buf: the token's printable form ("Ġ" as a
+ * space, "Ċ" as a newline, other non-ASCII bytes dropped; "<id>" for an id without text).
+ * Returns the length written (at most cap - 1) or JD_EINVAL. */
+int jd_host_token_text(const jd_host_model *h, int id, char *buf, int cap);
 /* Synthetic LoRA parliament: state = splitmix64(seed); per layer 16 vote rows uniform
  * (2u-1)*vote_amp, then experts e < n_alive draw A then B as rand_normal()*ab_std. */
 int jd_host_lora_seed(jd_host_model *h, uint64_t seed, int n_alive, float ab_std, float vote_amp);
@@ -139,10 +147,23 @@ int jd_host_lora_load(jd_host_model *h, const char *path);
  * (jd_f16_to_f32 and jd_dequant_q4_0/q5_0/q8_0/q4_k/q6_k, janusdoe.c:2545-2596).
  * Returns JD_OK, or JD_EUNSUPPORTED for another type. */
 int jd_dequant(const void *src, float *out, uint64_t n, int dt);
+/* Tensor-parallel shard of a host model for rank `rank` of `world` (the partition that
+ * jdg_host_upload_tp uploads; no counterpart in the single-process reference): query heads
+ * [q_head0, q_head0 + q_heads) with their q rows and Wo contraction columns, KV heads
+ * [kv_head0, kv_head0 + kv_heads), FFN hidden units [hidden0, hidden0 + hidden) with their
+ * gate/up rows and down contraction columns, vocabulary rows [vocab0, vocab0 + vocab).
+ * Returns JD_EINVAL when heads, KV heads or hidden units do not divide by world. */
+typedef struct {
+    int q_head0, q_heads, kv_head0, kv_heads, hidden0, hidden, vocab0, vocab;
+} jd_tp_shard;
+int jd_tp_shard_of(const jd_host_model *h, int rank, int world, jd_tp_shard *out);
 /* Write a synthetic llama-family GGUF v3 (the format gguf_host_load reads): weights
  * N(0, std) quantised per block to dtype (JD_Q8_0 or JD_Q4_K; norms f32 = 1), metadata
- * keys as the loader matches them.  Tensors are generated in parallel blocks from
- * splitmix64(seed ^ tensor index ^ block index); threads <= 0 uses all cores. */
+ * keys as the loader matches them, BOS 1 / EOS 2 and a synthetic vocabulary of `vocab`
+ * tokens (control tokens, the printable ASCII characters, then pseudo-words with and
+ * without the "\xc4\xa0" space marker, with some repeated texts).  Tensors are generated
+ * in parallel blocks from splitmix64(seed ^ tensor index ^ block index); threads <= 0
+ * uses all cores. */
 int jd_gguf_write_synthetic(const char *path, const char *arch, int n_layers, int dim, int hidden,
                             int n_heads, int n_kv_heads, int vocab, float rope_theta, float rms_eps,
                             int dtype, uint64_t seed, float std, int threads);

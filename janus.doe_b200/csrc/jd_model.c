@@ -368,10 +368,27 @@ int jd_dequant(const void *src, float *out, uint64_t n, int dt) {
     return jdq_decode((const uint8_t *)src, out, n, dt) == 0 ? JD_OK : JD_EUNSUPPORTED;
 }
 
+int jd_tp_shard_of(const jd_host_model *h, int rank, int world, jd_tp_shard *out) {
+    if (!h || !out || world < 1 || rank < 0 || rank >= world || h->n_heads < 1 || h->n_kv_heads < 1) return JD_EINVAL;
+    if (h->n_heads % world || h->n_kv_heads % world || h->hidden % world) return JD_EINVAL;
+    out->q_heads = h->n_heads / world;
+    out->q_head0 = rank * out->q_heads;
+    out->kv_heads = h->n_kv_heads / world;
+    out->kv_head0 = rank * out->kv_heads;
+    out->hidden = h->hidden / world;
+    out->hidden0 = rank * out->hidden;
+    const int per = (h->vocab + world - 1) / world;   /* ceil: the last rank may hold fewer */
+    out->vocab0 = rank * per;
+    out->vocab = out->vocab0 >= h->vocab ? 0 : (out->vocab0 + per > h->vocab ? h->vocab - out->vocab0 : per);
+    return JD_OK;
+}
+
 /* ============================== host model ============================== */
 typedef struct {
     uint8_t *map; size_t map_size;   /* file mapping, or NULL */
     void **owned; int n_owned, cap_owned;
+    int *vocab_slot;                 /* open-addressing index of the token strings (-1 empty) */
+    uint32_t vocab_mask;
 } jd_host_priv;
 
 static int jd_priv_own(jd_host_priv *p, void *buf) {
@@ -440,6 +457,106 @@ static int jd_host_finish(jd_host_model *h, int rope_override, int lora_rank) {
     h->lora_rank = lora_rank;
     h->lora_alpha = 0.1f;
     return jd_host_lora_alloc(h, 4);
+}
+
+/* ---------------------------------------------------------------------------------
+ * Host tokenizer (janusdoe.c:3329-3356): whole-word lookups of the GGUF vocabulary.
+ * The vocabulary is indexed once at load in an open-addressing hash table (FNV-1a over
+ * the token's bytes up to its first NUL, as the loader stores it); every token string maps
+ * to its lowest id, which is what a first-match scan over the ids returns. */
+#define JD_GSPACE "\xc4\xa0" /* "Ġ", the byte-level BPE space marker (UTF-8 C4 A0) */
+static uint64_t jd_fnv(uint64_t h, const unsigned char *p, size_t n) {
+    for (size_t i = 0; i < n; i++) h = (h ^ p[i]) * 0x100000001b3ull;
+    return h;
+}
+static const uint64_t JD_FNV0 = 0xcbf29ce484222325ull;
+
+/* Token text == (space marker if sp) + w[0..n), compared without building the key. */
+static int jd_tok_eq(const char *tok, int sp, const char *w, size_t n) {
+    if (sp) {
+        if ((unsigned char)tok[0] != 0xC4 || (unsigned char)tok[1] != 0xA0) return 0;
+        tok += 2;
+    }
+    return strncmp(tok, w, n) == 0 && tok[n] == '\0';
+}
+
+static int jd_vocab_index_build(jd_host_model *h) {
+    jd_host_priv *pv = (jd_host_priv *)h->priv;
+    if (!pv || !h->vocab_tokens || h->n_vocab_tokens <= 0) return JD_OK;
+    uint32_t cap = 64;
+    while (cap < 2u * (uint32_t)h->n_vocab_tokens) cap <<= 1;
+    pv->vocab_slot = malloc((size_t)cap * sizeof(int));
+    if (!pv->vocab_slot) return JD_ENOMEM;
+    for (uint32_t i = 0; i < cap; i++) pv->vocab_slot[i] = -1;
+    pv->vocab_mask = cap - 1;
+    for (int id = 0; id < h->n_vocab_tokens; id++) {
+        const char *t = h->vocab_tokens[id];
+        if (!t) continue;
+        size_t n = strlen(t);
+        uint32_t i = (uint32_t)jd_fnv(JD_FNV0, (const unsigned char *)t, n) & pv->vocab_mask;
+        for (;; i = (i + 1) & pv->vocab_mask) {
+            int o = pv->vocab_slot[i];
+            if (o < 0) { pv->vocab_slot[i] = id; break; }
+            if (strcmp(h->vocab_tokens[o], t) == 0) break; /* a lower id already holds it */
+        }
+    }
+    return JD_OK;
+}
+
+/* Lowest id whose text is (space marker if sp) + w[0..n), or -1. */
+static int jd_vocab_find(const jd_host_model *h, int sp, const char *w, size_t n) {
+    const jd_host_priv *pv = (const jd_host_priv *)h->priv;
+    if (!pv || !pv->vocab_slot) return -1;
+    uint64_t hv = sp ? jd_fnv(JD_FNV0, (const unsigned char *)JD_GSPACE, 2) : JD_FNV0;
+    hv = jd_fnv(hv, (const unsigned char *)w, n);
+    for (uint32_t i = (uint32_t)hv & pv->vocab_mask;; i = (i + 1) & pv->vocab_mask) {
+        int o = pv->vocab_slot[i];
+        if (o < 0) return -1;
+        if (jd_tok_eq(h->vocab_tokens[o], sp, w, n)) return o;
+    }
+}
+
+int jd_host_tokenize(const jd_host_model *h, const char *text, int *out, int max) {
+    if (!h || !text || !out || max < 0) return JD_EINVAL;
+    int n = 0;
+    const char *w = text;
+    while (n < max) {
+        while (*w == ' ') w++;
+        if (!*w) break;
+        const char *end = w;
+        while (*end && *end != ' ') end++;
+        const size_t len = (size_t)(end - w), key = len > 120 ? 120 : len; /* words look up by <= 120 bytes */
+        int id = jd_vocab_find(h, 1, w, key);                              /* "Ġword" */
+        if (id < 0) id = jd_vocab_find(h, 0, w, key);                      /* "word" */
+        if (id >= 0) out[n++] = id;
+        else /* byte by byte, the whole word, bytes without a token skipped */
+            for (const char *c = w; c < end && n < max; c++) {
+                const int ci = jd_vocab_find(h, 0, c, 1);
+                if (ci >= 0) out[n++] = ci;
+            }
+        w = end;
+    }
+    return n;
+}
+
+int jd_host_token_text(const jd_host_model *h, int id, char *buf, int cap) {
+    if (!h || !buf || cap < 1) return JD_EINVAL;
+    int n = 0;
+    if (id < 0 || id >= h->n_vocab_tokens || !h->vocab_tokens || !h->vocab_tokens[id]) {
+        n = snprintf(buf, (size_t)cap, "<%d>", id);
+        return n < cap ? n : cap - 1;
+    }
+    const unsigned char *s = (const unsigned char *)h->vocab_tokens[id];
+    for (int i = 0; s[i] && n < cap - 1; i++) {
+        if (s[i] == 0xC4 && (s[i + 1] == 0xA0 || s[i + 1] == 0x8A)) { /* Ġ space, Ċ newline */
+            buf[n++] = s[i + 1] == 0xA0 ? ' ' : '\n';
+            i++;
+        } else if (s[i] >= 32 && s[i] < 127) {
+            buf[n++] = (char)s[i];
+        }
+    }
+    buf[n] = '\0';
+    return n;
 }
 
 int jd_host_load_gguf(jd_host_model *h, const char *path, int rope_override, int lora_rank) {
@@ -581,6 +698,8 @@ int jd_host_load_gguf(jd_host_model *h, const char *path, int rope_override, int
     ti = NULL;
     rc = jd_host_finish(h, rope_override, lora_rank);
     if (rc != JD_OK) goto bail;
+    rc = jd_vocab_index_build(h);
+    if (rc != JD_OK) goto bail;
     return JD_OK;
 bail:
     free(ti);
@@ -592,6 +711,7 @@ void jd_host_free(jd_host_model *h) {
     if (!h) return;
     jd_host_priv *pv = (jd_host_priv *)h->priv;
     if (pv) {
+        free(pv->vocab_slot);
         for (int i = 0; i < pv->n_owned; i++) free(pv->owned[i]);
         free(pv->owned);
         if (pv->map) munmap(pv->map, pv->map_size);
@@ -762,6 +882,29 @@ static void jd_gen_tensor(uint8_t *dst, uint64_t n, int dt, uint64_t seed, float
     for (int t = 0; t < started; t++) pthread_join(th[t], NULL);
 }
 
+/* Text of token id of the synthetic vocabulary: 0-2 "<unk>" "<s>" "</s>", 3-97 the printable
+ * ASCII characters, then pseudo-words (syllables of the base-20 digits of n) as "Ġword"
+ * (even offsets) and "word" (odd offsets); every id with id % 997 == 500 repeats the text of
+ * id - 400, so lookups must return the lowest id of a text. */
+static void jd_synth_token(int id, char *buf, size_t cap) {
+    static const char *syl[20] = {"a", "e", "i", "o", "u", "ka", "ne", "ri", "so", "tu",
+                                  "ma", "le", "pi", "do", "gu", "sh", "th", "ch", "qu", "x"};
+    if (id >= 500 && id % 997 == 500) { jd_synth_token(id - 400, buf, cap); return; }
+    if (id < 3) { snprintf(buf, cap, "%s", id == 0 ? "<unk>" : id == 1 ? "<s>" : "</s>"); return; }
+    if (id < 98) { snprintf(buf, cap, "%c", (char)(32 + id - 3)); return; }
+    const int j = id - 98;
+    size_t o = 0;
+    if ((j & 1) == 0) { buf[o++] = (char)0xC4; buf[o++] = (char)0xA0; }
+    char digits[16];
+    int nd = 0;
+    for (unsigned n = (unsigned)(j / 2 + 1); n; n /= 20) digits[nd++] = (char)(n % 20);
+    while (nd-- > 0 && o + 3 < cap) {
+        const char *sy = syl[(int)digits[nd]];
+        while (*sy && o + 1 < cap) buf[o++] = *sy++;
+    }
+    buf[o] = '\0';
+}
+
 int jd_gguf_write_synthetic(const char *path, const char *arch, int n_layers, int dim, int hidden, int n_heads,
                             int n_kv_heads, int vocab, float rope_theta, float rms_eps, int dtype, uint64_t seed,
                             float std, int threads) {
@@ -803,7 +946,7 @@ int jd_gguf_write_synthetic(const char *path, const char *arch, int n_layers, in
     FILE *f = fopen(path, "wb");
     if (!f) { free(t); return JD_EIO; }
     char k[128];
-    int ok = w32(f, 0x46554747) && w32(f, 3) && w64(f, (uint64_t)n) && w64(f, 10);
+    int ok = w32(f, 0x46554747) && w32(f, 3) && w64(f, (uint64_t)n) && w64(f, 13);
     ok = ok && wkv_s(f, "general.architecture", arch);
     snprintf(k, 128, "%s.embedding_length", arch); ok = ok && wkv_u(f, k, dim);
     snprintf(k, 128, "%s.block_count", arch); ok = ok && wkv_u(f, k, n_layers);
@@ -814,6 +957,13 @@ int jd_gguf_write_synthetic(const char *path, const char *arch, int n_layers, in
     snprintf(k, 128, "%s.rope.freq_base", arch); ok = ok && wkv_f(f, k, rope_theta);
     snprintf(k, 128, "%s.attention.layer_norm_rms_epsilon", arch); ok = ok && wkv_f(f, k, rms_eps);
     snprintf(k, 128, "%s.context_length", arch); ok = ok && wkv_u(f, k, 4096);
+    ok = ok && wkv_u(f, "tokenizer.ggml.bos_token_id", 1) && wkv_u(f, "tokenizer.ggml.eos_token_id", 2);
+    ok = ok && wstr(f, "tokenizer.ggml.tokens") && w32(f, 9) && w32(f, 8) && w64(f, (uint64_t)vocab);
+    for (int id = 0; id < vocab && ok; id++) {
+        char tb[64];
+        jd_synth_token(id, tb, sizeof tb);
+        ok = wstr(f, tb);
+    }
     for (int i = 0; i < n && ok; i++) {
         ok = wstr(f, t[i].name) && w32(f, t[i].nd) && w64(f, t[i].d0);
         if (t[i].nd == 2) ok = ok && w64(f, t[i].d1);

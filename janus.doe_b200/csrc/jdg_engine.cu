@@ -17,6 +17,7 @@
 #include "jdg_engine.h"
 #include "jdg_kernels.cuh"
 #include "jdg_b1.cuh"
+#include "jdg_b1p.cuh"
 
 using namespace jdg;
 
@@ -217,6 +218,8 @@ extern "C" int jdg_own_upload(jdg_ctx *ctx, const jd_model *m, int max_batch, jd
     return JD_OK;
 }
 
+static bool b1p_usable(jdg_engine *e);
+
 int jdg_own_upload_impl(jdg_engine *e, const jd_model *m, int max_batch) {
     const jd_config &c = m->c;
     e->B_max = max_batch;
@@ -312,6 +315,34 @@ int jdg_own_upload_impl(jdg_engine *e, const jd_model *m, int max_batch) {
     CK(cudaMemcpy(e->gu_tab, gu.data(), gu.size() * sizeof(float *), cudaMemcpyHostToDevice));
     CK(cudaMemcpy(e->dn_tab, dn.data(), dn.size() * sizeof(float *), cudaMemcpyHostToDevice));
     CK(cudaMemcpy(e->alive_dev, alive.data(), alive.size() * 4, cudaMemcpyHostToDevice));
+    {   // per-layer parameter blocks of the persistent batch-1 step: header (weight pointers,
+        // alive mask, temperature), attn_norm, ffn_norm, factored vote rows wvn[r][e]
+        const size_t stride = b1p_par_stride(D);
+        std::vector<char> blk((size_t)L * stride, 0);
+        for (int l = 0; l < L; l++) {
+            const jd_layer &ly = m->layers[l];
+            char *b = blk.data() + (size_t)l * stride;
+            B1PLayer q;
+            memset(&q, 0, sizeof q);
+            q.wqkv = e->layers[l].wqkv;
+            q.wo = e->layers[l].wo;
+            q.temperature = e->layers[l].temperature;
+            for (int x = 0; x < kMaxE; x++) {
+                q.gu[x] = gu[(size_t)l * kMaxE + x];
+                q.dn[x] = dn[(size_t)l * kMaxE + x];
+                if (alive[(size_t)l * kMaxE + x]) q.alive |= 1u << x;
+            }
+            memcpy(b, &q, sizeof q);
+            float *an = reinterpret_cast<float *>(b + kPParHdr), *fn = an + D, *wvn = fn + D;
+            memcpy(an, ly.attn_norm, (size_t)D * 4);
+            memcpy(fn, ly.ffn_norm, (size_t)D * 4);
+            for (int r = 0; r < D; r++)
+                for (int x = 0; x < kMaxE; x++)
+                    wvn[r * kMaxE + x] = (q.alive >> x & 1u) ? ly.w_vote[(size_t)x * D + r] * ly.ffn_norm[r] : 0.f;
+        }
+        DALLOC(e->b1p_layers, blk.size());
+        CK(cudaMemcpy(e->b1p_layers, blk.data(), blk.size(), cudaMemcpyHostToDevice));
+    }
     // RoPE cache as alloc_run builds it (janusdoe.c:866-873)
     const int half = e->HD / 2;
     std::vector<float> cs((size_t)e->max_seq * half), sn((size_t)e->max_seq * half);
@@ -335,10 +366,12 @@ int jdg_own_upload_impl(jdg_engine *e, const jd_model *m, int max_batch) {
     DALLOC(e->att, (size_t)B * e->qd * 4);
     size_t part_a = (size_t)B * e->Hh * e->nchunk * (e->HD + 2);
     size_t part_b = (size_t)e->Hh * (e->max_seq / kB1Chunk + 1) * (e->HD + 2);
+    size_t part_c = (size_t)e->Hh * (e->max_seq / kPChunk + 1) * (e->HD + 2);
+    part_b = part_b > part_c ? part_b : part_c;
     DALLOC(e->part, (part_a > part_b ? part_a : part_b) * 4);
     DALLOC(e->amax_v, ((size_t)V / 4 + 2) * 4);
     DALLOC(e->amax_i, ((size_t)V / 4 + 2) * 4);
-    DALLOC(e->vpart, ((size_t)D / 4 + 2) * 17 * 4);
+    DALLOC(e->vpart, ((size_t)D / 4 + 2 > 1024 ? (size_t)D / 4 + 2 : 1024) * 17 * 4);
     DALLOC(e->sel_gu, kMaxE * sizeof(float *));
     DALLOC(e->ema_new, 4);
     DALLOC(e->x2, (size_t)D * 4);
@@ -347,6 +380,9 @@ int jdg_own_upload_impl(jdg_engine *e, const jd_model *m, int max_batch) {
     {
         const char *g = getenv("JDG_GENERIC");
         e->force_generic = g && g[0] == '1';
+        // batch-1 own-model path: the persistent one-kernel step ("step") or the kernel chain
+        const char *c = getenv("JDG_B1");
+        e->force_chain = !(c && !strcmp(c, "step"));
     }
     e->b1_ok = D % 128 == 0 && H % 128 == 0 && D / 128 <= 8 && H / 128 <= 12 && e->qd == D && D <= 1024 &&
                (e->HD == 64 || e->HD == 128) && D / 4 + 64 <= 1024 && e->max_seq <= 1024;
@@ -364,6 +400,7 @@ int jdg_own_upload_impl(jdg_engine *e, const jd_model *m, int max_batch) {
     rc = jdg_reset(e, -1);
     if (rc != JD_OK) return rc;
     CK(cudaStreamSynchronize(e->st));
+    b1p_usable(e);  // decided here, outside any stream capture
     return JD_OK;
 }
 
@@ -617,9 +654,107 @@ static void enqueue_own_step_b1(jdg_engine *e) {
 }
 
 
+// ------------------------------------------------------------------------------------
+// Batch-1 persistent step (jdg_b1p.cuh): one cooperative launch per decode step.
+template <int NV, int NH>
+static cudaError_t b1p_prepare(size_t smem, int *blocks_per_sm) {
+    cudaError_t r = cudaFuncSetAttribute(k_b1_step<NV, NH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (r != cudaSuccess) return r;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, k_b1_step<NV, NH>, kPThreads, smem);
+}
+template <int NV, int NH>
+static void b1p_launch(jdg_engine *e, const B1PArgs &a, size_t smem) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(e->b1p_grid);
+    cfg.blockDim = dim3(kPThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = e->st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeCooperative;
+    at[0].val.cooperative = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, k_b1_step<NV, NH>, a);
+    e->launches++;
+}
+
+static int b1p_variant(const jdg_engine *e) {
+    const int nv = e->D / 128, nh = e->hidden / 128;
+    if (nv == 2 && nh == 3) return 0;
+    if (nv == 4 && nh == 6) return 1;
+    if (nv == 6 && nh == 9) return 2;
+    return -1;
+}
+
+static size_t b1p_smem_bytes(const jdg_engine *e, int grid) {
+    const int rq = (e->qkvd + grid - 1) / grid, rd = (e->D + grid - 1) / grid;
+    return (size_t)b1p_smem(e->D, e->Hh, e->hidden, e->kmax, e->max_seq / kPChunk + 1, rq, rd).total * 4;
+}
+
+// Whether the persistent step serves this engine (decided once): shapes it is written for,
+// every CTA resident on its own SM (cooperative launch), one attention item per CTA.
+static bool b1p_usable(jdg_engine *e) {
+    if (e->b1p_grid > 0) return true;
+    if (e->b1p_grid < 0 || e->force_chain || !e->b1p_layers) return false;
+    e->b1p_grid = -1;
+    const int var = b1p_variant(e);
+    if (var < 0 || e->HD != kPHD || e->qd != e->D || e->max_seq > 1024 || e->Hh % e->KVH ||
+        e->Hh / e->KVH > kPMaxHG || e->L > JD_MAX_LAYERS)
+        return false;
+    int dev = e->ctx->device, n_sm = 0, coop = 0;
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);
+    if (!coop || n_sm < 1 || e->KVH * (e->max_seq / kPChunk + 1) > n_sm) return false;
+    const size_t smem = b1p_smem_bytes(e, n_sm);
+    int per_sm = 0;
+    cudaError_t r = var == 0 ? b1p_prepare<2, 3>(smem, &per_sm)
+                  : var == 1 ? b1p_prepare<4, 6>(smem, &per_sm)
+                             : b1p_prepare<6, 9>(smem, &per_sm);
+    if (r != cudaSuccess || per_sm < 1) {
+        cudaGetLastError();
+        return false;
+    }
+    e->b1p_grid = n_sm;
+    return true;
+}
+
+static void enqueue_own_step_b1p(jdg_engine *e) {
+    B1PArgs a = {};
+    const int G = e->b1p_grid;
+    a.layers = (const char *)e->b1p_layers;
+    a.tok_emb = e->tok_emb; a.output = e->output; a.output_norm = e->output_norm;
+    a.rope_cos = e->rope_cos; a.rope_sin = e->rope_sin;
+    a.V = e->V; a.D = e->D; a.H = e->Hh; a.KVH = e->KVH; a.hidden = e->hidden; a.qkvd = e->qkvd;
+    a.max_seq = e->max_seq; a.L = e->L; a.kmax = e->kmax; a.nch_max = e->max_seq / kPChunk + 1;
+    a.eps = e->eps; a.scale = 1.0f / sqrtf((float)e->HD); a.clamp = e->clamp;
+    a.inv_clamp = e->clamp > 0 ? 1.0f / e->clamp : 0.f;
+    a.tok = e->tok; a.pos = e->pos; a.x = e->x; a.qkv = e->qkv; a.part = e->part; a.vpart = e->vpart;
+    a.hbuf = e->hbuf; a.logits = e->logits; a.kc = e->kc; a.vc = e->vc; a.consensus = e->consensus;
+    a.tr_k = e->tr_k; a.tr_sel = e->tr_sel; a.tr_w = e->tr_w; a.tr_ema = e->tr_ema;
+    a.bar = e->tickets + 1000; a.ticket = e->tickets + 1001;
+    a.amax_v = e->amax_v; a.amax_i = e->amax_i; a.stats = e->stats;
+    a.tok_out = e->tok; a.plen = e->plen; a.prompt = e->prompt; a.hist = e->hist; a.hist_n = e->hist_n;
+    a.next_out = e->next_out; a.Hmax = e->Hmax; a.greedy_pick = e->temp <= 0.f; a.err = e->err;
+    a.tl = e->timeline;
+    a.rq = (e->qkvd + G - 1) / G;
+    a.rd = (e->D + G - 1) / G;
+    const size_t smem = b1p_smem_bytes(e, G);
+    cudaMemsetAsync(a.bar, 0, 4, e->st);
+    switch (b1p_variant(e)) {
+    case 0: b1p_launch<2, 3>(e, a, smem); break;
+    case 1: b1p_launch<4, 6>(e, a, smem); break;
+    default: b1p_launch<6, 9>(e, a, smem); break;
+    }
+    if (!a.greedy_pick) jdg_launch_pick(e, 1);
+}
+
 // One own-model decode step for slots 0..B-1 (forward_token, janusdoe.c:879-934, then
 // the next-token pick).
 static void enqueue_own_step(jdg_engine *e, int B) {
+    if (B == 1 && !e->force_generic && b1p_usable(e)) {
+        enqueue_own_step_b1p(e);
+        return;
+    }
     if (B == 1 && b1_shape_ok(e) && !e->force_generic) {
         enqueue_own_step_b1(e);
         return;

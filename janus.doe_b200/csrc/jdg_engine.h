@@ -81,6 +81,9 @@ struct jdg_engine {
     int *amax_i = nullptr;
     int b1_ok = 0;                // shapes fit the batch-1 PDL chain
     int force_generic = 0;        // JDG_GENERIC=1: use the generic kernels at batch 1
+    int force_chain = 1;          // batch 1: the kernel chain (JDG_B1=step selects the persistent step)
+    void *b1p_layers = nullptr;   // per-layer table of the persistent batch-1 step (B1PLayer[L])
+    int b1p_grid = 0;             // CTAs of the persistent step (0: not usable)
     int *tr_k = nullptr, *tr_sel = nullptr;
     float *tr_w = nullptr, *tr_ema = nullptr;
     // sampling

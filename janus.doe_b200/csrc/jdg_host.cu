@@ -252,18 +252,18 @@ static int host_upload_impl(jdg_engine *e, const jd_host_model *h, int max_batch
     HostPriv *hp = priv(e);
     const int D = h->dim, Hh = h->n_heads, KVH = h->n_kv_heads, HD = h->head_dim, HH = h->hidden;
     const int L = std::min(h->n_layers, JD_MAX_LAYERS);
-    if (Hh % world || KVH % world || HH % world) {
+    jd_tp_shard sh;
+    if (jd_tp_shard_of(h, rank, world, &sh) != JD_OK) {
         jdg_set_err(e->ctx, "heads %d/%d or hidden %d not divisible by %d ranks", Hh, KVH, HH, world);
         return JD_EINVAL;
     }
     hp->rank = rank;
     hp->world = world;
-    hp->H_loc = Hh / world;
-    hp->KVH_loc = KVH / world;
-    hp->hidden_loc = HH / world;
-    hp->V_loc = (h->vocab + world - 1) / world;
-    hp->V_off = rank * hp->V_loc;
-    if (hp->V_off + hp->V_loc > h->vocab) hp->V_loc = std::max(0, h->vocab - hp->V_off);
+    hp->H_loc = sh.q_heads;
+    hp->KVH_loc = sh.kv_heads;
+    hp->hidden_loc = sh.hidden;
+    hp->V_off = sh.vocab0;
+    hp->V_loc = sh.vocab;
     e->B_max = max_batch;
     e->L = L;
     e->D = D;
@@ -297,8 +297,8 @@ static int host_upload_impl(jdg_engine *e, const jd_host_model *h, int max_batch
         }
         // q|k|v rows of this rank's heads
         Packed pq, pk, pv, po, pg, pu, pd, pqkv, pgu;
-        const int q0 = rank * hp->H_loc * HD, q1 = q0 + hp->H_loc * HD;
-        const int k0 = rank * hp->KVH_loc * HD, k1 = k0 + hp->KVH_loc * HD;
+        const int q0 = sh.q_head0 * HD, q1 = q0 + sh.q_heads * HD;
+        const int k0 = sh.kv_head0 * HD, k1 = k0 + sh.kv_heads * HD;
         if (!repack(ly.wq, ly.wq_dt, D, range(q0, q1), 0, D, pq) || !repack(ly.wk, ly.wk_dt, D, range(k0, k1), 0, D, pk) ||
             !repack(ly.wv, ly.wv_dt, D, range(k0, k1), 0, D, pv)) {
             jdg_set_err(e->ctx, "layer %d q/k/v: dtype %d has no kernel for dim %d", l, ly.wq_dt, D);
@@ -317,7 +317,7 @@ static int host_upload_impl(jdg_engine *e, const jd_host_model *h, int max_batch
             return JD_EUNSUPPORTED;
         }
         // gate/up interleaved rows (g_i, u_i) of this rank's hidden slice
-        const int h0 = rank * hp->hidden_loc, h1 = h0 + hp->hidden_loc;
+        const int h0 = sh.hidden0, h1 = h0 + sh.hidden;
         std::vector<int> gi = range(h0, h1);
         if (!repack(ly.gate, ly.gate_dt, D, gi, 0, D, pg) || !repack(ly.up, ly.up_dt, D, gi, 0, D, pu)) {
             jdg_set_err(e->ctx, "layer %d gate/up: dtype %d has no kernel", l, ly.gate_dt);

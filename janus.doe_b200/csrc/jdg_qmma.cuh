@@ -36,57 +36,10 @@
 #include <cuda_fp16.h>
 #include <type_traits>
 
+#include "jdg_async.cuh"
 #include "jdg_hb1.cuh"
 
 namespace jdg {
-
-// ---------------------------------------------------------------------------------
-// mbarriers and bulk async copies (TMA) into shared memory.  Every wait is bounded.
-__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_u32(dst)),
-                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
-}
-// tile (x, y) of a 2-D tensor map into this CTA's shared memory
-__device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int x, int y, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-// Wait for phase `parity` of bar with an iteration limit (try_wait also suspends for a
-// bounded time per call); false when the limit ran out.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-    // the non-blocking test first: on a completed phase it costs ~13 cycles, try_wait ~150
-    uint32_t ready;
-    asm volatile("{ .reg .pred p; mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-                 : "=r"(ready)
-                 : "r"(smem_u32(bar)), "r"(parity)
-                 : "memory");
-    if (ready) return true;
-    for (int it = 0; it < (1 << 20); it++) {
-        uint32_t done;
-        asm volatile(
-            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-            : "=r"(done)
-            : "r"(smem_u32(bar)), "r"(parity)
-            : "memory");
-        if (done) return true;
-    }
-    return false;
-}
 
 constexpr int kQmRows = 128;             // weight rows per CTA (MMA M)
 constexpr int kQmTok = 32;               // tokens (B rows 0..31 hi, 32..63 lo)

@@ -9,8 +9,9 @@
  *       (ids 0..255, janusdoe.c:228); chat() samples at temperature 0.8, top-k 40.
  *   m --host model.gguf [--ask TEXT] [--rope-neox | --rope-norm] [--lora FILE]
  *               [--lora-rank R] [--gen N]
- *       host mode (janusdoe.c:3762-3795): gguf_host_load, BOS + whole-word tokenisation,
- *       greedy generation with the LoRA parliament, stop at EOS.
+ *       host mode (janusdoe.c:3762-3795): gguf_host_load, BOS + whole-word tokenisation
+ *       (jd_host_tokenize), greedy generation with the LoRA parliament, stop at EOS.
+ *   --print-ids prints the prompt's and the generated token ids after the text.
  */
 #include <stdint.h>
 #include <stdio.h>
@@ -31,56 +32,13 @@ static void usage(void) {
     printf("  --lora FILE     LoRA parliament sidecar for --host (default: drawn from --seed)\n");
     printf("  --gen N         tokens to generate (default 64)\n");
     printf("  --temp T --topk K   own-model sampling (default 0.8 and 40, as chat())\n");
+    printf("  --print-ids     also print the prompt and generated token ids\n");
 }
 
-static int find_tok(const jd_host_model *h, const char *s) {
-    for (int i = 0; i < h->n_vocab_tokens; i++)
-        if (h->vocab_tokens[i] && strcmp(h->vocab_tokens[i], s) == 0) return i;
-    return -1;
-}
-
-/* janusdoe.c:3333-3345 host_tokenize: whole words as "Ġword", then "word", else characters */
-static int host_tokenize(const jd_host_model *h, const char *prompt, int *out, int max) {
-    int n = 0;
-    char buf[160];
-    const char *w = prompt;
-    while (*w && n < max) {
-        while (*w == ' ') w++;
-        if (!*w) break;
-        const char *e = w;
-        while (*e && *e != ' ') e++;
-        int len = (int)(e - w);
-        if (len > 120) len = 120;
-        snprintf(buf, sizeof buf, "\xc4\xa0%.*s", len, w);
-        int id = find_tok(h, buf);
-        if (id < 0) {
-            snprintf(buf, sizeof buf, "%.*s", len, w);
-            id = find_tok(h, buf);
-        }
-        if (id >= 0) out[n++] = id;
-        else
-            for (const char *c = w; c < e && n < max; c++) {
-                char ch[2] = {*c, 0};
-                int ci = find_tok(h, ch);
-                if (ci >= 0) out[n++] = ci;
-            }
-        w = e;
-    }
-    return n;
-}
-
-/* janusdoe.c:3346-3356 host_decode_print */
-static void host_print(const jd_host_model *h, int id) {
-    if (id < 0 || id >= h->n_vocab_tokens || !h->vocab_tokens[id]) {
-        printf(" %d", id);
-        return;
-    }
-    const unsigned char *s = (const unsigned char *)h->vocab_tokens[id];
-    for (int i = 0; s[i]; i++) {
-        if (s[i] == 0xC4 && s[i + 1] == 0xA0) { putchar(' '); i++; }
-        else if (s[i] == 0xC4 && s[i + 1] == 0x8A) { putchar('\n'); i++; }
-        else if (s[i] >= 32 && s[i] < 127) putchar(s[i]);
-    }
+static void print_ids(const char *what, const int *ids, int n) {
+    printf("[ids] %s", what);
+    for (int i = 0; i < n; i++) printf(" %d", ids[i]);
+    printf("\n");
 }
 
 static int fail(jdg_ctx *ctx, const char *what, int rc) {
@@ -89,7 +47,7 @@ static int fail(jdg_ctx *ctx, const char *what, int rc) {
 }
 
 int main(int argc, char **argv) {
-    int depth = 0, gen = 64, topk = 40, rope_override = -1, vocab = 0, lora_rank = 16;
+    int depth = 0, gen = 64, topk = 40, rope_override = -1, vocab = 0, lora_rank = 16, show_ids = 0;
     uint64_t seed = 0;
     float temp = 0.8f;
     const char *gguf = NULL, *host = NULL, *ask = "The capital of France is", *lora = NULL;
@@ -107,6 +65,7 @@ int main(int argc, char **argv) {
         else if (!strcmp(argv[i], "--topk") && i + 1 < argc) topk = atoi(argv[++i]);
         else if (!strcmp(argv[i], "--rope-neox")) rope_override = 0;
         else if (!strcmp(argv[i], "--rope-norm")) rope_override = 1;
+        else if (!strcmp(argv[i], "--print-ids")) show_ids = 1;
         else if (!strcmp(argv[i], "--help") || !strcmp(argv[i], "-h")) { usage(); return 0; }
     }
     if (!host && depth <= 0) { usage(); return 1; }
@@ -125,7 +84,7 @@ int main(int argc, char **argv) {
         const int max_seq = 256;
         int toks[256], nt = 0;
         if (hm.bos >= 0 && hm.bos < hm.vocab) toks[nt++] = hm.bos;
-        if (hm.vocab_tokens) nt += host_tokenize(&hm, ask, toks + nt, 200);
+        if (hm.vocab_tokens) nt += jd_host_tokenize(&hm, ask, toks + nt, 200);
         if (nt == 0) toks[nt++] = 1;
         if (gen > max_seq - nt) gen = max_seq - nt;
         if ((rc = jdg_host_upload(ctx, &hm, 1, max_seq, &eng)) != JD_OK) return fail(ctx, "upload", rc);
@@ -136,11 +95,18 @@ int main(int argc, char **argv) {
         float ms = 0;
         jdg_last_run_ms(eng, &ms);
         printf("[host] %s", ask);
-        for (int i = 0; i < gen; i++) {
-            if (hm.eos >= 0 && out[i] == hm.eos) break;
-            host_print(&hm, out[i]);
+        int ng = 0;
+        for (; ng < gen; ng++) {
+            if (hm.eos >= 0 && out[ng] == hm.eos) break;
+            char tb[512];
+            if (hm.vocab_tokens && jd_host_token_text(&hm, out[ng], tb, sizeof tb) >= 0) fputs(tb, stdout);
+            else printf(" %d", out[ng]);
         }
         printf("\n[m] %d steps in %.2f ms on the GPU\n", nt - 1 + gen, ms);
+        if (show_ids) {
+            print_ids("prompt", toks, nt);
+            print_ids("generated", out, ng);
+        }
         free(out);
         jdg_engine_free(eng);
         jd_host_free(&hm);
@@ -177,6 +143,12 @@ int main(int argc, char **argv) {
             else printf("<%d>", out[i]);
         }
         printf("\n[m] %d steps in %.2f ms on the GPU\n", n - 1 + gen, ms);
+        if (show_ids) {
+            int ng = 0;
+            while (ng < gen && out[ng] != 257) ng++;
+            print_ids("prompt", ids, n);
+            print_ids("generated", out, ng);
+        }
         free(out);
         free(ids);
         jdg_engine_free(eng);

@@ -64,6 +64,11 @@ class JdHostModel(C.Structure):
                 ("vocab_tokens", C.POINTER(C.c_char_p)), ("n_vocab_tokens", C.c_int), ("priv", C.c_void_p)]
 
 
+class JdTpShard(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("q_head0", "q_heads", "kv_head0", "kv_heads", "hidden0", "hidden",
+                                        "vocab0", "vocab")]
+
+
 class JdgTrace(C.Structure):
     _fields_ = [("k", I32P), ("sel", I32P), ("w", F32P), ("ema", F32P)]
 
@@ -94,6 +99,9 @@ def lib():
         "jd_gguf_write_synthetic": [C.c_char_p, C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                     C.c_float, C.c_float, C.c_int, C.c_uint64, C.c_float, C.c_int],
         "jd_dequant": [C.c_void_p, F32P, C.c_uint64, C.c_int],
+        "jd_tp_shard_of": [C.POINTER(JdHostModel), C.c_int, C.c_int, C.c_void_p],
+        "jd_host_tokenize": [C.POINTER(JdHostModel), C.c_char_p, I32P, C.c_int],
+        "jd_host_token_text": [C.POINTER(JdHostModel), C.c_int, C.c_char_p, C.c_int],
         "jdg_open": [C.c_int, C.POINTER(C.c_void_p)],
         "jdg_close": [C.c_void_p],
         "jdg_last_error": [C.c_void_p],
@@ -212,6 +220,21 @@ class HostModel:
 
     def lora_load(self, path):
         check(lib().jd_host_lora_load(C.byref(self.h), path.encode()))
+
+    def tokenize(self, text, max_ids=256):
+        """host_tokenize: ids of the words of text (bytes or str)."""
+        out = np.zeros(max(1, max_ids), np.int32)
+        n = lib().jd_host_tokenize(C.byref(self.h), text if isinstance(text, bytes) else text.encode(),
+                                   _p(out, I32P), max_ids)
+        check(min(n, 0))
+        return [int(t) for t in out[:n]]
+
+    def token_text(self, tok):
+        """The printable form of token tok (bytes)."""
+        buf = C.create_string_buffer(512)
+        n = lib().jd_host_token_text(C.byref(self.h), int(tok), buf, 512)
+        check(min(n, 0))
+        return buf.raw[:n]
 
     def close(self):
         if self.h.priv:

@@ -133,6 +133,8 @@ class Oracle:
         L.jdo_host_state_free.argtypes = [C.POINTER(JdoHostState)]
         L.jdo_host_forward.argtypes = [C.POINTER(JdoHost), C.POINTER(JdoHostState), C.c_int, C.c_int, F32P,
                                        C.POINTER(JdoElect)]
+        L.jdo_host_elect.argtypes = [C.POINTER(JdoHost), C.c_int, C.POINTER(C.c_float), F32P, C.c_int, I32P, F32P,
+                                     C.POINTER(JdoElect)]
 
     # ---- helpers
     def splitmix64(self, x):
@@ -305,6 +307,8 @@ class Reference:
         L.jdr_host_lora_seed.argtypes = [C.c_uint64, C.c_int, C.c_float, C.c_float]
         L.jdr_host_reset_seq.argtypes = [C.c_int]
         L.jdr_host_forward.argtypes = [C.c_int, C.c_int, F32P, F32P]
+        L.jdr_host_tokenize.argtypes = [C.c_char_p, I32P, C.c_int]
+        L.jdr_host_decode_print.argtypes = [C.c_int, C.c_char_p, C.c_int]
         self.depth = 0
         self.V = 0
 
@@ -349,6 +353,16 @@ class Reference:
         self.lib.jdr_host_dims(iptr(d))
         self.hdims = d
         self.hL, self.hV = int(d[0]), int(d[6])
+
+    def host_tokenize(self, text, max_ids=256):
+        out = np.zeros(max(1, max_ids), np.int32)
+        n = self.lib.jdr_host_tokenize(text if isinstance(text, bytes) else text.encode(), iptr(out), max_ids)
+        return [int(t) for t in out[:n]]
+
+    def host_decode_print(self, tok):
+        buf = C.create_string_buffer(512)
+        n = self.lib.jdr_host_decode_print(int(tok), buf, 512)
+        return buf.raw[:max(0, n)]
 
     def host_forward(self, tok, pos):
         lg = np.zeros(self.hV, np.float32)

@@ -193,6 +193,23 @@ JDR_API int jdr_host_forward(int token, int pos, float *logits, float *ema) {
     if (ema) for (int l = 0; l < g_h.host_n_layers && l < LORA_MAX_LAYERS; l++) ema[l] = g_h.consensus[l];
     return 0;
 }
+/* host_tokenize on the loaded vocabulary (janusdoe.c:3334) */
+JDR_API int jdr_host_tokenize(const char *text, int *out, int max) { return host_tokenize(&g_h, text, out, max); }
+/* host_decode_print (janusdoe.c:3348) captured from stdout into buf (NUL-terminated) */
+JDR_API int jdr_host_decode_print(int id, char *buf, int cap) {
+    fflush(stdout);
+    FILE *saved = stdout, *mem = fmemopen(buf, (size_t)cap, "w");
+    if (!mem) return -1;
+    stdout = mem;
+    host_decode_print(&g_h, id);
+    fflush(mem);
+    long n = ftell(mem);
+    stdout = saved;
+    fclose(mem);
+    if (n >= cap) n = cap - 1;
+    buf[n] = '\0';
+    return (int)n;
+}
 JDR_API void jdr_host_free(void) {
     gguf_host_free(&g_h);
     free(g_kc); free(g_vc); g_kc = g_vc = NULL; g_max_seq = 0;

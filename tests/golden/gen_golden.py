@@ -11,6 +11,7 @@ Runs the reference source compiled by oracle/Makefile (oracle/_ref/libjdref*.so,
   own_depth12.npz  depth-12 GQA 12/4 model with 5-8 alive experts per layer, seed 3: 10 steps
   host_q8.npz / host_q4k.npz  gguf_host_forward on synthetic GGUFs (written by the library's
                    generator, identified by md5) with a seeded LoRA parliament: 10 steps
+  host_tokens.npz  host_tokenize and host_decode_print on a generated GGUF's vocabulary
 Usage:  python tests/golden/gen_golden.py
 """
 import ctypes as C
@@ -180,6 +181,37 @@ def host_fixture(name):
     os.remove(path)
 
 
+TOKEN_TEXTS = [b"", b"   ", b"a", b"zzqqy xylophone", "caf\u00e9 na\u00efve".encode(), b"k" * 150 + b" x",
+               b"!@# $%^ &*()", b"<s> </s> <unk>", b"x" * 121, bytes(range(32, 127))]
+
+
+def tokenizer_fixture():
+    """host_tokenize / host_decode_print on the synthetic vocabulary of a generated GGUF:
+    the texts above plus sentences of vocabulary words (every 7th word id from 98), and the
+    printed form of ids -2..V+2."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import conftest  # noqa: F401
+    import janus_doe_b200 as jd
+    path = "/tmp/jd_golden_tok.gguf"
+    V = 3000
+    jd.write_synthetic_gguf(path, "llama", 1, 256, 512, 4, 2, V, 1e4, 1e-5, 8, 3, 0.02)
+    ref = Reference("")
+    ref.host_load(path)
+    words = [ref.host_decode_print(i).strip() for i in range(98, V, 7)]
+    texts = TOKEN_TEXTS + [b" ".join(words[i:i + 40]) for i in range(0, len(words), 40)]
+    ids, lens = [], []
+    for t in texts:
+        r = ref.host_tokenize(t, 256)
+        ids += r
+        lens.append(len(r))
+    printed = [ref.host_decode_print(i) for i in range(-2, V + 3)]
+    ref.lib.jdr_host_free()
+    np.savez_compressed(os.path.join(OUT, "host_tokens.npz"), gguf_md5=np.array(md5(path)),
+                        texts=np.array(texts, dtype=object), ids=np.array(ids, np.int32), lens=np.array(lens, np.int32),
+                        printed=np.array(printed, dtype=object))
+    os.remove(path)
+
+
 def main():
     ref = Reference("")
     rng_fixture(ref)
@@ -190,6 +222,7 @@ def main():
     own_fixture(ref, "own_depth12", 12, 4, 8256, 1024, 3, True, 6, 4, {8})
     for name in HOST:
         host_fixture(name)
+    tokenizer_fixture()
     print("fixtures written to", OUT)
 
 

@@ -200,3 +200,39 @@ def test_product_dequant_rejects_unknown_type(jd):
     with pytest.raises(jd.JdError) as ei:
         jd.dequant(np.zeros(64, np.uint8), 32, 3)
     assert ei.value.code == jd.JD_EUNSUPPORTED
+
+
+def test_host_tokenizer_matches_reference(jd, tmp_path):
+    """Whole-word tokenisation and token printing (janusdoe.c:3329-3356) against the reference
+    build on the synthetic vocabulary: "Ġword" and "word" forms, repeated texts (lowest id),
+    unknown words spelled byte by byte, bytes without a token, words beyond 120 bytes, runs of
+    spaces, and the id limit."""
+    from oracle.oracle import Reference
+    try:
+        ref = Reference("")
+    except RuntimeError:
+        pytest.skip("reference build absent")
+    path = str(tmp_path / "tok.gguf")
+    jd.write_synthetic_gguf(path, "llama", 1, 256, 512, 4, 2, 3000, 1e4, 1e-5, 8, 3, 0.02)
+    hm = jd.HostModel(path, lora_rank=8)
+    ref.host_load(path)
+    try:
+        V = 3000
+        words = [hm.token_text(i).strip() for i in range(98, V, 7)]
+        texts = [b"", b"   ", b"a", b" ".join(words[:40]), b"  " + b"   ".join(words[40:80]) + b"  ",
+                 b"zzqqy xylophone " + words[3], "café naïve 日本".encode(),
+                 b"k" * 150 + b" " + words[5], b"!@# $%^ &*()", b"<s> </s> <unk>",
+                 b" ".join(words[80:]), b"x" * 121, bytes(range(32, 127))]
+        texts += [hm.token_text(i).strip() for i in range(400, V, 997)]
+        for t in texts:
+            for mx in (256, 5):
+                assert hm.tokenize(t, mx) == ref.host_tokenize(t, mx), (t[:60], mx)
+        assert hm.tokenize(b"anything", 0) == []
+        for i in list(range(-2, 120)) + list(range(120, V, 13)) + [V - 1, V, V + 5]:
+            assert hm.token_text(i) == ref.host_decode_print(i), i
+        # repeated texts resolve to the lowest id
+        for i in range(500, V, 997):
+            assert hm.tokenize(hm.token_text(i).strip() or b"?") == ref.host_tokenize(hm.token_text(i).strip() or b"?")
+    finally:
+        hm.close()
+        ref.lib.jdr_host_free()

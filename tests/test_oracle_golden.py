@@ -96,3 +96,22 @@ def test_host_decode(orc, jd, tmp_path, name):
             assert np.array_equal(hm.ema(), g["ema"][pos]), pos
     finally:
         hm.close()
+
+
+def test_host_tokenizer_golden(jd, tmp_path):
+    """The library's tokenizer and token printing against the reference's outputs recorded
+    in host_tokens.npz (no reference build needed)."""
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "host_tokens.npz"), allow_pickle=True)
+    path = str(tmp_path / "tok.gguf")
+    jd.write_synthetic_gguf(path, "llama", 1, 256, 512, 4, 2, 3000, 1e4, 1e-5, 8, 3, 0.02)
+    assert hashlib.md5(open(path, "rb").read()).hexdigest() == str(g["gguf_md5"])
+    hm = jd.HostModel(path, lora_rank=8)
+    try:
+        off = 0
+        for t, n in zip(g["texts"], g["lens"]):
+            assert hm.tokenize(bytes(t), 256) == [int(x) for x in g["ids"][off:off + n]], bytes(t)[:40]
+            off += n
+        for i, s in zip(range(-2, 3003), g["printed"]):
+            assert hm.token_text(i) == bytes(s), i
+    finally:
+        hm.close()

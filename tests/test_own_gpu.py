@@ -13,13 +13,16 @@ from oracle.oracle import OwnModel
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=["chain", "generic"])
+@pytest.fixture(params=["step", "chain", "generic"])
 def b1_path(request, monkeypatch):
-    """Batch 1 runs either the PDL kernel chain (default) or the generic batched kernels."""
+    """Batch 1 runs the persistent one-kernel step (JDG_B1=step), the PDL kernel chain
+    (JDG_B1=chain) or the generic batched kernels (JDG_GENERIC=1)."""
+    monkeypatch.delenv("JDG_GENERIC", raising=False)
+    monkeypatch.setenv("JDG_B1", "chain")
     if request.param == "generic":
         monkeypatch.setenv("JDG_GENERIC", "1")
-    else:
-        monkeypatch.delenv("JDG_GENERIC", raising=False)
+    elif request.param == "step":
+        monkeypatch.setenv("JDG_B1", "step")
     return request.param
 
 
