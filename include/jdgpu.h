@@ -167,6 +167,12 @@ int jd_tp_shard_of(const jd_host_model *h, int rank, int world, jd_tp_shard *out
 int jd_gguf_write_synthetic(const char *path, const char *arch, int n_layers, int dim, int hidden,
                             int n_heads, int n_kv_heads, int vocab, float rope_theta, float rms_eps,
                             int dtype, uint64_t seed, float std, int threads);
+/* The same with the output head in its own type (the layers and tok_emb in dtype); both may
+ * be JD_F32, JD_F16, JD_Q4_0, JD_Q5_0, JD_Q8_0, JD_Q4_K or JD_Q6_K (real host files often
+ * carry a Q6_K head beside Q4_K layers). */
+int jd_gguf_write_synthetic_mixed(const char *path, const char *arch, int n_layers, int dim, int hidden,
+                                  int n_heads, int n_kv_heads, int vocab, float rope_theta, float rms_eps,
+                                  int dtype, int out_dtype, uint64_t seed, float std, int threads);
 
 /* ------------------------------------------------------------------------------------
  * GPU engine.
@@ -216,6 +222,15 @@ int jdg_set_prompt(jdg_engine *e, int B, const int *tokens, int P, const int *le
  * current token at the current position, then picks the next one (the prompt's while
  * it lasts, else sampled/greedy).  Generated tokens land in the history buffer. */
 int jdg_run(jdg_engine *e, int B, int n_steps);
+/* Prompt prefill (own model; replaces the token-by-token prefill of chat(), janusdoe.c:3660):
+ * right after jdg_set_prompt, runs every prompt token of slots 0..B-1 but the last through
+ * the model as one batch per sequence and leaves each slot where len-1 jdg_run steps would:
+ * KV cache and per-layer EMA filled, at position len-1 with the last prompt token next.
+ * Elections use the EMA as an ordered scan over the tokens, so they equal token-by-token
+ * decoding's.  JD_EUNSUPPORTED for a host-model engine (its prompts run through jdg_run). */
+int jdg_prefill(jdg_engine *e, int B);
+/* Election trace of the last prefilled sequence's first n prompt tokens ([n][n_layers]...). */
+int jdg_get_prefill_trace(jdg_engine *e, int n, jdg_trace *trace);
 /* Read back: current token and position per slot, and the last n history entries. */
 int jdg_get_state(jdg_engine *e, int B, int *tok, int *pos);
 int jdg_get_history(jdg_engine *e, int B, int n, int *tokens);

@@ -361,7 +361,8 @@ static uint16_t jd_f2h(float v) {
 }
 /* janusdoe.c:2674-2680 jd_pq_for: dtypes with a row kernel (here: a GPU kernel) */
 static int jd_has_rows(int dt, int c) {
-    return (dt == JD_Q8_0 && c % 32 == 0) || (dt == JD_Q4_K && c % 256 == 0);
+    return ((dt == JD_Q8_0 || dt == JD_Q4_0 || dt == JD_Q5_0) && c % 32 == 0) ||
+           ((dt == JD_Q4_K || dt == JD_Q6_K) && c % 256 == 0) || (dt == JD_F16 && c % 4 == 0);
 }
 int jd_dequant(const void *src, float *out, uint64_t n, int dt) {
     if (!src || !out) return JD_EINVAL;
@@ -836,6 +837,61 @@ static void jd_quant_q4_k(const float *x, uint8_t *b) {
         }
 }
 
+/* Q4_0 / Q5_0 block of 32 (layouts in jd_quant.h): symmetric codes q = round(x/d) + 8 (+16)
+ * clamped to 4 (5) bits, d = max|x| / 8 (16) as f16. */
+static void jd_quant_q4_0_q5_0(const float *x, uint8_t *b, int five) {
+    float amax = 0;
+    for (int i = 0; i < 32; i++) if (fabsf(x[i]) > amax) amax = fabsf(x[i]);
+    const int bias = five ? 16 : 8, top = five ? 31 : 15;
+    uint16_t hd = jd_f2h(amax / (float)bias);
+    float d = jdq_half(hd);
+    int q[32];
+    for (int i = 0; i < 32; i++) {
+        int v = d > 0 ? (int)lrintf(x[i] / d) + bias : bias;
+        q[i] = v < 0 ? 0 : v > top ? top : v;
+    }
+    b[0] = (uint8_t)(hd & 0xFF); b[1] = (uint8_t)(hd >> 8);
+    uint8_t *nib = b + (five ? 6 : 2);
+    if (five) {
+        uint32_t fifth = 0;
+        for (int i = 0; i < 32; i++) fifth |= (uint32_t)((q[i] >> 4) & 1) << i;
+        b[2] = (uint8_t)fifth; b[3] = (uint8_t)(fifth >> 8); b[4] = (uint8_t)(fifth >> 16); b[5] = (uint8_t)(fifth >> 24);
+    }
+    for (int i = 0; i < 16; i++) nib[i] = (uint8_t)((q[i] & 15) | ((q[i + 16] & 15) << 4));
+}
+/* Q6_K superblock of 256: 16 groups of 16 with an int8 scale each, d = max|scale|/127 (f16),
+ * codes q = round(x/(d*sc)) + 32 in 6 bits, stored as low nibbles + 2-bit high parts. */
+static void jd_quant_q6_k(const float *x, uint8_t *b) {
+    float gs[16], maxgs = 0;
+    for (int g = 0; g < 16; g++) {
+        float amax = 0;
+        for (int i = 0; i < 16; i++) if (fabsf(x[16 * g + i]) > amax) amax = fabsf(x[16 * g + i]);
+        gs[g] = amax / 31.0f;
+        if (gs[g] > maxgs) maxgs = gs[g];
+    }
+    uint16_t hd = jd_f2h(maxgs / 127.0f);
+    float d = jdq_half(hd);
+    memset(b, 0, 210);
+    for (int g = 0; g < 16; g++) {
+        int sc = d > 0 ? (int)lrintf(gs[g] / d) : 0;
+        sc = sc < -128 ? -128 : sc > 127 ? 127 : sc;
+        /* scale index of group g (weights 16g..16g+15): half g/8, quarter (g%8)/2, l0 = 16*(g%2) */
+        const int hf = g / 8, u = (g % 8) / 2, li = g % 2;
+        b[192 + 8 * hf + li + 2 * u] = (uint8_t)(int8_t)sc;
+        const float step = d * (float)sc;
+        for (int i = 0; i < 16; i++) {
+            int q = step != 0 ? (int)lrintf(x[16 * g + i] / step) + 32 : 32;
+            q = q < 0 ? 0 : q > 63 ? 63 : q;
+            const int l = 16 * li + i, e = 128 * hf + 32 * u + l;  /* e == 16*g + i */
+            (void)e;
+            const int qlb = 64 * hf + l + 32 * (u & 1);
+            b[qlb] |= (uint8_t)((q & 15) << (4 * (u >> 1)));
+            b[128 + 32 * hf + l] |= (uint8_t)(((q >> 4) & 3) << (2 * u));
+        }
+    }
+    b[208] = (uint8_t)(hd & 0xFF); b[209] = (uint8_t)(hd >> 8);
+}
+
 typedef struct {
     uint8_t *dst; uint64_t n_chunks; int dt; uint64_t seed; float std; int ti;
     uint64_t next; pthread_mutex_t *mu;
@@ -853,7 +909,14 @@ static void jd_gen_chunk(const jd_gen_job *j, uint64_t ch) {
         x[i] = r * cosf(a) * j->std; x[i + 1] = r * sinf(a) * j->std;
     }
     if (j->dt == JD_Q8_0) for (int b = 0; b < 8; b++) jd_quant_q8_0(x + 32 * b, j->dst + (ch * 8 + b) * 34);
+    else if (j->dt == JD_Q4_0) for (int b = 0; b < 8; b++) jd_quant_q4_0_q5_0(x + 32 * b, j->dst + (ch * 8 + b) * 18, 0);
+    else if (j->dt == JD_Q5_0) for (int b = 0; b < 8; b++) jd_quant_q4_0_q5_0(x + 32 * b, j->dst + (ch * 8 + b) * 22, 1);
     else if (j->dt == JD_Q4_K) jd_quant_q4_k(x, j->dst + ch * 144);
+    else if (j->dt == JD_Q6_K) jd_quant_q6_k(x, j->dst + ch * 210);
+    else if (j->dt == JD_F16) for (int i = 0; i < 256; i++) {
+        uint16_t h = jd_f2h(x[i]);
+        j->dst[ch * 512 + 2 * i] = (uint8_t)(h & 0xFF); j->dst[ch * 512 + 2 * i + 1] = (uint8_t)(h >> 8);
+    }
     else memcpy(j->dst + ch * 1024, x, 1024);
 }
 static void *jd_gen_worker(void *a) {
@@ -908,10 +971,22 @@ static void jd_synth_token(int id, char *buf, size_t cap) {
 int jd_gguf_write_synthetic(const char *path, const char *arch, int n_layers, int dim, int hidden, int n_heads,
                             int n_kv_heads, int vocab, float rope_theta, float rms_eps, int dtype, uint64_t seed,
                             float std, int threads) {
+    return jd_gguf_write_synthetic_mixed(path, arch, n_layers, dim, hidden, n_heads, n_kv_heads, vocab, rope_theta,
+                                         rms_eps, dtype, dtype, seed, std, threads);
+}
+
+static int jd_synth_dtype_ok(int dt) {
+    return dt == JD_F32 || dt == JD_F16 || dt == JD_Q4_0 || dt == JD_Q5_0 || dt == JD_Q8_0 || dt == JD_Q4_K ||
+           dt == JD_Q6_K;
+}
+
+int jd_gguf_write_synthetic_mixed(const char *path, const char *arch, int n_layers, int dim, int hidden, int n_heads,
+                                  int n_kv_heads, int vocab, float rope_theta, float rms_eps, int dtype, int out_dtype,
+                                  uint64_t seed, float std, int threads) {
     if (!path || !arch || n_layers < 1 || n_layers > JD_MAX_LAYERS || dim < 1 || n_heads < 1 || n_kv_heads < 1 ||
         n_heads % n_kv_heads || dim % n_heads || vocab < 1 || hidden < 1)
         return JD_EINVAL;
-    if (dtype != JD_Q8_0 && dtype != JD_Q4_K && dtype != JD_F32) return JD_EUNSUPPORTED;
+    if (!jd_synth_dtype_ok(dtype) || !jd_synth_dtype_ok(out_dtype)) return JD_EUNSUPPORTED;
     int hd = dim / n_heads, qd = n_heads * hd, kd = n_kv_heads * hd;
     if (dim % 256 || hidden % 256 || qd % 256) return JD_EINVAL;
     int nt = 2 + 1 + 9 * n_layers;
@@ -922,7 +997,7 @@ int jd_gguf_write_synthetic(const char *path, const char *arch, int n_layers, in
 #define T1(nm, c) do { snprintf(t[n].name, 96, "%s", nm); t[n].d0 = (c); t[n].d1 = 1; t[n].nd = 1; t[n].dt = JD_F32; n++; } while (0)
     T2("token_embd.weight", dim, vocab, dtype);
     T1("output_norm.weight", dim);
-    T2("output.weight", dim, vocab, dtype);
+    T2("output.weight", dim, vocab, out_dtype);
     char nm[96];
     for (int l = 0; l < n_layers; l++) {
         snprintf(nm, 96, "blk.%d.attn_norm.weight", l); T1(nm, dim);

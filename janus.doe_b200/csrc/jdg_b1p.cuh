@@ -71,7 +71,7 @@ struct B1PArgs {
 
 // Shared-memory carve of the persistent step (floats; every piece 16-byte aligned).
 struct B1PSmem {
-    int wqkv, wo, k, v, x, att, h, q, p, ml, fm, y, xr, par0, par1, onorm, rope, total;
+    int wqkv, wo, k, v, x, att, h, q, p, po, ml, fm, y, xr, par0, par1, onorm, rope, total;
 };
 __host__ __device__ inline B1PSmem b1p_smem(int D, int H, int hidden, int kmax, int nch_max, int rq, int rd) {
     B1PSmem s;
@@ -86,6 +86,7 @@ __host__ __device__ inline B1PSmem b1p_smem(int D, int H, int hidden, int kmax, 
     s.h = take(kmax * hidden);
     s.q = take(kPMaxHG * kPHD);
     s.p = take(kPMaxHG * kPChunk);
+    s.po = take(4 * kPMaxHG * kPHD);
     s.ml = take(H * nch_max * 2);
     s.fm = take(H * nch_max);
     s.y = take(rd * kMaxE);
@@ -102,9 +103,6 @@ __device__ __forceinline__ unsigned long long p_gtimer() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
     return t;
-}
-__device__ __forceinline__ void p_prefetch_l2(const void *p) {
-    asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p));
 }
 
 constexpr unsigned long long kPWaitNs = 200ull * 1000 * 1000;  // 200 ms: any wait longer is an error
@@ -140,11 +138,33 @@ __device__ __forceinline__ bool p_grid_sync(const B1PArgs &a, unsigned &gen, int
                 }
             }
         }
-        __threadfence();
+        if (a.tl) {  // the next phase starts here in this CTA
+            const unsigned long long t = p_gtimer();
+            atomicMin(a.tl + 3 * (slot + 1), t);
+            atomicMax(a.tl + 3 * (256 + slot + 1) + 2, t);
+        }
         *s_flag = ok;
     }
     __syncthreads();
     return *s_flag != 0;
+}
+
+// L2 prefetch of [p, p + bytes) by the bulk-copy engine (no shared memory involved), split
+// into pieces of at most 64 KB with 16-byte granularity.
+__device__ __forceinline__ void p_prefetch_range(const void *p, size_t bytes) {
+    const char *c = reinterpret_cast<const char *>(p);
+    while (bytes >= 16) {
+        const uint32_t n = (uint32_t)(bytes > 65536 ? 65536 : bytes) & ~15u;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(c), "r"(n) : "memory");
+        c += n;
+        bytes -= n;
+    }
+}
+// This CTA's share (1/G, by blockIdx) of [p, p + bytes) prefetched into L2.
+__device__ __forceinline__ void p_prefetch_share(const void *p, size_t bytes) {
+    const size_t per = ((bytes + gridDim.x - 1) / gridDim.x + 15) & ~(size_t)15;
+    const size_t off = per * blockIdx.x;
+    if (off < bytes) p_prefetch_range(reinterpret_cast<const char *>(p) + off, off + per > bytes ? bytes - off : per);
 }
 
 // Wait for phase `parity` of a shared-memory mbarrier (bulk copies landing) with the same
@@ -289,6 +309,7 @@ static __global__ __launch_bounds__(kPThreads, 1) void k_b1_step(B1PArgs a) {
     const B1PSmem L = b1p_smem(D, a.H, a.hidden, a.kmax, a.nch_max, a.rq, a.rd);
     float *s_wqkv = sm + L.wqkv, *s_wo = sm + L.wo, *s_k = sm + L.k, *s_v = sm + L.v, *s_x = sm + L.x;
     float *s_att = sm + L.att, *s_h = sm + L.h, *s_q = sm + L.q, *s_p = sm + L.p, *s_ml = sm + L.ml;
+    float *s_po = sm + L.po;
     float *s_fm = sm + L.fm, *s_y = sm + L.y, *s_xr = sm + L.xr, *s_onorm = sm + L.onorm, *s_rope = sm + L.rope;
     float *s_par[2] = {sm + L.par0, sm + L.par1};
 
@@ -393,13 +414,25 @@ static __global__ __launch_bounds__(kPThreads, 1) void k_b1_step(B1PArgs a) {
         bulk_g2s(s_rope, a.rope_cos + (size_t)p * (kPHD / 2), kPHD / 2 * 4, &mb[5]);
         bulk_g2s(s_rope + kPHD / 2, a.rope_sin + (size_t)p * (kPHD / 2), kPHD / 2 * 4, &mb[5]);
     }
-    if (a.tl && blockIdx.x == 0 && tid == 0) atomicMin(a.tl, p_gtimer());
+    const size_t gu_bytes = (size_t)2 * a.hidden * D * 4;
+    if (tid < kMaxE) {  // layer 0's gate/up matrices of every alive expert, this CTA's share, into L2
+        const float *g = reinterpret_cast<const B1PLayer *>(a.layers)->gu[tid];
+        if (g) p_prefetch_share(g, gu_bytes);
+    }
+    if (a.tl && tid == 0) {
+        const unsigned long long t = p_gtimer();
+        atomicMin(a.tl, t);
+        atomicMin(a.tl + 3, t);
+        atomicMax(a.tl + 3 * 257 + 2, t);
+    }
     bool misc_ready = false;
+    bool par_ready = false;  // the next layer's parameters were already waited for (in P5)
 
     for (int l = 0; l < a.L; l++) {
         const int slot = 1 + 5 * l;
         if (l + 1 < a.L) stage_par(l + 1);  // its buffer was last read by layer l-1
-        wait_bar(3 + (l & 1));
+        if (!par_ready) wait_bar(3 + (l & 1));
+        par_ready = false;
         const float *par = s_par[l & 1];
         const B1PLayer &ly = *reinterpret_cast<const B1PLayer *>(par);
         const float *attn_norm = par + kPParHdr / 4, *ffn_norm = attn_norm + D, *wvn = ffn_norm + D;
@@ -436,7 +469,6 @@ static __global__ __launch_bounds__(kPThreads, 1) void k_b1_step(B1PArgs a) {
             if (l + 1 < a.L) release_and([&] { stage_qkv(l + 1); });
         }
         if (!p_grid_sync(a, gen, &s_flag, slot)) { drain(); return; }
-        if (a.tl && blockIdx.x == 0 && tid == 0) a.tl[3 * (slot + 1)] = p_gtimer();
         // ---------------- P2: attention item ----------------
         if (has_item) {
             if (!misc_ready) {
@@ -497,22 +529,33 @@ static __global__ __launch_bounds__(kPThreads, 1) void k_b1_step(B1PArgs a) {
                 }
             }
             __syncthreads();
-            for (int idx = tid; idx < hg * kPHD; idx += kPThreads) {  // o[j][d] = sum_t p[j][t] v[t][d]
-                const int j = idx / kPHD, d = idx % kPHD;
-                const float *pj = s_p + j * kPChunk;
-                float o0 = 0.f, o1 = 0.f;
-                int t = 0;
-                for (; t + 1 < i_nt; t += 2) {
-                    o0 = fmaf(pj[t], s_v[t * kPKRow + d], o0);
-                    o1 = fmaf(pj[t + 1], s_v[(t + 1) * kPKRow + d], o1);
+            {   // o[j][d] = sum_t p[j][t] v[t][d]: four position groups per (head, 4 dims), the
+                // group partials then summed in group order
+                const int nu = hg * (kPHD / 4);
+                for (int idx = tid; idx < 4 * nu; idx += kPThreads) {
+                    const int grp = idx / nu, u = idx % nu, j = u / (kPHD / 4), d4 = u % (kPHD / 4);
+                    const float *pj = s_p + j * kPChunk;
+                    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int t = grp; t < i_nt; t += 4) {
+                        const float pt = pj[t];
+                        const float4 v = reinterpret_cast<const float4 *>(s_v + t * kPKRow)[d4];
+                        o.x = fmaf(pt, v.x, o.x);
+                        o.y = fmaf(pt, v.y, o.y);
+                        o.z = fmaf(pt, v.z, o.z);
+                        o.w = fmaf(pt, v.w, o.w);
+                    }
+                    reinterpret_cast<float4 *>(s_po)[grp * nu + u] = o;
                 }
-                if (t < i_nt) o0 = fmaf(pj[t], s_v[t * kPKRow + d], o0);
-                a.part[((size_t)(ig * hg + j) * a.nch_max + ich) * (kPHD + 2) + d] = o0 + o1;
+                __syncthreads();
+                for (int idx = tid; idx < hg * kPHD; idx += kPThreads) {
+                    const int j = idx / kPHD, d = idx % kPHD, u4 = j * kPHD + d;
+                    const float o = ((s_po[u4] + s_po[4 * nu + u4]) + s_po[8 * nu + u4]) + s_po[12 * nu + u4];
+                    a.part[((size_t)(ig * hg + j) * a.nch_max + ich) * (kPHD + 2) + d] = o;
+                }
             }
             if (l + 1 < a.L) release_and([&] { stage_kv(l + 1); });
         }
         if (!p_grid_sync(a, gen, &s_flag, slot + 1)) { drain(); return; }
-        if (a.tl && blockIdx.x == 0 && tid == 0) a.tl[3 * (slot + 2)] = p_gtimer();
         // ---------------- P3: merge, Wo rows, partial votes ----------------
         {
             constexpr int AR = (NV * 128 + kPThreads - 1) / kPThreads;  // att elements per thread
@@ -592,7 +635,6 @@ static __global__ __launch_bounds__(kPThreads, 1) void k_b1_step(B1PArgs a) {
             if (l + 1 < a.L) release_and([&] { stage_wo(l + 1); });
         }
         if (!p_grid_sync(a, gen, &s_flag, slot + 2)) { drain(); return; }
-        if (a.tl && blockIdx.x == 0 && tid == 0) a.tl[3 * (slot + 3)] = p_gtimer();
         // ---------------- P4: election + gate/up of the elected experts ----------------
         {
             if (warp < 5) {  // totals in a fixed order: 8 strided partial sums per slot, then a tree
@@ -629,28 +671,15 @@ static __global__ __launch_bounds__(kPThreads, 1) void k_b1_step(B1PArgs a) {
             }
             const float inv = eo.inv;
             for (int i = tid; i < D; i += kPThreads) s_x[i] = __fmul_rn(__fmul_rn(s_x[i], inv), ffn_norm[i]);
-            // warm L2 with the down rows this CTA reads in P5 (and the LM head after the last layer)
-            {
-                const int lines = a.hidden * 4 / 128;
-                for (int idx = tid; idx < k * nr * lines; idx += kPThreads) {
-                    const int ki = idx / (nr * lines), rem = idx % (nr * lines), rr = rem / lines, li = rem % lines;
-                    const float *w = ly.dn[eo.sel[ki]];
-                    if (w) p_prefetch_l2(reinterpret_cast<const char *>(w + (size_t)(d0 + rr) * a.hidden) + 128 * li);
-                }
-                if (l + 1 == a.L) {
-                    const int rl = D * 4 / 128, gw = G * kPWarps;
-                    for (int row = blockIdx.x * kPWarps * 2; row < a.V; row += 2 * gw)
-                        for (int idx = tid; idx < 2 * kPWarps * rl; idx += kPThreads) {
-                            const int r = row + idx / rl;
-                            if (r < a.V) p_prefetch_l2(reinterpret_cast<const char *>(a.output + (size_t)r * D) + 128 * (idx % rl));
-                        }
-                }
+            // the down rows this CTA reads in P5, into L2 while the gate/up rows stream
+            if (tid < k * nr) {
+                const int ki = tid / nr, rr = tid % nr;
+                p_prefetch_range(ly.dn[eo.sel[ki]] + (size_t)(d0 + rr) * a.hidden, (size_t)a.hidden * 4);
             }
-            __syncthreads();
-            const int nunits = k * a.hidden, gw = G * kPWarps;
             if (tid < kMaxE) s_gub[tid] = tid < k ? ly.gu[eo.sel[tid]] : nullptr;
             __syncthreads();
             const float *const *gub = s_gub;
+            const int nunits = k * a.hidden, gw = G * kPWarps;
             float4 ga[NV], ua[NV], gb[NV], ub[NV];
             auto load_unit = [&](int uu, float4(&g4)[NV], float4(&u4)[NV]) {
                 if (uu >= nunits) return;
@@ -687,10 +716,21 @@ static __global__ __launch_bounds__(kPThreads, 1) void k_b1_step(B1PArgs a) {
             }
         }
         if (!p_grid_sync(a, gen, &s_flag, slot + 3)) { drain(); return; }
-        if (a.tl && blockIdx.x == 0 && tid == 0) a.tl[3 * (slot + 4)] = p_gtimer();
         // ---------------- P5: down rows of the elected experts, combined into x ----------------
         {
             const int k = eo.k;
+            // layer l's gate/up rows are consumed: bring the next layer's alive experts' gate/up
+            // matrices (all of them: the election is not known yet) or the LM head into L2
+            if (l + 1 < a.L) {
+                wait_bar(3 + ((l + 1) & 1));
+                par_ready = true;
+                if (tid < kMaxE) {
+                    const float *g = reinterpret_cast<const B1PLayer *>(s_par[(l + 1) & 1])->gu[tid];
+                    if (g) p_prefetch_share(g, gu_bytes);
+                }
+            } else if (tid == 0) {
+                p_prefetch_share(a.output, (size_t)a.V * D * 4);
+            }
             p_g2s<8>(reinterpret_cast<float4 *>(s_h), reinterpret_cast<const float4 *>(a.hbuf), k * a.hidden / 4);
             __syncthreads();
             // pairs (row rr, election slot ki) per warp, two in flight
@@ -732,11 +772,9 @@ static __global__ __launch_bounds__(kPThreads, 1) void k_b1_step(B1PArgs a) {
             fence_proxy_async_smem();  // s_par[l & 1] is refilled (layer l + 2) after the barrier
         }
         if (!p_grid_sync(a, gen, &s_flag, slot + 4)) { drain(); return; }
-        if (a.tl && blockIdx.x == 0 && tid == 0 && l + 1 < a.L) a.tl[3 * (slot + 5)] = p_gtimer();
     }
     // ---------------- LM head: final RMSNorm, logits, greedy pick ----------------
     const int lslot = 1 + 5 * a.L;
-    if (a.tl && blockIdx.x == 0 && tid == 0) a.tl[3 * lslot] = p_gtimer();
     if (!misc_ready) wait_bar(5);
     p_g2s<4>(reinterpret_cast<float4 *>(s_x), reinterpret_cast<const float4 *>(a.x), D / 4);
     __syncthreads();

@@ -748,6 +748,8 @@ static void enqueue_own_step_b1p(jdg_engine *e) {
     if (!a.greedy_pick) jdg_launch_pick(e, 1);
 }
 
+static void own_batch_layers(jdg_engine *e, int B, int prefill_slot);
+
 // One own-model decode step for slots 0..B-1 (forward_token, janusdoe.c:879-934, then
 // the next-token pick).
 static void enqueue_own_step(jdg_engine *e, int B) {
@@ -759,6 +761,24 @@ static void enqueue_own_step(jdg_engine *e, int B) {
         enqueue_own_step_b1(e);
         return;
     }
+    own_batch_layers(e, B, -1);
+    const int D = e->D, V = e->V;
+    if (B == 1) {
+        launch_gemv1(e, EPI_STORE, e->output, V, D, e->x, e->output_norm, 1, e->logits);
+    } else {
+        k_rmsnorm<<<B, 256, 0, e->st>>>(e->x, e->output_norm, e->xb, D, e->eps);
+        e->launches++;
+        SgemmArgs a = {};
+        a.A = e->xb; a.lda = D; a.M = B; a.W = e->output; a.N = V; a.K = D; a.C = e->logits; a.ldc = V;
+        launch_sgemm<EPI_STORE>(e, a, B, 1);
+    }
+    jdg_launch_pick(e, B);
+}
+
+// Embedding and every layer for B rows (sequences at one position each, or, with
+// prefill_slot >= 0, the prompt tokens of that sequence at positions 0..B-1, whose elections
+// take the EMA as a scan over the tokens in order).
+static void own_batch_layers(jdg_engine *e, int B, int prefill_slot) {
     const int D = e->D, H = e->hidden, L = e->L, V = e->V, qd = e->qd;
     const float scale = 1.0f / sqrtf((float)e->HD);
     k_embed<<<B, 256, 0, e->st>>>(e->tok_emb, V, D, e->tok, e->x, e->err);
@@ -783,7 +803,20 @@ static void enqueue_own_step(jdg_engine *e, int B) {
             a.A = e->att; a.lda = qd; a.M = B; a.W = ly.wo; a.N = D; a.K = qd; a.C = e->x; a.ldc = D;
             launch_sgemm<EPI_ADD>(e, a, B, 1);
         }
-        jdg_launch_elect(e, l, B, e->x, ly.ffn_norm, ly.w_vote, e->alive_dev + (size_t)l * kMaxE, ly.temperature, 0);
+        if (prefill_slot < 0) {
+            jdg_launch_elect(e, l, B, e->x, ly.ffn_norm, ly.w_vote, e->alive_dev + (size_t)l * kMaxE, ly.temperature, 0);
+        } else {
+            ElectArgs a = {};
+            a.x = e->x; a.norm_w = ly.ffn_norm; a.eps = e->eps; a.D = D; a.host = 0; a.w_vote = ly.w_vote;
+            a.alive = e->alive_dev + (size_t)l * kMaxE; a.temperature = ly.temperature; a.consensus = e->consensus;
+            a.L = L; a.l = l; a.xb = e->xb; a.kcnt = e->kcnt; a.sel = e->sel; a.selw = e->selw; a.tr_k = e->tr_k;
+            a.tr_sel = e->tr_sel; a.tr_w = e->tr_w; a.tr_ema = e->tr_ema;
+            a.prefill = 1; a.pf_votes = e->pf_votes; a.pf_cs = e->pf_cs;
+            a.pf_cons = e->consensus + (size_t)prefill_slot * L + l;
+            k_elect<<<B, 256, (size_t)D * 4, e->st>>>(a);
+            k_elect_scan<<<1, 256, (size_t)B * 4, e->st>>>(a, B);
+            e->launches += 2;
+        }
         const float *const *gu = e->gu_tab + (size_t)l * kMaxE;
         const float *const *dn = e->dn_tab + (size_t)l * kMaxE;
         if (e->n_alive[l] < 2) continue;  // parliament_elect returns 0 below MIN_EXPERTS
@@ -809,16 +842,6 @@ static void enqueue_own_step(jdg_engine *e, int B) {
             e->launches += 2;
         }
     }
-    if (B == 1) {
-        launch_gemv1(e, EPI_STORE, e->output, V, D, e->x, e->output_norm, 1, e->logits);
-    } else {
-        k_rmsnorm<<<B, 256, 0, e->st>>>(e->x, e->output_norm, e->xb, D, e->eps);
-        e->launches++;
-        SgemmArgs a = {};
-        a.A = e->xb; a.lda = D; a.M = B; a.W = e->output; a.N = V; a.K = D; a.C = e->logits; a.ldc = V;
-        launch_sgemm<EPI_STORE>(e, a, B, 1);
-    }
-    jdg_launch_pick(e, B);
 }
 
 static int enqueue_step(jdg_engine *e, int B) {
@@ -943,6 +966,8 @@ extern "C" int jdg_set_prompt(jdg_engine *e, int B, const int *tokens, int P, co
         memcpy(&pr[(size_t)b * e->Pmax], tokens + (size_t)b * P, (size_t)len[b] * 4);
         t0[b] = tokens[(size_t)b * P];
     }
+    e->prompt_host = pr;
+    e->plen_host.assign(len, len + B);
     CK(cudaMemcpyAsync(e->prompt, pr.data(), pr.size() * 4, cudaMemcpyHostToDevice, e->st));
     CK(cudaMemcpyAsync(e->plen, len, B * 4, cudaMemcpyHostToDevice, e->st));
     CK(cudaMemcpyAsync(e->tok, t0.data(), B * 4, cudaMemcpyHostToDevice, e->st));
@@ -970,6 +995,114 @@ extern "C" int jdg_run(jdg_engine *e, int B, int n_steps) {
     return check_err(e);
 }
 
+// ------------------------------------------------------------------------------------
+// Prompt prefill of the own model: the prompt tokens of a sequence go through the layers as
+// one batch of rows (GEMMs over all tokens, causal attention over the slot's KV cache), and
+// each layer's elections take the EMA as an ordered scan over the tokens, so that k, the
+// elected experts and the EMA are those of token-by-token decoding (janusdoe.c:3660).
+static int pf_alloc(jdg_engine *e) {
+    if (e->pf_x) return JD_OK;
+    const size_t P = e->max_seq, D = e->D, H = e->hidden, L = e->L;
+    DALLOC(e->pf_x, P * D * 4);
+    DALLOC(e->pf_xb, P * D * 4);
+    DALLOC(e->pf_qkv, P * e->qkvd * 4);
+    DALLOC(e->pf_att, P * e->qd * 4);
+    DALLOC(e->pf_part, P * e->Hh * e->nchunk * (e->HD + 2) * 4);
+    DALLOC(e->pf_hbuf, (size_t)kMaxE * P * H * 4);
+    DALLOC(e->pf_ybuf, (size_t)kMaxE * P * D * 4);
+    DALLOC(e->pf_kcnt, P * 4);
+    DALLOC(e->pf_sel, P * kMaxE * 4);
+    DALLOC(e->pf_selw, P * kMaxE * 4);
+    DALLOC(e->pf_rcnt, kMaxE * 4);
+    DALLOC(e->pf_ridx, kMaxE * P * 4);
+    DALLOC(e->pf_pairrow, P * kMaxE * 4);
+    DALLOC(e->pf_pos, P * 4);
+    DALLOC(e->pf_votes, P * kMaxE * 4);
+    DALLOC(e->pf_cs, P * 4);
+    DALLOC(e->pf_tr_k, P * L * 4);
+    DALLOC(e->pf_tr_sel, P * L * kMaxE * 4);
+    DALLOC(e->pf_tr_w, P * L * kMaxE * 4);
+    DALLOC(e->pf_tr_ema, P * L * 4);
+    std::vector<int> iota(P);
+    for (size_t i = 0; i < P; i++) iota[i] = (int)i;
+    CK(cudaMemcpy(e->pf_pos, iota.data(), P * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemset(e->pf_hbuf, 0, (size_t)kMaxE * P * H * 4));
+    CK(cudaMemset(e->pf_ybuf, 0, (size_t)kMaxE * P * D * 4));
+    return JD_OK;
+}
+
+// The batch rows of the engine, swapped for the prefill's while it runs.
+struct OwnRows {
+    int *tok, *pos, *kcnt, *sel, *rcnt, *ridx, *pairrow, *tr_k, *tr_sel;
+    float *x, *xb, *qkv, *att, *part, *hbuf, *ybuf, *selw, *kc, *vc, *tr_w, *tr_ema;
+    long kv_bstride;
+};
+static OwnRows rows_of(const jdg_engine *e) {
+    return OwnRows{e->tok, e->pos, e->kcnt, e->sel, e->rcnt, e->ridx, e->pairrow, e->tr_k, e->tr_sel,
+                   e->x, e->xb, e->qkv, e->att, e->part, e->hbuf, e->ybuf, e->selw, e->kc, e->vc, e->tr_w,
+                   e->tr_ema, e->kv_bstride};
+}
+static void set_rows(jdg_engine *e, const OwnRows &r) {
+    e->tok = r.tok; e->pos = r.pos; e->kcnt = r.kcnt; e->sel = r.sel; e->rcnt = r.rcnt; e->ridx = r.ridx;
+    e->pairrow = r.pairrow; e->tr_k = r.tr_k; e->tr_sel = r.tr_sel; e->x = r.x; e->xb = r.xb; e->qkv = r.qkv;
+    e->att = r.att; e->part = r.part; e->hbuf = r.hbuf; e->ybuf = r.ybuf; e->selw = r.selw; e->kc = r.kc;
+    e->vc = r.vc; e->tr_w = r.tr_w; e->tr_ema = r.tr_ema; e->kv_bstride = r.kv_bstride;
+}
+
+extern "C" int jdg_prefill(jdg_engine *e, int B) {
+    if (!e || B < 1 || B > e->B_max || (int)e->plen_host.size() < B) return JD_EINVAL;
+    if (e->kind != 0) {
+        jdg_set_err(e->ctx, "jdg_prefill: the host model's prompts run through jdg_run");
+        return JD_EUNSUPPORTED;
+    }
+    cudaSetDevice(e->ctx->device);
+    int rc = pf_alloc(e);
+    if (rc != JD_OK) return rc;
+    CK(cudaEventRecord(e->ev0, e->st));
+    const OwnRows saved = rows_of(e);
+    for (int b = 0; b < B; b++) {
+        const int n = e->plen_host[b] - 1;  // every prompt token but the last
+        if (n >= 1) {
+            OwnRows r = saved;
+            r.tok = e->prompt + (size_t)b * e->Pmax;
+            r.pos = e->pf_pos;
+            r.kcnt = e->pf_kcnt; r.sel = e->pf_sel; r.selw = e->pf_selw; r.rcnt = e->pf_rcnt; r.ridx = e->pf_ridx;
+            r.pairrow = e->pf_pairrow; r.tr_k = e->pf_tr_k; r.tr_sel = e->pf_tr_sel; r.tr_w = e->pf_tr_w;
+            r.tr_ema = e->pf_tr_ema; r.x = e->pf_x; r.xb = e->pf_xb; r.qkv = e->pf_qkv; r.att = e->pf_att;
+            r.part = e->pf_part; r.hbuf = e->pf_hbuf; r.ybuf = e->pf_ybuf;
+            r.kc = saved.kc + (size_t)b * saved.kv_bstride;
+            r.vc = saved.vc + (size_t)b * saved.kv_bstride;
+            r.kv_bstride = 0;  // every row is a position of this one sequence
+            set_rows(e, r);
+            own_batch_layers(e, n, b);
+            set_rows(e, saved);
+            e->pf_last_n = n;
+        }
+        // the slot continues at the last prompt token, as after n decode steps
+        const int last = e->prompt_host[(size_t)b * e->Pmax + n];
+        CK(cudaMemcpyAsync(e->tok + b, &last, 4, cudaMemcpyHostToDevice, e->st));
+        CK(cudaMemcpyAsync(e->pos + b, &n, 4, cudaMemcpyHostToDevice, e->st));
+        CK(cudaStreamSynchronize(e->st));  // `last` and `n` are stack values
+    }
+    CK(cudaEventRecord(e->ev1, e->st));
+    CK(cudaEventSynchronize(e->ev1));
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, e->ev0, e->ev1));
+    e->last_ms = ms;
+    return check_err(e);
+}
+
+extern "C" int jdg_get_prefill_trace(jdg_engine *e, int n, jdg_trace *tr) {
+    if (!e || !tr || n < 1 || n > e->pf_last_n || !e->pf_tr_k) return JD_EINVAL;
+    cudaSetDevice(e->ctx->device);
+    const size_t L = e->L;
+    if (tr->k) CK(cudaMemcpy(tr->k, e->pf_tr_k, (size_t)n * L * 4, cudaMemcpyDeviceToHost));
+    if (tr->sel) CK(cudaMemcpy(tr->sel, e->pf_tr_sel, (size_t)n * L * kMaxE * 4, cudaMemcpyDeviceToHost));
+    if (tr->w) CK(cudaMemcpy(tr->w, e->pf_tr_w, (size_t)n * L * kMaxE * 4, cudaMemcpyDeviceToHost));
+    if (tr->ema) CK(cudaMemcpy(tr->ema, e->pf_tr_ema, (size_t)n * L * 4, cudaMemcpyDeviceToHost));
+    return JD_OK;
+}
+
 extern "C" int jdg_last_run_ms(jdg_engine *e, float *ms) {
     if (!e || !ms) return JD_EINVAL;
     *ms = e->last_ms;
@@ -994,21 +1127,23 @@ extern "C" int jdg_reset_stats(jdg_engine *e) {
     return JD_OK;
 }
 
-// Debug: enable (n_slots > 0) or read the batch-1 kernel timeline.  out[slot*3 + {0,1,2}] =
-// earliest CTA entry, earliest return from the dependency wait, latest CTA exit (ns).
+// Debug: enable (n_slots > 0) or read the batch-1 kernel timeline.  Kernel chain:
+// out[slot*3 + {0,1,2}] = earliest CTA entry, earliest return from the dependency wait,
+// latest CTA exit (ns).  Persistent step: slot 1 + 5*layer + phase holds {earliest phase
+// start, -, latest phase end} and slot 256 + the same index {-, -, latest phase start}.
 extern "C" int jdg_debug_timeline(jdg_engine *e, int n_slots, uint64_t *out) {
-    if (!e || n_slots < 0) return JD_EINVAL;
+    if (!e || n_slots < 0 || n_slots > 512) return JD_EINVAL;
     cudaSetDevice(e->ctx->device);
     if (!e->timeline) {
-        DALLOC(e->timeline, (size_t)3 * 256 * 8);
+        DALLOC(e->timeline, (size_t)3 * 512 * 8);
         drop_graphs(e);
     }
     if (out) {
         CK(cudaMemcpyAsync(out, e->timeline, (size_t)3 * n_slots * 8, cudaMemcpyDeviceToHost, e->st));
         CK(cudaStreamSynchronize(e->st));
     }
-    std::vector<unsigned long long> init(3 * 256);
-    for (int i = 0; i < 256; i++) {
+    std::vector<unsigned long long> init(3 * 512);
+    for (int i = 0; i < 512; i++) {
         init[3 * i] = ~0ull;
         init[3 * i + 1] = ~0ull;
         init[3 * i + 2] = 0;

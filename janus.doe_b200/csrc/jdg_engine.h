@@ -86,6 +86,14 @@ struct jdg_engine {
     int b1p_grid = 0;             // CTAs of the persistent step (0: not usable)
     int *tr_k = nullptr, *tr_sel = nullptr;
     float *tr_w = nullptr, *tr_ema = nullptr;
+    // prompt prefill buffers (own model, allocated at the first jdg_prefill; rows = tokens)
+    float *pf_x = nullptr, *pf_xb = nullptr, *pf_qkv = nullptr, *pf_att = nullptr, *pf_part = nullptr;
+    float *pf_hbuf = nullptr, *pf_ybuf = nullptr, *pf_selw = nullptr, *pf_votes = nullptr, *pf_cs = nullptr;
+    int *pf_kcnt = nullptr, *pf_sel = nullptr, *pf_rcnt = nullptr, *pf_ridx = nullptr, *pf_pairrow = nullptr;
+    int *pf_pos = nullptr, *pf_tr_k = nullptr, *pf_tr_sel = nullptr;
+    float *pf_tr_w = nullptr, *pf_tr_ema = nullptr;
+    int pf_last_n = 0;                 // tokens of the last prefill (its trace rows)
+    std::vector<int> prompt_host, plen_host;  // copies of the last jdg_set_prompt
     // sampling
     float temp = 0.f;
     int top_k = 0;

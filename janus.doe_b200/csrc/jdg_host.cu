@@ -126,8 +126,27 @@ const QmMaps *qm_find_maps(jdg_engine *e, const QW &w) {
     return nullptr;
 }
 
-int block_elems(int dt) { return dt == JD_Q8_0 ? 32 : dt == JD_Q4_K ? 256 : dt == JD_F32 ? 1 : 0; }
-size_t block_bytes(int dt) { return dt == JD_Q8_0 ? 34 : dt == JD_Q4_K ? 144 : dt == JD_F32 ? 4 : 0; }
+// source block geometry of the GGUF types the upload accepts packed
+int block_elems(int dt) {
+    switch (dt) {
+    case JD_F32: case JD_F16: return 1;
+    case JD_Q4_0: case JD_Q5_0: case JD_Q8_0: return 32;
+    case JD_Q4_K: case JD_Q6_K: return 256;
+    default: return 0;
+    }
+}
+size_t block_bytes(int dt) {
+    switch (dt) {
+    case JD_F32: return 4;
+    case JD_F16: return 2;
+    case JD_Q4_0: return 18;
+    case JD_Q5_0: return 22;
+    case JD_Q8_0: return 34;
+    case JD_Q4_K: return 144;
+    case JD_Q6_K: return 210;
+    default: return 0;
+    }
+}
 
 // register bucket of the batch-1 chain for a packed matrix (0: not supported there)
 int hb1_maxc(const QW &w) {
@@ -155,6 +174,52 @@ bool repack(const void *src, int dt, int src_cols, const std::vector<int> &rows,
         out.q.resize((size_t)out.rows * cols * 4);
         for (size_t r = 0; r < rows.size(); r++)
             memcpy(&out.q[r * cols * 4], base + (size_t)rows[r] * row_bytes + (size_t)c0 * 4, (size_t)cols * 4);
+    } else if (dt == JD_F16) {
+        // half -> float is exact: stored as f32 rows
+        out.dt = JD_F32;
+        out.q.resize((size_t)out.rows * cols * 4);
+        for (size_t r = 0; r < rows.size(); r++) {
+            const uint8_t *rp = base + (size_t)rows[r] * row_bytes + (size_t)c0 * 2;
+            float *o = reinterpret_cast<float *>(&out.q[r * cols * 4]);
+            for (int j = 0; j < cols; j++) o[j] = jdq_half_at(rp + 2 * j);
+        }
+    } else if (dt == JD_Q4_0 || dt == JD_Q5_0) {
+        // 4/5-bit codes with one f16 scale per 32 weights: the value (q - 8)*d or (q - 16)*d is
+        // an int8 code times the same scale, so they are stored in the Q8_0 layout exactly
+        const int bias = dt == JD_Q4_0 ? 8 : 16;
+        out.dt = JD_Q8_0;
+        out.q.resize((size_t)out.rows * cols);
+        out.s.resize((size_t)out.rows * nb * 2);
+        for (size_t r = 0; r < rows.size(); r++) {
+            const uint8_t *rp = base + (size_t)rows[r] * row_bytes + (size_t)(c0 / 32) * bb;
+            for (int b = 0; b < nb; b++) {
+                const uint8_t *blk = rp + (size_t)b * bb, *nib = blk + (dt == JD_Q4_0 ? 2 : 6);
+                const uint32_t fifth = dt == JD_Q5_0 ? (uint32_t)blk[2] | ((uint32_t)blk[3] << 8) |
+                                                           ((uint32_t)blk[4] << 16) | ((uint32_t)blk[5] << 24)
+                                                     : 0u;
+                memcpy(&out.s[(r * nb + b) * 2], blk, 2);
+                int8_t *codes = reinterpret_cast<int8_t *>(&out.q[r * cols + (size_t)b * 32]);
+                for (int w = 0; w < 32; w++) {
+                    const int q = ((w < 16 ? nib[w] : nib[w - 16] >> 4) & 15) | (int)(((fifth >> w) & 1u) << 4);
+                    codes[w] = (int8_t)(q - bias);
+                }
+            }
+        }
+    } else if (dt == JD_Q6_K) {
+        // low-nibble bytes of every superblock [rows][K/2], then the 2-bit high parts
+        // [rows][K/4], both in file order; headers [rows][K/256][32]: 16 int8 scales, f16 d
+        out.q.resize((size_t)out.rows * cols / 2 + (size_t)out.rows * cols / 4);
+        out.s.assign((size_t)out.rows * nb * 32, 0);
+        uint8_t *ql = out.q.data(), *qh = out.q.data() + (size_t)out.rows * cols / 2;
+        for (size_t r = 0; r < rows.size(); r++) {
+            const uint8_t *rp = base + (size_t)rows[r] * row_bytes + (size_t)(c0 / 256) * 210;
+            for (int b = 0; b < nb; b++) {
+                const uint8_t *blk = rp + (size_t)b * 210;
+                memcpy(ql + r * (cols / 2) + (size_t)b * 128, blk, 128);
+                memcpy(qh + r * (cols / 4) + (size_t)b * 64, blk + 128, 64);
+                memcpy(&out.s[(r * nb + b) * 32], blk + 192, 18);
+            }
+        }
     } else if (dt == JD_Q8_0) {
         out.q.resize((size_t)out.rows * cols);
         out.s.resize((size_t)out.rows * nb * 2);
@@ -165,7 +230,7 @@ bool repack(const void *src, int dt, int src_cols, const std::vector<int> &rows,
                 memcpy(&out.q[r * cols + (size_t)b * 32], rp + (size_t)b * 34 + 2, 32);
             }
         }
-    } else {
+    } else if (dt == JD_Q4_K) {
         out.q.resize((size_t)out.rows * cols / 2);
         out.s.resize((size_t)out.rows * nb * 16);
         for (size_t r = 0; r < rows.size(); r++) {
@@ -175,6 +240,8 @@ bool repack(const void *src, int dt, int src_cols, const std::vector<int> &rows,
                 memcpy(&out.q[r * (cols / 2) + (size_t)b * 128], rp + (size_t)b * 144 + 16, 128);
             }
         }
+    } else {
+        return false;
     }
     return true;
 }
@@ -541,6 +608,7 @@ static void launch_q(jdg_engine *e, const QW &w, const float *X, int ldx, int M,
         switch (w.dt) {
         case JD_Q8_0: k_qgemv<8, EPI><<<grid, 256, sm, e->st>>>(a); break;
         case JD_Q4_K: k_qgemv<12, EPI><<<grid, 256, sm, e->st>>>(a); break;
+        case JD_Q6_K: k_qgemv<14, EPI><<<grid, 256, sm, e->st>>>(a); break;
         default: k_qgemv<0, EPI><<<grid, 256, sm, e->st>>>(a); break;
         }
     } else if (tc) {
@@ -610,6 +678,7 @@ static void launch_q(jdg_engine *e, const QW &w, const float *X, int ldx, int M,
         switch (w.dt) {
         case JD_Q8_0: k_qgemm<8, EPI><<<grid, 256, sm, e->st>>>(a); break;
         case JD_Q4_K: k_qgemm<12, EPI><<<grid, 256, sm, e->st>>>(a); break;
+        case JD_Q6_K: k_qgemm<14, EPI><<<grid, 256, sm, e->st>>>(a); break;
         default: k_qgemm<0, EPI><<<grid, 256, sm, e->st>>>(a); break;
         }
     }
@@ -622,9 +691,11 @@ int jdg_host_set_attrs(jdg_engine *e) {
 #define SETA(K) cudaFuncSetAttribute(K, cudaFuncAttributeMaxDynamicSharedMemorySize, big)
     SETA((k_qgemv<8, EPI_STORE>)); SETA((k_qgemv<8, EPI_ADD>)); SETA((k_qgemv<8, EPI_SWIGLU>));
     SETA((k_qgemv<12, EPI_STORE>)); SETA((k_qgemv<12, EPI_ADD>)); SETA((k_qgemv<12, EPI_SWIGLU>));
+    SETA((k_qgemv<14, EPI_STORE>)); SETA((k_qgemv<14, EPI_ADD>)); SETA((k_qgemv<14, EPI_SWIGLU>));
     SETA((k_qgemv<0, EPI_STORE>)); SETA((k_qgemv<0, EPI_ADD>)); SETA((k_qgemv<0, EPI_SWIGLU>));
     SETA((k_qgemm<8, EPI_STORE>)); SETA((k_qgemm<8, EPI_ADD>)); SETA((k_qgemm<8, EPI_SWIGLU>));
     SETA((k_qgemm<12, EPI_STORE>)); SETA((k_qgemm<12, EPI_ADD>)); SETA((k_qgemm<12, EPI_SWIGLU>));
+    SETA((k_qgemm<14, EPI_STORE>)); SETA((k_qgemm<14, EPI_ADD>)); SETA((k_qgemm<14, EPI_SWIGLU>));
     SETA((k_qgemm<0, EPI_STORE>)); SETA((k_qgemm<0, EPI_ADD>)); SETA((k_qgemm<0, EPI_SWIGLU>));
     SETA((k_hb1_attn<64>)); SETA((k_hb1_attn<128>));
 #define SETA_Q(K)                                                                                             \

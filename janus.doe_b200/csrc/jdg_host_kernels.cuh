@@ -6,7 +6,11 @@
 //   Q8_0: q[row][K] int8 codes; s[row][K/32] f16 scales d         (34 bytes / 32 weights)
 //   Q4_K: q[row][K/2] bytes (each 144-byte superblock's 128 code bytes, in file order);
 //         s[row][K/256] 16-byte headers {f16 d, f16 dmin, 12 packed 6-bit scales/mins}
+//   Q6_K: q = [row][K/2] low-nibble bytes then [row][K/4] 2-bit high parts (file order per
+//         superblock); s[row][K/256] 32-byte headers {16 int8 scales, f16 d}  (7 bits/weight)
 //   F32:  q[row][K] floats
+// Q4_0 / Q5_0 arrive in the Q8_0 layout (their codes minus 8 / 16 are int8 codes with the
+// same per-32 f16 scale) and F16 as F32: both exact.
 // The value of a weight is exactly the reference's dequantisation (janusdoe.c:2566-2585):
 //   Q8_0: d * q;   Q4_K: (d*s_j) * q - (dmin*m_j) for sub-block j.
 #pragma once
@@ -16,7 +20,7 @@
 namespace jdg {
 
 struct QW {
-    int dt;            // JD_F32 (0), JD_Q8_0 (8), JD_Q4_K (12)
+    int dt;            // JD_F32 (0), JD_Q8_0 (8), JD_Q4_K (12), JD_Q6_K (14)
     int rows, cols;
     const uint8_t *q;
     const uint8_t *s;
@@ -108,6 +112,43 @@ __device__ __forceinline__ float qrow_dot(const QW &w, int row, const float *xs,
             acc = fmaf(-mm1, xs_l, acc);
             acc = fmaf(d2, sh, acc);
             acc = fmaf(-mm2, xs_h, acc);
+        }
+    } else if (DT == 14) {
+        // Q6_K: a lane takes 16 low-nibble bytes of one half superblock (bytes b..b+15 of its
+        // 64) and the 16 high-part bytes they share: 16 weights of quarter u = b/32 (low
+        // nibbles) and 16 of quarter u + 2 (high nibbles), one int8 scale each
+        const uint8_t *qr = w.q + (size_t)row * (K / 2);
+        const uint8_t *hr = w.q + (size_t)w.rows * (K / 2) + (size_t)row * (K / 4);
+        const uint8_t *sr = w.s + (size_t)row * (K / 256) * 32;
+#pragma unroll 2
+        for (int byte0 = lane * 16; byte0 < K / 2; byte0 += 512) {
+            const int sb = byte0 >> 7, o = byte0 & 127, hf = o >> 6, b = o & 63, u = b >> 5, l0 = b & 31;
+            const uint4 lv = ld_stream_u4(qr + byte0);
+            const uint4 hv = ld_stream_u4(hr + (size_t)sb * 64 + 32 * hf + l0);
+            const uint8_t *hd = sr + (size_t)sb * 32;
+            const float d = h2f((uint16_t)(hd[16] | (hd[17] << 8)));
+            const float dl = d * (float)(int8_t)hd[8 * hf + (l0 >> 4) + 2 * u];
+            const float dh = d * (float)(int8_t)hd[8 * hf + (l0 >> 4) + 2 * (u + 2)];
+            const int e0 = sb * 256 + 128 * hf + b;
+            const float4 *xl = reinterpret_cast<const float4 *>(xs + e0);
+            const float4 *xh = reinterpret_cast<const float4 *>(xs + e0 + 64);
+            const uint32_t lw[4] = {lv.x, lv.y, lv.z, lv.w}, hw[4] = {hv.x, hv.y, hv.z, hv.w};
+            float sl = 0.f, sh = 0.f;
+#pragma unroll
+            for (int cc = 0; cc < 4; cc++) {
+                const float4 a4 = xl[cc], b4 = xh[cc];
+                const float av[4] = {a4.x, a4.y, a4.z, a4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const uint32_t qlb = (lw[cc] >> (8 * j)) & 0xFFu, qhb = (hw[cc] >> (8 * j)) & 0xFFu;
+                    const uint32_t q0 = (qlb & 15u) | (((qhb >> (2 * u)) & 3u) << 4);
+                    const uint32_t q1 = (qlb >> 4) | (((qhb >> (2 * u + 4)) & 3u) << 4);
+                    sl = fmaf(u2f_small(q0) - 32.0f, av[j], sl);
+                    sh = fmaf(u2f_small(q1) - 32.0f, bv[j], sh);
+                }
+            }
+            acc = fmaf(dl, sl, acc);
+            acc = fmaf(dh, sh, acc);
         }
     } else {
         const float *wr = reinterpret_cast<const float *>(w.q) + (size_t)row * K;
@@ -209,6 +250,27 @@ __device__ __forceinline__ void dequant_tile(const QW &w, int n0, int k0, float 
                     Ws[r][64 * c + 16 * h + j] = __fsub_rn(__fmul_rn(d1, u2f_small(byte & 15u)), mm1);
                     Ws[r][64 * c + 32 + 16 * h + j] = __fsub_rn(__fmul_rn(d2, u2f_small(byte >> 4)), mm2);
                 }
+            }
+        } else {
+            for (int j = 0; j < 64; j++) Ws[r][64 * c + j] = 0.f;
+        }
+    } else if (DT == 14) {
+        // 64 rows x 1 superblock: thread t handles row t/4; c = t%4 picks half c/2 and its low
+        // (quarters 0, 1) or high (quarters 2, 3) nibbles: 64 weights, value (d*sc)*(q - 32)
+        const int r = tid >> 2, c = tid & 3, row = n0 + r, hf = c >> 1, part = c & 1;
+        if (row < w.rows) {
+            const int K = w.cols, sb = k0 >> 8;
+            const uint8_t *ql = w.q + (size_t)row * (K / 2) + (size_t)sb * 128 + 64 * hf;
+            const uint8_t *qh = w.q + (size_t)w.rows * (K / 2) + (size_t)row * (K / 4) + (size_t)sb * 64 + 32 * hf;
+            const uint8_t *hd = w.s + ((size_t)row * (K / 256) + sb) * 32;
+            const float d = h2f((uint16_t)(hd[16] | (hd[17] << 8)));
+#pragma unroll 4
+            for (int b = 0; b < 64; b++) {
+                const int u = (b >> 5) + 2 * part;
+                const uint32_t qlb = ql[b], qhb = qh[b & 31];
+                const uint32_t q = (part ? qlb >> 4 : qlb & 15u) | (((qhb >> (2 * u)) & 3u) << 4);
+                const float ds = __fmul_rn(d, (float)(int8_t)hd[8 * hf + ((b & 31) >> 4) + 2 * u]);
+                Ws[r][128 * hf + 64 * part + b] = __fmul_rn(ds, u2f_small(q) - 32.0f);
             }
         } else {
             for (int j = 0; j < 64; j++) Ws[r][64 * c + j] = 0.f;

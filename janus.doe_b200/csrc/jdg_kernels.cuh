@@ -532,7 +532,76 @@ struct ElectArgs {
     float *selw;           // [B][16]
     int *tr_k, *tr_sel;
     float *tr_w, *tr_ema;  // [B][L](*16)
+    // prompt prefill (own model): rows are the tokens of one sequence; k_elect only writes
+    // each token's votes and consensus measure, k_elect_scan runs the EMA over the tokens
+    int prefill;
+    float *pf_votes;       // [B][16]
+    float *pf_cs;          // [B]
+    float *pf_cons;        // the sequence's EMA of this layer (in: before the prompt, out: after)
 };
+
+// The selection half of parliament_elect (janusdoe.c:811-837) / host_parliament_elect
+// (janusdoe.c:3067-3085) from the votes v[e] of the alive slots and the updated EMA.
+__device__ __forceinline__ int elect_select(const float *v, const int *alive_idx, int na, float ema, int host,
+                                            float temperature, int *sel, float *w) {
+    int k = (int)__fmul_rn((float)na, __fsub_rn(1.0f, ema));
+    if (k < 2) k = 2;
+    if (k > na) k = na;
+    bool used[kMaxE];
+    for (int e = 0; e < kMaxE; e++) used[e] = false;
+    for (int ki = 0; ki < k; ki++) {
+        float bv = -1e30f;
+        int bi = host ? -1 : 0;
+        for (int i = 0; i < na; i++) {
+            const int e = alive_idx[i];
+            if (!used[e] && v[e] > bv) {
+                bv = v[e];
+                bi = e;
+            }
+        }
+        if (bi < 0)
+            for (int i = 0; i < na; i++)
+                if (!used[alive_idx[i]]) {
+                    bi = alive_idx[i];
+                    break;
+                }
+        sel[ki] = bi;
+        w[ki] = v[bi];
+        used[bi] = true;
+    }
+    const float temp = host ? 1.0f : (temperature > 0.05f ? temperature : 1.0f);
+    float mx = w[0];
+    for (int i = 1; i < k; i++)
+        if (w[i] > mx) mx = w[i];
+    float sum = 0.f;
+    for (int i = 0; i < k; i++) {
+        float arg = __fsub_rn(w[i], mx);
+        if (!host) arg = arg / temp;
+        w[i] = expf(arg);
+        sum = __fadd_rn(sum, w[i]);
+    }
+    if (!host || (sum > 0.0f && isfinite(sum))) {
+        for (int i = 0; i < k; i++) w[i] = w[i] / sum;
+    } else {
+        for (int i = 0; i < k; i++) w[i] = 1.0f / (float)k;
+    }
+    return k;
+}
+
+// consensus measure of one election: fminf(1, std / (|mean| + 1)) over the alive votes
+__device__ __forceinline__ float elect_cs(const float *v, const int *alive_idx, int na) {
+    float mean = 0.f;
+    for (int i = 0; i < na; i++) mean = __fadd_rn(mean, v[alive_idx[i]]);
+    mean = mean / (float)na;
+    float var = 0.f;
+    for (int i = 0; i < na; i++) {
+        const float dd = __fsub_rn(v[alive_idx[i]], mean);
+        var = __fadd_rn(var, __fmul_rn(dd, dd));
+    }
+    var = var / (float)na;
+    return fminf(1.0f, sqrtf(__fadd_rn(var, 1e-8f)) / __fadd_rn(fabsf(mean), 1.0f));
+}
+
 static __global__ __launch_bounds__(256) void k_elect(ElectArgs a) {
     extern __shared__ float xs[];
     __shared__ float red[32];
@@ -590,6 +659,11 @@ static __global__ __launch_bounds__(256) void k_elect(ElectArgs a) {
     int alive_idx[kMaxE], na = 0;
     for (int e = 0; e < kMaxE; e++)
         if (a.alive[e]) alive_idx[na++] = e;
+    if (a.prefill) {  // votes and the consensus measure only; the EMA is a scan over the prompt
+        for (int e = 0; e < kMaxE; e++) a.pf_votes[(size_t)b * kMaxE + e] = a.alive[e] ? votes[e] : 0.f;
+        a.pf_cs[b] = na >= 2 ? elect_cs(votes, alive_idx, na) : 0.f;
+        return;
+    }
     float *cons = a.consensus + (size_t)b * a.L + a.l;
     int k = 0;
     int sel[kMaxE];
@@ -671,6 +745,47 @@ static __global__ __launch_bounds__(256) void k_elect(ElectArgs a) {
     for (int i = 0; i < kMaxE; i++) {
         a.tr_sel[tl * kMaxE + i] = i < k ? sel[i] : -1;
         a.tr_w[tl * kMaxE + i] = i < k ? w[i] : 0.f;
+    }
+}
+
+// Prompt prefill: the EMA of one layer over the B prompt tokens in order
+// (c_t = 0.9 c_{t-1} + 0.1 cs_t, the recurrence parliament_elect applies token by token,
+// janusdoe.c:809), then every token's election from its own EMA value in parallel.
+static __global__ __launch_bounds__(256) void k_elect_scan(ElectArgs a, int B) {
+    extern __shared__ float ema_t[];  // [B]
+    __shared__ int alive_idx[kMaxE], na_s;
+    if (threadIdx.x == 0) {
+        int na = 0;
+        for (int e = 0; e < kMaxE; e++)
+            if (a.alive[e]) alive_idx[na++] = e;
+        na_s = na;
+        float c = *a.pf_cons;
+        if (na >= 2)
+            for (int t = 0; t < B; t++) {
+                c = __fadd_rn(__fmul_rn(0.9f, c), __fmul_rn(0.1f, a.pf_cs[t]));
+                ema_t[t] = c;
+            }
+        else
+            for (int t = 0; t < B; t++) ema_t[t] = c;
+        *a.pf_cons = c;
+    }
+    __syncthreads();
+    const int na = na_s;
+    for (int t = threadIdx.x; t < B; t += blockDim.x) {
+        int sel[kMaxE];
+        float w[kMaxE], v[kMaxE];
+        for (int e = 0; e < kMaxE; e++) v[e] = a.pf_votes[(size_t)t * kMaxE + e];
+        const int k = na >= 2 ? elect_select(v, alive_idx, na, ema_t[t], 0, a.temperature, sel, w) : 0;
+        a.kcnt[t] = k;
+        const size_t tl = (size_t)t * a.L + a.l;
+        a.tr_k[tl] = k;
+        a.tr_ema[tl] = ema_t[t];
+        for (int i = 0; i < kMaxE; i++) {
+            a.sel[t * kMaxE + i] = i < k ? sel[i] : -1;
+            a.selw[t * kMaxE + i] = i < k ? w[i] : 0.f;
+            a.tr_sel[tl * kMaxE + i] = i < k ? sel[i] : -1;
+            a.tr_w[tl * kMaxE + i] = i < k ? w[i] : 0.f;
+        }
     }
 }
 

@@ -98,6 +98,9 @@ def lib():
         "jd_host_lora_load": [C.POINTER(JdHostModel), C.c_char_p],
         "jd_gguf_write_synthetic": [C.c_char_p, C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                     C.c_float, C.c_float, C.c_int, C.c_uint64, C.c_float, C.c_int],
+        "jd_gguf_write_synthetic_mixed": [C.c_char_p, C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                          C.c_int, C.c_float, C.c_float, C.c_int, C.c_int, C.c_uint64, C.c_float,
+                                          C.c_int],
         "jd_dequant": [C.c_void_p, F32P, C.c_uint64, C.c_int],
         "jd_tp_shard_of": [C.POINTER(JdHostModel), C.c_int, C.c_int, C.c_void_p],
         "jd_host_tokenize": [C.POINTER(JdHostModel), C.c_char_p, I32P, C.c_int],
@@ -116,6 +119,8 @@ def lib():
         "jdg_reset": [C.c_void_p, C.c_int],
         "jdg_set_prompt": [C.c_void_p, C.c_int, I32P, C.c_int, I32P, U64P],
         "jdg_run": [C.c_void_p, C.c_int, C.c_int],
+        "jdg_prefill": [C.c_void_p, C.c_int],
+        "jdg_get_prefill_trace": [C.c_void_p, C.c_int, C.POINTER(JdgTrace)],
         "jdg_get_state": [C.c_void_p, C.c_int, I32P, I32P],
         "jdg_get_history": [C.c_void_p, C.c_int, C.c_int, I32P],
         "jdg_step": [C.c_void_p, C.c_int, I32P, I32P, U64P, I32P, F32P, C.POINTER(JdgTrace)],
@@ -248,9 +253,14 @@ class HostModel:
 
 
 def write_synthetic_gguf(path, arch, n_layers, dim, hidden, n_heads, n_kv_heads, vocab, rope_theta, rms_eps, dtype,
-                         seed, std=0.02, threads=0):
-    check(lib().jd_gguf_write_synthetic(path.encode(), arch.encode(), n_layers, dim, hidden, n_heads, n_kv_heads,
-                                        vocab, rope_theta, rms_eps, dtype, seed, std, threads))
+                         seed, std=0.02, threads=0, out_dtype=None):
+    if out_dtype is None:
+        check(lib().jd_gguf_write_synthetic(path.encode(), arch.encode(), n_layers, dim, hidden, n_heads, n_kv_heads,
+                                            vocab, rope_theta, rms_eps, dtype, seed, std, threads))
+    else:
+        check(lib().jd_gguf_write_synthetic_mixed(path.encode(), arch.encode(), n_layers, dim, hidden, n_heads,
+                                                  n_kv_heads, vocab, rope_theta, rms_eps, dtype, out_dtype, seed, std,
+                                                  threads))
 
 
 def dequant(W, n, dt):
@@ -337,6 +347,19 @@ class Engine:
         ms = C.c_float(0)
         lib().jdg_last_run_ms(self.h, C.byref(ms))
         return ms.value
+
+    def prefill(self, B):
+        """Batched prompt prefill of slots 0..B-1 (after set_prompt); returns device ms."""
+        self._ck(lib().jdg_prefill(self.h, B))
+        ms = C.c_float(0)
+        lib().jdg_last_run_ms(self.h, C.byref(ms))
+        return ms.value
+
+    def prefill_trace(self, n):
+        """Elections of the last prefilled sequence's first n tokens, as trace arrays [n][L]."""
+        t, d = self._trace_bufs(n)
+        self._ck(lib().jdg_get_prefill_trace(self.h, n, C.byref(t)))
+        return d
 
     def state(self, B):
         t = np.zeros(B, np.int32)

@@ -137,8 +137,29 @@ def test_synthetic_writer_rejects_bad_shapes(jd, tmp_path):
     with pytest.raises(jd.JdError):
         jd.write_synthetic_gguf(str(tmp_path / "x.gguf"), "llama", 1, 300, 256, 4, 4, 10, 1e4, 1e-6, 12, 1)
     with pytest.raises(jd.JdError) as ei:
-        jd.write_synthetic_gguf(str(tmp_path / "x.gguf"), "llama", 1, 256, 256, 4, 4, 10, 1e4, 1e-6, 2, 1)
+        jd.write_synthetic_gguf(str(tmp_path / "x.gguf"), "llama", 1, 256, 256, 4, 4, 10, 1e4, 1e-6, 13, 1)
     assert ei.value.code == jd.JD_EUNSUPPORTED
+
+
+@pytest.mark.parametrize("dt", [1, 2, 6, 14])
+def test_synthetic_writer_other_types_match_oracle(jd, orc, tmp_path, dt):
+    """Output heads in F16 / Q4_0 / Q5_0 / Q6_K: the product loader keeps them packed, and the
+    oracle's decoder and the library's decoder give the same weights from the file."""
+    import ctypes as C
+    path = str(tmp_path / "m.gguf")
+    jd.write_synthetic_gguf(path, "llama", 1, 512, 512, 8, 8, 300, 1e4, 1e-5, 8, 3, 0.02, out_dtype=dt)
+    hm = jd.HostModel(path, lora_rank=8)
+    om = OHost(orc, path, 8, -1, 8)
+    try:
+        assert hm.h.output_dt == dt and om.h.output_dt == dt
+        rb = {1: 1024, 2: 16 * 18, 6: 16 * 22, 14: 2 * 210}[dt]
+        W = np.frombuffer(C.string_at(hm.h.output, 300 * rb), np.uint8).copy()
+        a, b = jd.dequant(W, 300 * 512, dt), orc.dequant(W, 300 * 512, dt)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+        assert 0.005 < float(np.std(a)) < 0.05   # the quantiser kept the N(0, 0.02) scale
+    finally:
+        om.close()
+        hm.close()
 
 
 def test_open_without_gpu_reports(jd):

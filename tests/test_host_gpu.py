@@ -22,6 +22,13 @@ SMALL = {
 }
 # full-width layers of the 1.1B Q8_0 and 8B Q4_K shapes (fewer layers, smaller vocabulary):
 # rows of 5632 and 14336 weights exercise the widest register buckets of the batch-1 chain
+# output heads and layers in the other GGUF types the loader keeps packed
+MIXED = {
+    # name: arch, dim, layers, heads, kv, ffn, vocab, layer dtype, head dtype, theta, lora rank, adapters
+    "q4k_q6k_head": ("llama", 512, 2, 8, 2, 1024, 2000, 12, 14, 5e5, 16, 8),
+    "q4_0_f16_head": ("qwen2", 256, 2, 4, 2, 512, 1000, 2, 1, 1e4, 8, 4),
+    "q5_0_q6k_head": ("llama", 512, 2, 8, 4, 1024, 1500, 6, 14, 5e5, 8, 4),
+}
 WIDE = {
     "q8_c4_layer": ("qwen2", 2048, 2, 32, 4, 5632, 3000, 8, 1e4, 8, 4),
     "q4k_c5_layer": ("llama", 4096, 1, 32, 8, 14336, 2000, 12, 5e5, 16, 8),
@@ -95,11 +102,46 @@ def _random_packed(rng, dt, rows, cols):
 
 
 def test_qmatvec_rejects_unsupported(jd, gpu_ctx):
-    """Packed dtypes without a kernel are reported, never read as f32 (janusdoe.c:2739)."""
-    W = np.zeros((4, 18 * 8), np.uint8)
+    """Packed dtypes without a kernel (here Q5_K, type 13) are reported, never read as f32
+    (janusdoe.c:2739)."""
+    W = np.zeros((4, 176), np.uint8)
     with pytest.raises(jd.JdError) as ei:
-        jd.qmatvec(gpu_ctx, W, jd.JD_Q4_0, np.zeros(256, np.float32), 4, 256)
+        jd.qmatvec(gpu_ctx, W, 13, np.zeros(256, np.float32), 4, 256)
     assert ei.value.code == jd.JD_EUNSUPPORTED
+
+
+@pytest.mark.parametrize("dt,rows,cols", [(14, 300, 2048), (14, 70, 4096), (2, 200, 1024), (6, 130, 2048),
+                                          (1, 90, 512)])
+@pytest.mark.parametrize("B", [1, 3])
+def test_qmatvec_more_types(jd, orc, gpu_ctx, dt, rows, cols, B):
+    """Q6_K (native 6-bit kernels), Q4_0 / Q5_0 (int8 codes in the Q8_0 layout) and F16 (as
+    f32) against jd_qmatvec's restatement, on rows written by the library's quantiser."""
+    rng = np.random.default_rng(rows + dt)
+    x = rng.standard_normal((B, cols)).astype(np.float32)
+    Wb = _typed_rows(jd, dt, rows, cols, rows + cols)
+    got = jd.qmatvec(gpu_ctx, Wb, dt, x, rows, cols)
+    for b in range(B):
+        ref = orc.qmatvec(Wb, dt, x[b], rows, cols)
+        err = np.max(np.abs(got[b] - ref)) / max(1e-30, np.max(np.abs(ref)))
+        assert err <= 1e-5, (b, err)
+
+
+def _typed_rows(jd, dt, rows, cols, seed):
+    """rows x cols weights of type dt: the output head of a synthetic GGUF in that type."""
+    import tempfile
+    from oracle.oracle import Oracle
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "t.gguf")
+        jd.write_synthetic_gguf(path, "llama", 1, cols, 256, cols // 64, cols // 64, rows, 1e4, 1e-5, 8, seed, 0.02,
+                                out_dtype=dt)
+        hm = jd.HostModel(path, lora_rank=8)
+        try:
+            assert hm.h.output_dt == dt
+            import ctypes as C
+            rb = {1: cols * 2, 2: cols // 32 * 18, 6: cols // 32 * 22, 14: cols // 256 * 210}[dt]
+            return np.frombuffer(C.string_at(hm.h.output, rows * rb), np.uint8).reshape(rows, rb).copy()
+        finally:
+            hm.close()
 
 
 def _oracle_stream(om, prompt, n_gen):
@@ -208,3 +250,36 @@ def test_host_lora_sidecar_roundtrip(jd, orc, gpu_ctx, tmp_path):
         om.close()
         hm.close()
         hm2.close()
+
+
+@pytest.mark.parametrize("name", sorted(MIXED))
+def test_host_mixed_types_parity(jd, orc, gpu_ctx, tmp_path, name, b1_path):
+    """Host models whose layers are Q4_K / Q4_0 / Q5_0 with a Q6_K or F16 output head, kept
+    packed: teacher-forced logits and elections at batch 1 and at 3 sequences."""
+    arch, D, L, H, KV, FF, V, dt, odt, theta, R, na = MIXED[name]
+    path = str(tmp_path / ("%s.gguf" % name))
+    jd.write_synthetic_gguf(path, arch, L, D, FF, H, KV, V, theta, 1e-5, dt, 31, 0.02, out_dtype=odt)
+    hm = jd.HostModel(path, lora_rank=R)
+    assert hm.h.output_dt == odt and hm.h.layers[0].wq_dt == dt
+    hm.lora_seed(23, na, 0.01, 1.0 / D ** 0.5)
+    om = OHost(orc, path, R, -1, 64)
+    om.lora_seed(23, na, 0.01, 1.0 / D ** 0.5)
+    try:
+        for B in (1, 3):
+            P, G = 4, 4
+            prompts = np.random.default_rng(B).integers(0, V, (B, P)).astype(np.int32)
+            ref = [_oracle_stream(om, prompts[b], G) for b in range(B)]
+            eng = jd.Engine.host(gpu_ctx, hm, B, 64)
+            try:
+                eng.reset()
+                for pos in range(P + G - 1):
+                    tok = np.array([ref[b][0][pos] for b in range(B)], np.int32)
+                    nxt, _, lg, tr = eng.step(tok, np.full(B, pos, np.int32), logits=True, trace=True)
+                    for b in range(B):
+                        assert logit_err(lg[b], ref[b][1][pos]) <= LOGIT_TOL, (B, b, pos)
+                        assert not compare_trace(tr, ref[b][2][pos], L, b=b), (B, b, pos)
+            finally:
+                eng.close()
+    finally:
+        om.close()
+        hm.close()

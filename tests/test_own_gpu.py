@@ -217,3 +217,44 @@ def test_sampling_matches_oracle(jd, orc, gpu_ctx):
     finally:
         eng.close()
         om.close()
+
+
+@pytest.mark.parametrize("P", [2, 37, 200])
+def test_batched_prefill_matches_token_by_token(jd, orc, gpu_ctx, P):
+    """Batched prompt prefill (all prompt tokens as one batch per layer, EMA as an ordered
+    scan) on the depth-12 variable-topology model: every prompt token's k, elected experts,
+    weights and EMA per layer equal the oracle's token-by-token decode, and the greedy stream
+    that follows (the KV cache the prefill wrote) equals the oracle's."""
+    om, pm = _pair(jd, orc, 12, 3, True, n_kv_heads=4, vocab_size=8256, seq_len=1024)
+    prompt, _ = orc.prompt(3 * 1000 + 7, 8256, P)
+    G = 24
+    om.reset()
+    traces, lg = [], None
+    for pos, t in enumerate(prompt):
+        lg, tr = om.forward(int(t), pos, trace=True)
+        traces.append(tr)
+    exp = []
+    pos = P
+    for _ in range(G):
+        nxt = int(np.argmax(lg))
+        exp.append(nxt)
+        lg = om.forward(nxt, pos)
+        pos += 1
+    eng = jd.Engine.own(gpu_ctx, pm, 1)
+    try:
+        eng.reset()
+        eng.set_prompt(np.array([prompt]), [P])
+        ms = eng.prefill(1)
+        assert ms > 0
+        tok, p = eng.state(1)
+        assert int(p[0]) == P - 1 and int(tok[0]) == int(prompt[-1])
+        tr = eng.prefill_trace(P - 1)
+        ties = 0
+        for t in range(P - 1):
+            bad = compare_trace(tr, traces[t], 12, b=t)
+            assert not bad, (t, bad[:3])
+        eng.run(1, G)   # the last prompt token, then greedy tokens
+        assert list(eng.history(1, G)[0]) == exp
+    finally:
+        eng.close()
+        om.close()
