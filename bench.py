@@ -440,9 +440,10 @@ def run_own(args, name, w, steps, warmup, dist, world, rank, local):
     eng = jd.Engine.own(ctx, model, B)
     eng.set_sampling(w["temp"], w["top_k"])
     prompts, rngs = prompts_for(w, rank)
-    # prefill (sequential, timed separately)
+    # prompt prefill, timed separately: one sequence runs its prompt as one batch of tokens
+    # (jdg_prefill); a batch of sequences runs it position by position as batched steps
     eng.set_prompt(prompts, [P] * B, rngs)
-    prefill_ms = eng.run(B, P - 1)
+    prefill_ms = eng.prefill(B) if B == 1 else eng.run(B, P - 1)
     # warm-up decode steps
     eng.run(B, warmup)
     # timed decode steps

@@ -427,6 +427,10 @@ static __global__ __launch_bounds__(kPThreads, 1) void k_b1_step(B1PArgs a) {
     }
     bool misc_ready = false;
     bool par_ready = false;  // the next layer's parameters were already waited for (in P5)
+    // fine timeline of CTA 0 (debug): slot 300 + 8*layer + i
+    auto mark = [&](int l, int i) {
+        if (a.tl && blockIdx.x == 0 && tid == 0 && l < 26) a.tl[3 * (300 + 8 * l + i)] = p_gtimer();
+    };
 
     for (int l = 0; l < a.L; l++) {
         const int slot = 1 + 5 * l;
@@ -435,6 +439,12 @@ static __global__ __launch_bounds__(kPThreads, 1) void k_b1_step(B1PArgs a) {
         par_ready = false;
         const float *par = s_par[l & 1];
         const B1PLayer &ly = *reinterpret_cast<const B1PLayer *>(par);
+        // the HBM is idle in the latency-bound phases P1-P3: bring this layer's gate/up
+        // matrices of every alive expert (the election is not known yet) into L2 for P4;
+        // in the last layer also the LM head
+        if (l > 0 && tid < kMaxE && ly.gu[tid]) p_prefetch_share(ly.gu[tid], gu_bytes);
+        if (l + 1 == a.L && tid == kMaxE) p_prefetch_share(a.output, (size_t)a.V * D * 4);
+        mark(l, 0);
         const float *attn_norm = par + kPParHdr / 4, *ffn_norm = attn_norm + D, *wvn = ffn_norm + D;
         // ---------------- P1: RMSNorm + q/k/v rows ----------------
         {
@@ -454,6 +464,7 @@ static __global__ __launch_bounds__(kPThreads, 1) void k_b1_step(B1PArgs a) {
             const float inv = 1.0f / sqrtf(ss / (float)D + a.eps);
             for (int i = tid; i < D; i += kPThreads) s_x[i] = __fmul_rn(__fmul_rn(s_x[i], inv), attn_norm[i]);
             __syncthreads();
+            mark(l, 1);
             wait_bar(0);
             for (int rr = warp; rr < nq; rr += kPWarps) {
                 const float *wr = s_wqkv + (size_t)rr * D;
@@ -496,6 +507,7 @@ static __global__ __launch_bounds__(kPThreads, 1) void k_b1_step(B1PArgs a) {
             if (has_p && tid < kPHD) s_v[(p - it0) * kPKRow + tid] = __ldcg(a.qkv + D + kd + (size_t)ig * kPHD + tid);
             wait_bar(1);
             __syncthreads();
+            mark(l, 2);
             if (has_p && tid < kPHD) {  // append k (roped) and v at p
                 kdst_l[(size_t)p * kd + (size_t)ig * kPHD + tid] = s_k[(p - it0) * kPKRow + tid];
                 vdst_l[(size_t)p * kd + (size_t)ig * kPHD + tid] = s_v[(p - it0) * kPKRow + tid];
@@ -514,6 +526,7 @@ static __global__ __launch_bounds__(kPThreads, 1) void k_b1_step(B1PArgs a) {
                 }
             }
             __syncthreads();
+            mark(l, 3);
             for (int j = warp; j < hg; j += kPWarps) {  // chunk softmax of head j
                 const float s0 = lane < i_nt ? s_p[j * kPChunk + lane] : -INFINITY;
                 const float s1 = lane + 32 < i_nt ? s_p[j * kPChunk + lane + 32] : -INFINITY;
@@ -553,6 +566,7 @@ static __global__ __launch_bounds__(kPThreads, 1) void k_b1_step(B1PArgs a) {
                     a.part[((size_t)(ig * hg + j) * a.nch_max + ich) * (kPHD + 2) + d] = o;
                 }
             }
+            mark(l, 4);
             if (l + 1 < a.L) release_and([&] { stage_kv(l + 1); });
         }
         if (!p_grid_sync(a, gen, &s_flag, slot + 1)) { drain(); return; }
@@ -606,6 +620,7 @@ static __global__ __launch_bounds__(kPThreads, 1) void k_b1_step(B1PArgs a) {
                 }
             }
             __syncthreads();
+            mark(l, 5);
             wait_bar(2);
             for (int rr = warp; rr < nr; rr += kPWarps) {
                 const float *wr = s_wo + (size_t)rr * D;
@@ -658,6 +673,7 @@ static __global__ __launch_bounds__(kPThreads, 1) void k_b1_step(B1PArgs a) {
             __syncthreads();
             if (warp == 0) p_elect_warp0(tot, ly.alive, ema_s[l], ly.temperature, D, a.eps, eo);
             __syncthreads();
+            mark(l, 6);
             const int k = eo.k;
             if (blockIdx.x == 0 && tid < kMaxE) {
                 a.tr_sel[(size_t)l * kMaxE + tid] = eo.sel[tid];
@@ -719,20 +735,9 @@ static __global__ __launch_bounds__(kPThreads, 1) void k_b1_step(B1PArgs a) {
         // ---------------- P5: down rows of the elected experts, combined into x ----------------
         {
             const int k = eo.k;
-            // layer l's gate/up rows are consumed: bring the next layer's alive experts' gate/up
-            // matrices (all of them: the election is not known yet) or the LM head into L2
-            if (l + 1 < a.L) {
-                wait_bar(3 + ((l + 1) & 1));
-                par_ready = true;
-                if (tid < kMaxE) {
-                    const float *g = reinterpret_cast<const B1PLayer *>(s_par[(l + 1) & 1])->gu[tid];
-                    if (g) p_prefetch_share(g, gu_bytes);
-                }
-            } else if (tid == 0) {
-                p_prefetch_share(a.output, (size_t)a.V * D * 4);
-            }
             p_g2s<8>(reinterpret_cast<float4 *>(s_h), reinterpret_cast<const float4 *>(a.hbuf), k * a.hidden / 4);
             __syncthreads();
+            mark(l, 7);
             // pairs (row rr, election slot ki) per warp, two in flight
             const int np = nr * k;
             float4 wa[NH], wb[NH];

@@ -1,0 +1,311 @@
+// jdg_tc32.cuh — f32-accurate GEMM on the tcgen05 tensor cores for the own model's batched
+// step (q/k/v, Wo, the elected experts' gate/up and down, the LM head):
+//
+//     C[t][n] = sum_k X[t][k] * W[n][k]      (t: token rows, n: weight rows)
+//
+// The f32 operands are split into TF32 parts, x = x_hi + x_lo with x_hi the top 10 mantissa
+// bits (exact) and x_lo = x - x_hi (exact in f32, its top 10 bits reach the tensor core), and
+// three kind::tf32 products are accumulated in f32 in tensor memory: W_hi.X_hi + W_hi.X_lo +
+// W_lo.X_hi.  Every product of two TF32 numbers is exact in f32; the dropped W_lo.X_lo and
+// the truncation of the lo parts are below 2^-20 of each term, i.e. f32-level accuracy.
+//
+// Operands live in global memory already in the shared-memory layout the MMA descriptors
+// address (canonical K-major, no swizzle): for a block of 128 rows and a 32-wide K chunk, the
+// core matrix (row group g < 16, K group c < 8) of 8 rows x 4 elements (16 bytes a row) sits
+// at byte (c * 16 + g) * 128 — 16 KB per block and part.  Weights are laid out once at upload
+// ([row tile][K chunk][hi | lo]); activations by a prep kernel before each product
+// ([segment][token tile][K chunk][hi | lo], rows past the segment's count zero).  So a stage
+// is four 1-D bulk copies (cp.async.bulk, no tensor maps), and every byte is read once.
+//
+// CTA (128 threads) = one 128-row x 128-token output tile over a K range (split-K CTAs of a
+// tile add their partials in split order in the last CTA, by ticket): thread 0 streams
+// stages into a 3-deep ring, thread 32 issues the 12 MMAs (M128 N128 K8) of each 32-wide
+// chunk and commits the stage back, then all four warps read their 32 TMEM lanes (rows) and
+// apply the epilogue.  Every wait is bounded by wall time; on a timeout the CTA flags
+// JDG_ERR_TIMEOUT, waits (bounded) for what it issued, frees its tensor memory and returns.
+#pragma once
+#include "jdg_async.cuh"
+#include "jdg_kernels.cuh"
+
+namespace jdg {
+
+constexpr int kTcRows = 128;                   // weight rows per tile (MMA M)
+constexpr int kTcTok = 128;                    // tokens per tile (MMA N)
+constexpr int kTcK = 32;                       // K elements per chunk (one stage)
+constexpr int kTcBlk = kTcRows * kTcK * 4;     // 16 KB: one part of one operand block
+constexpr int kTcStages = 3;
+constexpr int kTcStageBytes = 4 * kTcBlk;      // W hi, W lo, X hi, X lo
+constexpr int kTcSmem = 1024 + kTcStages * kTcStageBytes;
+constexpr int kTcMaxSplit = 8;
+// kind::tf32 instruction descriptor: D f32 (bits 4-5 = 1), A and B TF32 (bits 7-9, 10-12 = 2),
+// both K-major, N = 128 (bits 17-22 = N/8), M = 128 (bits 24-28 = M/16)
+constexpr uint32_t kTcIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(kTcTok >> 3) << 17) |
+                              ((uint32_t)(kTcRows >> 4) << 24);
+
+// byte offset of element (row r, k) inside a 128 x 32 block
+__host__ __device__ __forceinline__ uint32_t tc_off(int r, int k) {
+    return (uint32_t)((((k >> 2) * 16 + (r >> 3)) * 128) + (r & 7) * 16 + (k & 3) * 4);
+}
+__device__ __forceinline__ void tc_split(float x, float &hi, float &lo) {
+    hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+    lo = x - hi;  // exact
+}
+
+// Weight blocks of an N x K f32 matrix (rows past N zero): grid-stride over (row, 4-element group).
+static __global__ void k_tc_wprep(const float *__restrict__ W, int N, int K, uint8_t *__restrict__ out) {
+    const int nkc = K / kTcK, rt_n = (N + kTcRows - 1) / kTcRows;
+    const long total = (long)rt_n * kTcRows * (K / 4);
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const int row = (int)(i / (K / 4)), k4 = (int)(i % (K / 4)) * 4;
+        const int rt = row / kTcRows, r = row % kTcRows, kc = k4 / kTcK, k = k4 % kTcK;
+        float4 v = row < N ? *reinterpret_cast<const float4 *>(W + (size_t)row * K + k4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 h, l;
+        tc_split(v.x, h.x, l.x);
+        tc_split(v.y, h.y, l.y);
+        tc_split(v.z, h.z, l.z);
+        tc_split(v.w, h.w, l.w);
+        uint8_t *blk = out + ((size_t)rt * nkc + kc) * 2 * kTcBlk;
+        *reinterpret_cast<float4 *>(blk + tc_off(r, k)) = h;
+        *reinterpret_cast<float4 *>(blk + kTcBlk + tc_off(r, k)) = l;
+    }
+}
+
+// Activation blocks: segment s, token j of the segment is row idx[s*ldi + j] of X (idx null:
+// row j, segment 0), j < cnt[s] (cnt null: M); tokens past the count are zeros.
+// out: [seg][token tile < ttiles][K chunk][hi | lo][16 KB]
+struct TcPrep {
+    const float *X;
+    int ldx, K;
+    const int *idx;
+    int ldi;
+    const int *cnt;
+    int M, nseg, ttiles;
+    uint8_t *out;
+};
+static __global__ void k_tc_xprep(TcPrep p) {
+    const int nkc = p.K / kTcK;
+    const long per_seg = (long)p.ttiles * kTcTok * (p.K / 4);
+    const long total = per_seg * p.nseg;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const int s = (int)(i / per_seg);
+        const long rem = i % per_seg;
+        const int j = (int)(rem / (p.K / 4)), k4 = (int)(rem % (p.K / 4)) * 4;
+        const int n = p.cnt ? p.cnt[s] : p.M;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < n) {
+            const int row = p.idx ? p.idx[(size_t)s * p.ldi + j] : j;
+            v = *reinterpret_cast<const float4 *>(p.X + (size_t)row * p.ldx + k4);
+        }
+        float4 h, l;
+        tc_split(v.x, h.x, l.x);
+        tc_split(v.y, h.y, l.y);
+        tc_split(v.z, h.z, l.z);
+        tc_split(v.w, h.w, l.w);
+        const int tt = j / kTcTok, t = j % kTcTok, kc = k4 / kTcK, k = k4 % kTcK;
+        uint8_t *blk = p.out + (((size_t)s * p.ttiles + tt) * nkc + kc) * 2 * kTcBlk;
+        *reinterpret_cast<float4 *>(blk + tc_off(t, k)) = h;
+        *reinterpret_cast<float4 *>(blk + kTcBlk + tc_off(t, k)) = l;
+    }
+}
+
+struct TcArgs {
+    const uint8_t *const *wt;  // per segment: weight blocks of W (n_rows x K); null = no work
+    const uint8_t *xt;         // activation blocks [seg][ttiles][nkc][2][16 KB]
+    const int *cnt;            // per segment token counts (null: M, one segment)
+    int M, n_rows, nkc, ttiles;
+    float *C;                  // C[seg * c_seg + t * ldc + col]
+    int ldc;
+    long c_seg;
+    int epi;                   // EPI_STORE, EPI_ADD (C += alpha * Y), EPI_SWIGLU (C[t][n/2] = silu(Y[2i]) * Y[2i+1])
+    float alpha;
+    int ksplit;
+    float *part;               // [tiles][ksplit][128 tokens][128 rows]
+    unsigned *tickets;         // one per tile (returned to zero by the last CTA)
+    int *err;
+};
+
+__device__ __forceinline__ uint64_t tc_desc(uint32_t saddr) {
+    // LBO (K-direction core-matrix stride) = 16 row groups x 128 B, SBO (row-group stride) = 128
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((2048u >> 4) & 0x3FFF) << 16) |
+           ((uint64_t)((128u >> 4) & 0x3FFF) << 32) | (1ull << 46);
+}
+__device__ __forceinline__ void tc_mma(uint32_t dtmem, uint64_t da, uint64_t db, uint32_t acc) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %3, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %4, p; }" ::"r"(dtmem),
+        "l"(da), "l"(db), "r"(acc), "r"(kTcIdesc));
+}
+__device__ __forceinline__ unsigned long long tc_now() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+// mbarrier phase wait bounded by 200 ms of wall time
+__device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity) {
+    const unsigned long long t0 = tc_now();
+    for (int it = 0;; it++) {
+        uint32_t done;
+        asm volatile("{ .reg .pred p; mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                     : "=r"(done)
+                     : "r"(smem_u32(bar)), "r"(parity)
+                     : "memory");
+        if (done) return true;
+        if ((it & 63) == 63 && tc_now() - t0 > 200ull * 1000 * 1000) return false;
+    }
+}
+
+__device__ __forceinline__ void tc_store(const TcArgs &a, int seg, int t, int n, float v, int lane) {
+    float *c = a.C + (size_t)seg * a.c_seg + (size_t)t * a.ldc;
+    if (a.epi == EPI_SWIGLU) {
+        const float other = __shfl_xor_sync(JDG_FULL, v, 1);  // every lane takes part
+        if ((lane & 1) == 0 && n + 1 < a.n_rows) c[n >> 1] = __fmul_rn(silu_ref(v), other);
+    } else if (n < a.n_rows) {
+        if (a.epi == EPI_ADD) c[n] = __fadd_rn(c[n], __fmul_rn(v, a.alpha));
+        else c[n] = v;
+    }
+}
+
+static __global__ __launch_bounds__(128) void k_tc32_gemm(TcArgs a) {
+    extern __shared__ __align__(1024) uint8_t tc_sm[];
+    uint8_t *stages = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tc_sm) + 1023) & ~(uintptr_t)1023);
+    __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], done;
+    __shared__ uint32_t tmem_slot;
+    __shared__ int abort_flag, s_last;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rt = blockIdx.x, tt = blockIdx.y, seg = blockIdx.z / a.ksplit, ks = blockIdx.z % a.ksplit;
+    const int n_tok_seg = a.cnt ? a.cnt[seg] : a.M;
+    const int ntok = min(kTcTok, n_tok_seg - tt * kTcTok);
+    const uint8_t *wt = a.wt[seg];
+    if (ntok <= 0 || !wt) return;  // whole CTA, before any barrier or allocation
+    const int per = (a.nkc + a.ksplit - 1) / a.ksplit, kc0 = ks * per, kc1 = min(a.nkc, kc0 + per);
+    const int nloc = max(0, kc1 - kc0);
+    if (tid == 0) {
+        for (int s = 0; s < kTcStages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&done, 1);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                     "r"(kTcTok));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_slot;
+    const uint8_t *wbase = wt + ((size_t)rt * a.nkc) * 2 * kTcBlk;
+    const uint8_t *xbase = a.xt + (((size_t)seg * a.ttiles + tt) * a.nkc) * 2 * kTcBlk;
+    int issued_ld = 0, issued_mma = 0;
+    if (tid == 0) {
+        // ---------------- producer: four 16 KB bulk copies per chunk ----------------
+        for (int i = 0; i < nloc; i++) {
+            const int s = i % kTcStages;
+            if (i >= kTcStages && !tc_wait(&empty[s], (uint32_t)((i / kTcStages) - 1) & 1u)) {
+                abort_flag = 1;
+                break;
+            }
+            if (*(volatile int *)&abort_flag) break;
+            uint8_t *st = stages + (size_t)s * kTcStageBytes;
+            const int kc = kc0 + i;
+            mbar_expect_tx(&full[s], kTcStageBytes);
+            bulk_g2s(st, wbase + (size_t)kc * 2 * kTcBlk, 2 * kTcBlk, &full[s]);
+            bulk_g2s(st + 2 * kTcBlk, xbase + (size_t)kc * 2 * kTcBlk, 2 * kTcBlk, &full[s]);
+            issued_ld = i + 1;
+        }
+    } else if (tid == 32) {
+        // ---------------- MMA issuer ----------------
+        for (int i = 0; i < nloc; i++) {
+            const int s = i % kTcStages;
+            if (!tc_wait(&full[s], (uint32_t)(i / kTcStages) & 1u) || *(volatile int *)&abort_flag) {
+                abort_flag = 1;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t st = smem_u32(stages + (size_t)s * kTcStageBytes);
+            const uint32_t wh = st, wl = st + kTcBlk, xh = st + 2 * kTcBlk, xl = st + 3 * kTcBlk;
+#pragma unroll
+            for (int q = 0; q < kTcK / 8; q++) {  // K slices of 8: two K groups of the block
+                const uint32_t o = (uint32_t)q * 2 * 2048;
+                tc_mma(tmem, tc_desc(wh + o), tc_desc(xh + o), (i > 0 || q > 0) ? 1u : 0u);
+                tc_mma(tmem, tc_desc(wh + o), tc_desc(xl + o), 1u);
+                tc_mma(tmem, tc_desc(wl + o), tc_desc(xh + o), 1u);
+            }
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                             smem_u32(&empty[s]))
+                         : "memory");
+            issued_mma = i + 1;
+        }
+        // the accumulator is complete when everything issued so far has finished
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(&done))
+                     : "memory");
+    }
+    __syncwarp();
+    // ---------------- epilogue: warp w holds rows 32w..32w+31 (TMEM lanes) ----------------
+    const bool got = tc_wait(&done, 0);
+    if (!got) abort_flag = 1;
+    __syncthreads();
+    const bool ok = !abort_flag && nloc > 0;
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const int row = warp * 32 + lane, n = rt * kTcRows + row;
+    const uint32_t tbase = tmem + ((uint32_t)(warp * 32) << 16);
+    if (ok && a.ksplit == 1) {
+        for (int c0 = 0; c0 < kTcTok; c0 += 8) {
+            if (c0 >= ntok) break;  // uniform over the warp
+            float v[8];
+            qm_ld8_tc(tbase + (uint32_t)c0, v);
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+                if (c0 + j < ntok) tc_store(a, seg, tt * kTcTok + c0 + j, n, v[j], lane);
+        }
+    } else if (ok) {
+        const size_t tile = ((size_t)seg * gridDim.y + tt) * gridDim.x + rt;
+        float *pp = a.part + (tile * a.ksplit + ks) * (size_t)kTcTok * kTcRows;
+        for (int c0 = 0; c0 < kTcTok; c0 += 8) {
+            if (c0 >= ntok) break;
+            float v[8];
+            qm_ld8_tc(tbase + (uint32_t)c0, v);
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+                if (c0 + j < ntok) pp[(size_t)(c0 + j) * kTcRows + row] = v[j];
+        }
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+            const unsigned tk = atomicAdd(a.tickets + tile, 1u);
+            s_last = tk == (unsigned)a.ksplit - 1;
+            if (s_last) {
+                __threadfence();
+                a.tickets[tile] = 0;
+            }
+        }
+        __syncthreads();
+        if (s_last) {
+            const float *p0 = a.part + tile * a.ksplit * (size_t)kTcTok * kTcRows;
+            for (int t = 0; t < ntok; t++) {
+                float acc = 0.f;
+                for (int z = 0; z < a.ksplit; z++) acc += __ldcg(p0 + ((size_t)z * kTcTok + t) * kTcRows + row);
+                tc_store(a, seg, tt * kTcTok + t, n, acc, lane);
+            }
+        }
+    }
+    if (abort_flag) {
+        if (tid == 0) atomicOr(a.err, JDG_ERR_TIMEOUT);
+        // let the issued copies and MMAs land before the memory goes away
+        if (tid == 0)
+            for (int i = max(0, issued_ld - kTcStages); i < issued_ld; i++)
+                tc_wait(&full[i % kTcStages], (uint32_t)(i / kTcStages) & 1u);
+        if (tid == 32 && issued_mma > 0) tc_wait(&empty[(issued_mma - 1) % kTcStages], (uint32_t)((issued_mma - 1) / kTcStages) & 1u);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTok));
+    }
+}
+
+}  // namespace jdg
