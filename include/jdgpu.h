@@ -222,6 +222,18 @@ int jdg_set_prompt(jdg_engine *e, int B, const int *tokens, int P, const int *le
  * current token at the current position, then picks the next one (the prompt's while
  * it lasts, else sampled/greedy).  Generated tokens land in the history buffer. */
 int jdg_run(jdg_engine *e, int B, int n_steps);
+/* Hebbian --learn pass (host_learn_run, janusdoe.c:3416-3447) over the token stream toks on
+ * the engine's LoRA parliament (one GPU): for t < nt-1 a forward of toks[t] at position t on
+ * fresh caches of slot 0 (the EMA carries on), the prophecy-debt signal of toks[t+1], and a
+ * notorch step (janusdoe.c:3102-3132) on every expert elected in that token, in layer and slot
+ * order, then quarantine (janusdoe.c:3136-3144).  The reference's global RNG state and
+ * notorch offset are explicit (in/out); *deaths receives the experts quarantined.  lr is the
+ * reference's learning rate argument. */
+int jdg_host_learn(jdg_engine *e, const int *toks, int nt, float lr, uint64_t *rng_state, int *notorch_offset,
+                   int *deaths);
+/* LoRA factors A [dim][rank], B [rank][dim] and alive flag of expert slot x of layer l as the
+ * engine holds them (any pointer may be NULL). */
+int jdg_host_get_expert(jdg_engine *e, int l, int x, float *A, float *B, int *alive);
 /* Prompt prefill (own model; replaces the token-by-token prefill of chat(), janusdoe.c:3660):
  * right after jdg_set_prompt, runs every prompt token of slots 0..B-1 but the last through
  * the model as one batch per sequence and leaves each slot where len-1 jdg_run steps would:

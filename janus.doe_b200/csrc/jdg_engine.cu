@@ -18,6 +18,7 @@
 #include "jdg_kernels.cuh"
 #include "jdg_b1.cuh"
 #include "jdg_b1p.cuh"
+#include "jdg_tc32.cuh"
 
 using namespace jdg;
 
@@ -219,6 +220,7 @@ extern "C" int jdg_own_upload(jdg_ctx *ctx, const jd_model *m, int max_batch, jd
 }
 
 static bool b1p_usable(jdg_engine *e);
+static int tc_build(jdg_engine *e, const jd_model *m);
 
 int jdg_own_upload_impl(jdg_engine *e, const jd_model *m, int max_batch) {
     const jd_config &c = m->c;
@@ -401,10 +403,102 @@ int jdg_own_upload_impl(jdg_engine *e, const jd_model *m, int max_batch) {
     if (rc != JD_OK) return rc;
     CK(cudaStreamSynchronize(e->st));
     b1p_usable(e);  // decided here, outside any stream capture
+    rc = tc_build(e, m);
+    if (rc != JD_OK) return rc;
     return JD_OK;
 }
 
 // ------------------------------------------------------------------------------------
+// Tensor-core blocks of every own-model matrix the batched step multiplies (TF32 hi/lo in the
+// MMA layout, jdg_tc32.cuh), built on the device from the uploaded f32 weights.
+static size_t tc_blocks_bytes(int N, int K) { return (size_t)((N + kTcRows - 1) / kTcRows) * (K / kTcK) * 2 * kTcBlk; }
+
+static int tc_blocks(jdg_engine *e, const float *W, int N, int K, uint8_t **out) {
+    DALLOC(*out, tc_blocks_bytes(N, K));
+    k_tc_wprep<<<1184, 256, 0, e->st>>>(W, N, K, *out);
+    return JD_OK;
+}
+
+static int tc_table(jdg_engine *e, const uint8_t *const *ptrs, int n, const uint8_t ***out) {
+    DALLOC(*out, (size_t)n * sizeof(void *));
+    CK(cudaMemcpy((void *)*out, ptrs, (size_t)n * sizeof(void *), cudaMemcpyHostToDevice));
+    return JD_OK;
+}
+
+static int tc_build(jdg_engine *e, const jd_model *m) {
+    const char *g = getenv("JDG_SIMT_GEMM");
+    if ((g && g[0] == '1') || e->D % kTcK || e->hidden % kTcK || e->qd % kTcK) return JD_OK;
+    const int D = e->D, H = e->hidden, L = e->L;
+    std::vector<const float *> gu_h((size_t)L * kMaxE), dn_h((size_t)L * kMaxE);
+    CK(cudaMemcpy(gu_h.data(), e->gu_tab, gu_h.size() * sizeof(void *), cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(dn_h.data(), e->dn_tab, dn_h.size() * sizeof(void *), cudaMemcpyDeviceToHost));
+    for (int l = 0; l < L; l++) {
+        LayerDev &ly = e->layers[l];
+        int rc = tc_blocks(e, ly.wqkv, e->qkvd, D, &ly.tc_wqkv);
+        if (rc == JD_OK) rc = tc_blocks(e, ly.wo, D, e->qd, &ly.tc_wo);
+        if (rc != JD_OK) return rc;
+        const uint8_t *gt[kMaxE] = {nullptr}, *dt[kMaxE] = {nullptr};
+        for (int x = 0; x < kMaxE; x++) {
+            if (!gu_h[(size_t)l * kMaxE + x]) continue;
+            uint8_t *b1 = nullptr, *b2 = nullptr;
+            rc = tc_blocks(e, gu_h[(size_t)l * kMaxE + x], 2 * H, D, &b1);
+            if (rc == JD_OK) rc = tc_blocks(e, dn_h[(size_t)l * kMaxE + x], D, H, &b2);
+            if (rc != JD_OK) return rc;
+            gt[x] = b1;
+            dt[x] = b2;
+        }
+        const uint8_t *one[1] = {ly.tc_wqkv}, *two[1] = {ly.tc_wo};
+        int rc2 = tc_table(e, gt, kMaxE, &ly.tc_gu);
+        if (rc2 == JD_OK) rc2 = tc_table(e, dt, kMaxE, &ly.tc_dn);
+        if (rc2 == JD_OK) rc2 = tc_table(e, one, 1, &ly.tc_wqkv_tab);
+        if (rc2 == JD_OK) rc2 = tc_table(e, two, 1, &ly.tc_wo_tab);
+        if (rc2 != JD_OK) return rc2;
+    }
+    int rc = tc_blocks(e, e->output, e->V, D, &e->tc_out);
+    if (rc != JD_OK) return rc;
+    const uint8_t *ot[1] = {e->tc_out};
+    rc = tc_table(e, ot, 1, &e->tc_out_tab);
+    if (rc != JD_OK) return rc;
+    // activation blocks for up to max(batch, context) rows in 16 segments, the widest K
+    const int rows = std::max(e->B_max, e->max_seq), kmax = std::max(D, H);
+    const int tt = (rows + kTcTok - 1) / kTcTok;
+    e->tc_xt_bytes = (size_t)kMaxE * tt * (kmax / kTcK) * 2 * kTcBlk;
+    DALLOC(e->tc_xt, e->tc_xt_bytes);
+    DALLOC(e->tc_part, (size_t)64 << 20);
+    DALLOC(e->tc_tickets, 16384 * 4);
+    CK(cudaMemsetAsync(e->tc_tickets, 0, 16384 * 4, e->st));
+    CK(cudaFuncSetAttribute(k_tc32_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));
+    CK(cudaStreamSynchronize(e->st));
+    e->tc_ok = 1;
+    return JD_OK;
+}
+
+// C = X.W^T on the tensor cores: X rows from `X` (segment s at X + s*x_seg, rows idx[s*ldi+j]
+// when idx is given, counts cnt[s] or M), W as per-segment block tables `wt` (n_rows x K).
+static void launch_tc(jdg_engine *e, const uint8_t *const *wt, int nseg, const float *X, long x_seg, int ldx,
+                      const int *idx, int ldi, const int *cnt, int M, int max_rows, int n_rows, int K, float *C,
+                      int ldc, long c_seg, int epi, float alpha) {
+    const int ttiles = (max_rows + kTcTok - 1) / kTcTok, nkc = K / kTcK;
+    TcPrep p = {};
+    p.X = X; p.x_seg = x_seg; p.ldx = ldx; p.K = K; p.idx = idx; p.ldi = ldi; p.cnt = cnt; p.M = M;
+    p.nseg = nseg; p.ttiles = ttiles; p.out = e->tc_xt;
+    k_tc_xprep<<<1184, 256, 0, e->st>>>(p);
+    const int rtiles = (n_rows + kTcRows - 1) / kTcRows;
+    // split K until about one CTA per SM (every split keeps at least one chunk)
+    int ks = 1;
+    const int tiles = rtiles * ttiles * nseg;
+    if (nseg == 1)
+        while (ks < kTcMaxSplit && tiles * (ks + 1) <= 160 && nkc / (ks + 1) >= 2) ks++;
+    const int per = (nkc + ks - 1) / ks;
+    ks = (nkc + per - 1) / per;
+    TcArgs a = {};
+    a.wt = wt; a.xt = e->tc_xt; a.cnt = cnt; a.M = M; a.n_rows = n_rows; a.nkc = nkc; a.ttiles = ttiles;
+    a.C = C; a.ldc = ldc; a.c_seg = c_seg; a.epi = epi; a.alpha = alpha; a.ksplit = ks; a.part = e->tc_part;
+    a.tickets = e->tc_tickets; a.err = e->err;
+    k_tc32_gemm<<<dim3(rtiles, ttiles, nseg * ks), kTcThreads, kTcSmem, e->st>>>(a);
+    e->launches += 2;
+}
+
 static int pick_bm(int B) { return B <= 16 ? 16 : B <= 32 ? 32 : 64; }
 
 template <int EPI>
@@ -420,7 +514,7 @@ static void launch_sgemm(jdg_engine *e, const SgemmArgs &a, int B, int nseg) {
 
 static void launch_gemv1(jdg_engine *e, int epi, const float *W, int N, int K, const float *X, const float *norm_w,
                          int prenorm, float *Y) {
-    GemvArgs a;
+    GemvArgs a = {};
     a.W = W;
     a.N = N;
     a.K = K;
@@ -439,7 +533,7 @@ static void launch_gemv1(jdg_engine *e, int epi, const float *W, int N, int K, c
 }
 
 static void launch_attention(jdg_engine *e, int l, int B, float scale, float bias) {
-    AttnArgs a;
+    AttnArgs a = {};
     a.qkv = e->qkv;
     a.ld = e->qkvd;
     a.kc = e->kc + (size_t)l * e->max_seq * e->kd;
@@ -464,7 +558,7 @@ static void launch_attention(jdg_engine *e, int l, int B, float scale, float bia
 }
 
 void jdg_launch_rope(jdg_engine *e, int l, int B) {
-    RopeArgs r;
+    RopeArgs r = {};
     r.qkv = e->qkv;
     r.ld = e->qkvd;
     r.H = e->Hh;
@@ -486,7 +580,7 @@ void jdg_launch_rope(jdg_engine *e, int l, int B) {
 void jdg_launch_attention(jdg_engine *e, int l, int B, float scale, float bias) { launch_attention(e, l, B, scale, bias); }
 
 void jdg_launch_pick(jdg_engine *e, int B) {
-    PickArgs pa;
+    PickArgs pa = {};
     pa.logits = e->logits;
     pa.V = e->ldl;
     pa.ldl = e->ldl;
@@ -514,7 +608,7 @@ void jdg_launch_pick_tp(jdg_engine *e, int B, const float *v, const int *ix, int
 
 void jdg_launch_elect(jdg_engine *e, int l, int B, const float *xin, const float *norm_w, const float *w_vote,
                       const int *alive, float temperature, int host) {
-    ElectArgs a;
+    ElectArgs a = {};
     a.x = xin;
     a.norm_w = norm_w;
     a.eps = e->eps;
@@ -768,9 +862,13 @@ static void enqueue_own_step(jdg_engine *e, int B) {
     } else {
         k_rmsnorm<<<B, 256, 0, e->st>>>(e->x, e->output_norm, e->xb, D, e->eps);
         e->launches++;
-        SgemmArgs a = {};
-        a.A = e->xb; a.lda = D; a.M = B; a.W = e->output; a.N = V; a.K = D; a.C = e->logits; a.ldc = V;
-        launch_sgemm<EPI_STORE>(e, a, B, 1);
+        if (e->tc_ok) {
+            launch_tc(e, e->tc_out_tab, 1, e->xb, 0, D, nullptr, 0, nullptr, B, B, V, D, e->logits, V, 0, EPI_STORE, 1.f);
+        } else {
+            SgemmArgs a = {};
+            a.A = e->xb; a.lda = D; a.M = B; a.W = e->output; a.N = V; a.K = D; a.C = e->logits; a.ldc = V;
+            launch_sgemm<EPI_STORE>(e, a, B, 1);
+        }
     }
     jdg_launch_pick(e, B);
 }
@@ -790,14 +888,21 @@ static void own_batch_layers(jdg_engine *e, int B, int prefill_slot) {
         } else {
             k_rmsnorm<<<B, 256, 0, e->st>>>(e->x, ly.attn_norm, e->xb, D, e->eps);
             e->launches++;
-            SgemmArgs a = {};
-            a.A = e->xb; a.lda = D; a.M = B; a.W = ly.wqkv; a.N = e->qkvd; a.K = D; a.C = e->qkv; a.ldc = e->qkvd;
-            launch_sgemm<EPI_STORE>(e, a, B, 1);
+            if (e->tc_ok) {
+                launch_tc(e, ly.tc_wqkv_tab, 1, e->xb, 0, D, nullptr, 0, nullptr, B, B, e->qkvd, D, e->qkv, e->qkvd, 0,
+                          EPI_STORE, 1.f);
+            } else {
+                SgemmArgs a = {};
+                a.A = e->xb; a.lda = D; a.M = B; a.W = ly.wqkv; a.N = e->qkvd; a.K = D; a.C = e->qkv; a.ldc = e->qkvd;
+                launch_sgemm<EPI_STORE>(e, a, B, 1);
+            }
         }
         jdg_launch_rope(e, l, B);
         launch_attention(e, l, B, scale, 1.0f);
         if (B == 1) {
             launch_gemv1(e, EPI_ADD, ly.wo, D, qd, e->att, nullptr, 0, e->x);
+        } else if (e->tc_ok) {
+            launch_tc(e, ly.tc_wo_tab, 1, e->att, 0, qd, nullptr, 0, nullptr, B, B, D, qd, e->x, D, 0, EPI_ADD, 1.f);
         } else {
             SgemmArgs a = {};
             a.A = e->att; a.lda = qd; a.M = B; a.W = ly.wo; a.N = D; a.K = qd; a.C = e->x; a.ldc = D;
@@ -830,14 +935,22 @@ static void own_batch_layers(jdg_engine *e, int B, int prefill_slot) {
             e->launches += 2;
         } else {
             k_route<<<1, 512, 0, e->st>>>(e->kcnt, e->sel, B, e->rcnt, e->ridx, e->pairrow, e->stats);
-            SgemmArgs a = {};
-            a.A = e->xb; a.lda = D; a.idx = e->ridx; a.ldi = B; a.cnt = e->rcnt; a.Wtab = gu; a.N = 2 * H; a.K = D;
-            a.C = e->hbuf; a.ldc = H; a.c_seg_rows = B;
-            launch_sgemm<EPI_SWIGLU>(e, a, B, kMaxE);
-            SgemmArgs d = {};
-            d.A = e->hbuf; d.lda = H; d.a_seg_rows = B; d.cnt = e->rcnt; d.Wtab = dn; d.N = D; d.K = H;
-            d.C = e->ybuf; d.ldc = D; d.c_seg_rows = B;
-            launch_sgemm<EPI_STORE>(e, d, B, kMaxE);
+            if (e->tc_ok) {
+                // segments = expert slots: gate/up of the routed rows of xb (gathered), then down
+                launch_tc(e, ly.tc_gu, kMaxE, e->xb, 0, D, e->ridx, B, e->rcnt, 0, B, 2 * H, D, e->hbuf, H,
+                          (long)B * H, EPI_SWIGLU, 1.f);
+                launch_tc(e, ly.tc_dn, kMaxE, e->hbuf, (long)B * H, H, nullptr, 0, e->rcnt, 0, B, D, H, e->ybuf, D,
+                          (long)B * D, EPI_STORE, 1.f);
+            } else {
+                SgemmArgs a = {};
+                a.A = e->xb; a.lda = D; a.idx = e->ridx; a.ldi = B; a.cnt = e->rcnt; a.Wtab = gu; a.N = 2 * H; a.K = D;
+                a.C = e->hbuf; a.ldc = H; a.c_seg_rows = B;
+                launch_sgemm<EPI_SWIGLU>(e, a, B, kMaxE);
+                SgemmArgs d = {};
+                d.A = e->hbuf; d.lda = H; d.a_seg_rows = B; d.cnt = e->rcnt; d.Wtab = dn; d.N = D; d.K = H;
+                d.C = e->ybuf; d.ldc = D; d.c_seg_rows = B;
+                launch_sgemm<EPI_STORE>(e, d, B, kMaxE);
+            }
             k_combine<<<B, 256, 0, e->st>>>(e->kcnt, e->selw, e->pairrow, e->ybuf, D, e->x);
             e->launches += 2;
         }
@@ -897,6 +1010,10 @@ static int get_graph(jdg_engine *e, int B, cudaGraphExec_t *out) {
 static void drop_graphs(jdg_engine *e) {
     for (auto &kv : e->graphs) cudaGraphExecDestroy(kv.second);
     e->graphs.clear();
+}
+int jdg_host_drop_graphs(jdg_engine *e) {
+    drop_graphs(e);
+    return JD_OK;
 }
 
 static int check_err(jdg_engine *e) {

@@ -10,6 +10,11 @@
 struct LayerDev {
     float *attn_norm = nullptr, *ffn_norm = nullptr, *wqkv = nullptr, *wo = nullptr, *w_vote = nullptr;
     float temperature = 0.f;
+    // tensor-core blocks (TF32 hi/lo, jdg_tc32.cuh) of q/k/v and Wo; per expert slot the
+    // gate/up and down blocks, as device tables of 16 pointers (null for dead slots)
+    uint8_t *tc_wqkv = nullptr, *tc_wo = nullptr;
+    const uint8_t **tc_gu = nullptr, **tc_dn = nullptr;
+    const uint8_t **tc_wqkv_tab = nullptr, **tc_wo_tab = nullptr;  // one-entry tables
 };
 
 // packed host-model weight on the device (layout chosen by jdg_host.cu at upload)
@@ -86,6 +91,14 @@ struct jdg_engine {
     int b1p_grid = 0;             // CTAs of the persistent step (0: not usable)
     int *tr_k = nullptr, *tr_sel = nullptr;
     float *tr_w = nullptr, *tr_ema = nullptr;
+    // tensor-core GEMMs of the batched own-model step (jdg_tc32.cuh)
+    int tc_ok = 0;                       // blocks built; JDG_SIMT_GEMM=1 keeps the SIMT kernels
+    uint8_t *tc_out = nullptr;           // LM head blocks
+    const uint8_t **tc_out_tab = nullptr;
+    uint8_t *tc_xt = nullptr;            // activation blocks, sized for 16 segments
+    size_t tc_xt_bytes = 0;
+    float *tc_part = nullptr;            // split-K partials
+    unsigned *tc_tickets = nullptr;
     // prompt prefill buffers (own model, allocated at the first jdg_prefill; rows = tokens)
     float *pf_x = nullptr, *pf_xb = nullptr, *pf_qkv = nullptr, *pf_att = nullptr, *pf_part = nullptr;
     float *pf_hbuf = nullptr, *pf_ybuf = nullptr, *pf_selw = nullptr, *pf_votes = nullptr, *pf_cs = nullptr;

@@ -14,6 +14,7 @@
 #include "jdg_engine.h"
 #include "jdg_hb1.cuh"
 #include "jdg_hpar.cuh"
+#include "jdg_learn.cuh"
 #include "jdg_qmma.cuh"
 
 using namespace jdg;
@@ -70,6 +71,13 @@ struct HostPriv {
     // q/k/v GEMM (they read only the normed layer input) and joined before the LoRA apply
     cudaStream_t st2 = nullptr;
     std::vector<cudaEvent_t> ev_fork, ev_join;  // one pair per layer
+    // Hebbian --learn (jdg_learn.cuh): captures of the forward, signal, update list
+    bool learn_on = false;                  // the generic step captures dy and x
+    float *learn_dyraw = nullptr, *learn_x = nullptr, *learn_dy = nullptr, *learn_sig = nullptr;
+    int *learn_next = nullptr, *learn_dead = nullptr;
+    LearnUpd *learn_upd = nullptr;
+    float **learn_A = nullptr, **learn_B = nullptr;
+    int **learn_alive = nullptr;
 };
 
 HostPriv *priv(jdg_engine *e) { return (HostPriv *)e->host_priv; }
@@ -886,7 +894,13 @@ int jdg_enqueue_host_step(jdg_engine *e, int B) {
             e->launches++;
         }
         launch_q<EPI_SWIGLU>(e, hp->gu[l], e->x, D, B, e->hbuf, e->hidden, 1.f, 1, hl.ffn_norm);
-        if (!tp) {
+        if (!tp && hp->learn_on && l == L - 1) {
+            // the learning target dy is the last layer's FFN output (janusdoe.c:3274): kept,
+            // then added to the residual exactly as the fused epilogue would
+            launch_q<EPI_STORE>(e, hp->dn[l], e->hbuf, e->hidden, B, hp->learn_dyraw, D, 1.f);
+            k_add_scaled<<<(D + 255) / 256, 256, 0, e->st>>>(e->x, hp->learn_dyraw, hl.focus, D);
+            e->launches++;
+        } else if (!tp) {
             launch_q<EPI_ADD>(e, hp->dn[l], e->hbuf, e->hidden, B, e->x, D, hl.focus);
         } else {
             launch_q<EPI_STORE>(e, hp->dn[l], e->hbuf, e->hidden, B, hp->partial, D, 1.f);
@@ -912,6 +926,13 @@ int jdg_enqueue_host_step(jdg_engine *e, int B) {
     }
     if (!tp) {
         launch_q<EPI_STORE>(e, hp->out, e->x, D, B, e->logits, hp->V_loc, 1.f, 1, e->output_norm);
+        if (hp->learn_on) {
+            // the normed final hidden is in xb (janusdoe.c:3311): both targets RMS-normalised,
+            // then the signal of the next token from the logits
+            k_learn_capture<<<1, 1024, 0, e->st>>>(e->xb, hp->learn_dyraw, D, hp->learn_x, hp->learn_dy);
+            k_learn_signal<<<1, 1024, 0, e->st>>>(e->logits, hp->V_loc, hp->learn_next, hp->learn_sig);
+            e->launches += 2;
+        }
         jdg_launch_pick(e, B);
     } else {
         launch_q<EPI_STORE>(e, hp->out, e->x, D, B, e->logits, hp->V_loc, 1.f, 1, e->output_norm);
@@ -989,6 +1010,159 @@ extern "C" int jdg_host_upload_tp(jdg_ctx *ctx, const jd_host_model *h, int max_
         return rc;
     }
     *out = e;
+    return JD_OK;
+}
+
+// ------------------------------------------------------------------------------------
+// Hebbian --learn pass (janusdoe.c:3416-3447) on the engine's LoRA parliament.
+static float learn_uniform(uint64_t *s) {  // janusdoe.c:191-192
+    uint64_t x = *s;
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    *s = x;
+    return (float)(x & 0x7FFFFFFFull) / (float)0x7FFFFFFF;
+}
+static float learn_normal(uint64_t *s) {  // janusdoe.c:193 (host libm, as the reference)
+    float u1 = learn_uniform(s), u2 = learn_uniform(s);
+    if (u1 < 1e-10f) u1 = 1e-10f;
+    return sqrtf(-2.0f * logf(u1)) * cosf(6.2831853f * u2);
+}
+
+static int learn_alloc(jdg_engine *e) {
+    HostPriv *hp = priv(e);
+    if (hp->learn_x) return JD_OK;
+    const int D = e->D, L = e->L;
+    DALLOC(hp->learn_dyraw, (size_t)D * 4);
+    DALLOC(hp->learn_x, (size_t)D * 4);
+    DALLOC(hp->learn_dy, (size_t)D * 4);
+    DALLOC(hp->learn_sig, 4);
+    DALLOC(hp->learn_next, 4);
+    DALLOC(hp->learn_dead, (size_t)L * JD_MAX_EXPERTS * 4);
+    DALLOC(hp->learn_upd, (size_t)L * JD_MAX_EXPERTS * sizeof(LearnUpd));
+    DALLOC(hp->learn_A, (size_t)L * sizeof(float *));
+    DALLOC(hp->learn_B, (size_t)L * sizeof(float *));
+    DALLOC(hp->learn_alive, (size_t)L * sizeof(int *));
+    std::vector<float *> pa(L), pb(L);
+    std::vector<int *> pl(L);
+    for (int l = 0; l < L; l++) {
+        pa[l] = hp->lora_A[l];
+        pb[l] = hp->lora_B[l];
+        pl[l] = e->hl[l].alive;
+    }
+    CK(cudaMemcpy(hp->learn_A, pa.data(), L * sizeof(float *), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(hp->learn_B, pb.data(), L * sizeof(float *), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(hp->learn_alive, pl.data(), L * sizeof(int *), cudaMemcpyHostToDevice));
+    return JD_OK;
+}
+
+int jdg_reset(jdg_engine *e, int slot);
+int jdg_host_drop_graphs(jdg_engine *e);
+
+extern "C" int jdg_host_learn(jdg_engine *e, const int *toks, int nt, float lr, uint64_t *rng, int *notorch_offset,
+                              int *deaths) {
+    if (!e || !toks || nt < 1 || !rng || !notorch_offset || e->kind != 1 || !priv(e)) return JD_EINVAL;
+    HostPriv *hp = priv(e);
+    if (hp->world != 1 || e->lora_rank < 1) {
+        jdg_set_err(e->ctx, "jdg_host_learn: one GPU and a LoRA parliament are needed");
+        return JD_EUNSUPPORTED;
+    }
+    cudaSetDevice(jdg_ctx_device(e->ctx));
+    int rc = learn_alloc(e);
+    if (rc != JD_OK) return rc;
+    const int L = e->L, D = e->D, R = e->lora_rank, nr = R < kLearnLanes ? R : kLearnLanes;
+    // fresh caches for slot 0 (the reference allocates them per pass); the EMA carries on
+    const size_t kv = (size_t)L * e->max_seq * e->kd * 4;
+    CK(cudaMemsetAsync(e->kc, 0, kv, e->st));
+    CK(cudaMemsetAsync(e->vc, 0, kv, e->st));
+    std::vector<int> alive((size_t)L * JD_MAX_EXPERTS);
+    for (int l = 0; l < L; l++)
+        CK(cudaMemcpyAsync(&alive[(size_t)l * JD_MAX_EXPERTS], e->hl[l].alive, JD_MAX_EXPERTS * 4,
+                           cudaMemcpyDeviceToHost, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    const int saved_generic = e->force_generic;
+    e->force_generic = 1;  // the generic step carries the learning captures
+    hp->learn_on = true;
+    int killed = 0, err_rc = JD_OK;
+    std::vector<int> tr_k(L), tr_sel((size_t)L * kMaxE), dead;
+    std::vector<LearnUpd> upd;
+    for (int t = 0; t + 1 < nt && t < e->max_seq - 1; t++) {
+        int io[3] = {toks[t], t, toks[t + 1]};
+        CK(cudaMemcpyAsync(e->tok, &io[0], 4, cudaMemcpyHostToDevice, e->st));
+        CK(cudaMemcpyAsync(e->pos, &io[1], 4, cudaMemcpyHostToDevice, e->st));
+        CK(cudaMemcpyAsync(hp->learn_next, &io[2], 4, cudaMemcpyHostToDevice, e->st));
+        err_rc = jdg_enqueue_host_step(e, 1);
+        if (err_rc != JD_OK) break;
+        float sig = 0.f;
+        CK(cudaMemcpyAsync(&sig, hp->learn_sig, 4, cudaMemcpyDeviceToHost, e->st));
+        CK(cudaMemcpyAsync(tr_k.data(), e->tr_k, (size_t)L * 4, cudaMemcpyDeviceToHost, e->st));
+        CK(cudaMemcpyAsync(tr_sel.data(), e->tr_sel, (size_t)L * kMaxE * 4, cudaMemcpyDeviceToHost, e->st));
+        CK(cudaStreamSynchronize(e->st));
+        // the experts elected in this token, layer by layer, slot by slot (janusdoe.c:3437-3445)
+        upd.clear();
+        if (fabsf(sig) >= 1e-8f) {
+            for (int l = 0; l < L; l++)
+                for (int x = 0; x < JD_MAX_EXPERTS; x++) {
+                    if (!alive[(size_t)l * JD_MAX_EXPERTS + x]) continue;
+                    bool elected = false;
+                    for (int q = 0; q < tr_k[l]; q++) elected |= tr_sel[(size_t)l * kMaxE + q] == x;
+                    if (!elected) continue;
+                    LearnUpd u;
+                    u.l = l;
+                    u.e = x;
+                    u.base = *notorch_offset % R;
+                    for (int j = 0; j < kLearnLanes; j++) u.noise[j] = j < nr ? learn_normal(rng) : 0.f;
+                    *notorch_offset = (u.base + nr) % R;
+                    upd.push_back(u);
+                }
+        }
+        if (!upd.empty()) {
+            float s = sig > 2.0f ? 2.0f : sig < -2.0f ? -2.0f : sig;
+            LearnArgs a;
+            a.upd = hp->learn_upd; a.A = hp->learn_A; a.B = hp->learn_B; a.alive = hp->learn_alive;
+            a.x = hp->learn_x; a.dy = hp->learn_dy; a.D = D; a.R = R; a.nr = nr; a.lr = lr * s; a.dead = hp->learn_dead;
+            CK(cudaMemcpyAsync(hp->learn_upd, upd.data(), upd.size() * sizeof(LearnUpd), cudaMemcpyHostToDevice, e->st));
+            k_learn_update<<<(unsigned)upd.size(), 256, 0, e->st>>>(a);
+            e->launches++;
+            dead.assign(upd.size(), 0);
+            CK(cudaMemcpyAsync(dead.data(), hp->learn_dead, dead.size() * 4, cudaMemcpyDeviceToHost, e->st));
+            CK(cudaStreamSynchronize(e->st));
+            for (size_t m = 0; m < upd.size(); m++)
+                if (dead[m]) {  // quarantined: the kernel cleared its alive flag on the device
+                    alive[(size_t)upd[m].l * JD_MAX_EXPERTS + upd[m].e] = 0;
+                    killed++;
+                }
+        }
+    }
+    hp->learn_on = false;
+    e->force_generic = saved_generic;
+    if (killed) {
+        // elections, the chain and the batched parliament read the alive lists
+        for (int l = 0; l < L; l++) {
+            std::vector<int> al;
+            for (int x = 0; x < JD_MAX_EXPERTS; x++)
+                if (alive[(size_t)l * JD_MAX_EXPERTS + x]) al.push_back(x);
+            e->n_alive[l] = (int)al.size();
+            al.resize(kMaxE, 0);
+            if (hp->alive_list[l]) CK(cudaMemcpy(hp->alive_list[l], al.data(), kMaxE * 4, cudaMemcpyHostToDevice));
+        }
+        jdg_host_drop_graphs(e);
+    }
+    if (deaths) *deaths = killed;
+    if (err_rc != JD_OK) return err_rc;
+    CK(cudaStreamSynchronize(e->st));
+    return JD_OK;
+}
+
+// A [D][R], B [R][D] and the alive flag of LoRA expert slot x of layer l
+extern "C" int jdg_host_get_expert(jdg_engine *e, int l, int x, float *A, float *B, int *alive) {
+    if (!e || e->kind != 1 || !priv(e) || l < 0 || l >= e->L || x < 0 || x >= JD_MAX_EXPERTS) return JD_EINVAL;
+    HostPriv *hp = priv(e);
+    cudaSetDevice(jdg_ctx_device(e->ctx));
+    const size_t n = (size_t)e->D * e->lora_rank;
+    if (A) CK(cudaMemcpy(A, hp->lora_A[l] + (size_t)x * n, n * 4, cudaMemcpyDeviceToHost));
+    if (B) CK(cudaMemcpy(B, hp->lora_B[l] + (size_t)x * n, n * 4, cudaMemcpyDeviceToHost));
+    if (alive) CK(cudaMemcpy(alive, e->hl[l].alive + x, 4, cudaMemcpyDeviceToHost));
     return JD_OK;
 }
 

@@ -789,6 +789,12 @@ static __global__ __launch_bounds__(256) void k_elect_scan(ElectArgs a, int B) {
     }
 }
 
+// x[i] += y[i] * s (the residual add of a scaled FFN output)
+static __global__ void k_add_scaled(float *x, const float *y, float s, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) x[i] = __fadd_rn(x[i], __fmul_rn(y[i], s));
+}
+
 // ------------------------------------------------------------------------------------
 // Bucket (sequence, election slot) pairs by expert, in ascending sequence order.
 // grid 1, block 512 (warp e = expert slot).  idx[e*B + j] = b; pairrow[b*16+ki] = e*B + j.

@@ -3,11 +3,11 @@
 //
 //     C[t][n] = sum_k X[t][k] * W[n][k]      (t: token rows, n: weight rows)
 //
-// The f32 operands are split into TF32 parts, x = x_hi + x_lo with x_hi the top 10 mantissa
-// bits (exact) and x_lo = x - x_hi (exact in f32, its top 10 bits reach the tensor core), and
-// three kind::tf32 products are accumulated in f32 in tensor memory: W_hi.X_hi + W_hi.X_lo +
-// W_lo.X_hi.  Every product of two TF32 numbers is exact in f32; the dropped W_lo.X_lo and
-// the truncation of the lo parts are below 2^-20 of each term, i.e. f32-level accuracy.
+// The f32 operands are split into TF32 parts, x = x_hi + x_lo with x_hi = x rounded to 10
+// mantissa bits and x_lo = x - x_hi (exact in f32, |x_lo| <= 2^-11 |x|; the tensor core keeps
+// its top 10 bits, so 2^-22 |x|), and four kind::tf32 products are accumulated in f32 in
+// tensor memory: W_hi.X_hi + W_hi.X_lo + W_lo.X_hi + W_lo.X_lo.  Every product of two TF32
+// numbers is exact in f32, so each term carries about 2^-21 relative error.
 //
 // Operands live in global memory already in the shared-memory layout the MMA descriptors
 // address (canonical K-major, no swizzle): for a block of 128 rows and a 32-wide K chunk, the
@@ -17,11 +17,12 @@
 // ([segment][token tile][K chunk][hi | lo], rows past the segment's count zero).  So a stage
 // is four 1-D bulk copies (cp.async.bulk, no tensor maps), and every byte is read once.
 //
-// CTA (128 threads) = one 128-row x 128-token output tile over a K range (split-K CTAs of a
+// CTA (192 threads) = one 128-row x 128-token output tile over a K range (split-K CTAs of a
 // tile add their partials in split order in the last CTA, by ticket): thread 0 streams
-// stages into a 3-deep ring, thread 32 issues the 12 MMAs (M128 N128 K8) of each 32-wide
-// chunk and commits the stage back, then all four warps read their 32 TMEM lanes (rows) and
-// apply the epilogue.  Every wait is bounded by wall time; on a timeout the CTA flags
+// stages into a 3-deep ring; thread 32 issues the 16 MMAs (M128 N128 K8) of each 32-wide
+// chunk into one of two accumulator regions and commits the stage back; warps 2-5 drain each
+// chunk's region into f32 registers with round-to-nearest adds (the tensor core's own
+// accumulation then spans only one chunk, 128 products) and apply the epilogue.  Every wait is bounded by wall time; on a timeout the CTA flags
 // JDG_ERR_TIMEOUT, waits (bounded) for what it issued, frees its tensor memory and returns.
 #pragma once
 #include "jdg_async.cuh"
@@ -37,6 +38,7 @@ constexpr int kTcStages = 3;
 constexpr int kTcStageBytes = 4 * kTcBlk;      // W hi, W lo, X hi, X lo
 constexpr int kTcSmem = 1024 + kTcStages * kTcStageBytes;
 constexpr int kTcMaxSplit = 8;
+constexpr int kTcThreads = 192;                // warp 0 copies, warp 1 MMAs, warps 2-5 drain
 // kind::tf32 instruction descriptor: D f32 (bits 4-5 = 1), A and B TF32 (bits 7-9, 10-12 = 2),
 // both K-major, N = 128 (bits 17-22 = N/8), M = 128 (bits 24-28 = M/16)
 constexpr uint32_t kTcIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(kTcTok >> 3) << 17) |
@@ -46,9 +48,11 @@ constexpr uint32_t kTcIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(k
 __host__ __device__ __forceinline__ uint32_t tc_off(int r, int k) {
     return (uint32_t)((((k >> 2) * 16 + (r >> 3)) * 128) + (r & 7) * 16 + (k & 3) * 4);
 }
+// x = hi + lo: hi is x rounded to 10 mantissa bits (ties away from zero), lo = x - hi is exact
+// in f32 with |lo| <= 2^-11 |x|, and the tensor core's TF32 view of lo keeps it to 2^-22 |x|
 __device__ __forceinline__ void tc_split(float x, float &hi, float &lo) {
-    hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
-    lo = x - hi;  // exact
+    hi = __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+    lo = x - hi;
 }
 
 // Weight blocks of an N x K f32 matrix (rows past N zero): grid-stride over (row, 4-element group).
@@ -75,6 +79,7 @@ static __global__ void k_tc_wprep(const float *__restrict__ W, int N, int K, uin
 // out: [seg][token tile < ttiles][K chunk][hi | lo][16 KB]
 struct TcPrep {
     const float *X;
+    long x_seg;  // row base of segment s: X + s * x_seg
     int ldx, K;
     const int *idx;
     int ldi;
@@ -94,7 +99,7 @@ static __global__ void k_tc_xprep(TcPrep p) {
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (j < n) {
             const int row = p.idx ? p.idx[(size_t)s * p.ldi + j] : j;
-            v = *reinterpret_cast<const float4 *>(p.X + (size_t)row * p.ldx + k4);
+            v = *reinterpret_cast<const float4 *>(p.X + (size_t)s * p.x_seg + (size_t)row * p.ldx + k4);
         }
         float4 h, l;
         tc_split(v.x, h.x, l.x);
@@ -154,6 +159,27 @@ __device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity) {
     }
 }
 
+// 8 consecutive f32 columns (tokens) of this warp's 32 TMEM lanes (rows), waited for
+__device__ __forceinline__ void tc_ld8(uint32_t taddr, float (&v)[8]) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// the same without the wait (several loads in flight, then one tcgen05.wait::ld)
+__device__ __forceinline__ void tc_ld8_nw(uint32_t taddr, float *v) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tc_store(const TcArgs &a, int seg, int t, int n, float v, int lane) {
     float *c = a.C + (size_t)seg * a.c_seg + (size_t)t * a.ldc;
     if (a.epi == EPI_SWIGLU) {
@@ -165,10 +191,10 @@ __device__ __forceinline__ void tc_store(const TcArgs &a, int seg, int t, int n,
     }
 }
 
-static __global__ __launch_bounds__(128) void k_tc32_gemm(TcArgs a) {
+static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
     extern __shared__ __align__(1024) uint8_t tc_sm[];
     uint8_t *stages = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tc_sm) + 1023) & ~(uintptr_t)1023);
-    __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], done;
+    __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], ready[2], freed[2];
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag, s_last;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -184,13 +210,16 @@ static __global__ __launch_bounds__(128) void k_tc32_gemm(TcArgs a) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(&done, 1);
+        for (int q = 0; q < 2; q++) {
+            mbar_init(&ready[q], 1);
+            mbar_init(&freed[q], 4);  // the four drain warps
+        }
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
-                     "r"(kTcTok));
+                     "r"(2 * kTcTok));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -217,64 +246,90 @@ static __global__ __launch_bounds__(128) void k_tc32_gemm(TcArgs a) {
             issued_ld = i + 1;
         }
     } else if (tid == 32) {
-        // ---------------- MMA issuer ----------------
+        // ---------------- MMA issuer: chunk i into accumulator region i % 2 ----------------
         for (int i = 0; i < nloc; i++) {
-            const int s = i % kTcStages;
-            if (!tc_wait(&full[s], (uint32_t)(i / kTcStages) & 1u) || *(volatile int *)&abort_flag) {
+            const int s = i % kTcStages, q = i & 1;
+            bool ok = tc_wait(&full[s], (uint32_t)(i / kTcStages) & 1u);
+            if (ok && i >= 2) ok = tc_wait(&freed[q], (uint32_t)((i >> 1) - 1) & 1u);
+            if (!ok || *(volatile int *)&abort_flag) {
                 abort_flag = 1;
                 break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t st = smem_u32(stages + (size_t)s * kTcStageBytes);
             const uint32_t wh = st, wl = st + kTcBlk, xh = st + 2 * kTcBlk, xl = st + 3 * kTcBlk;
+            const uint32_t d = tmem + (uint32_t)(q * kTcTok);
 #pragma unroll
-            for (int q = 0; q < kTcK / 8; q++) {  // K slices of 8: two K groups of the block
-                const uint32_t o = (uint32_t)q * 2 * 2048;
-                tc_mma(tmem, tc_desc(wh + o), tc_desc(xh + o), (i > 0 || q > 0) ? 1u : 0u);
-                tc_mma(tmem, tc_desc(wh + o), tc_desc(xl + o), 1u);
-                tc_mma(tmem, tc_desc(wl + o), tc_desc(xh + o), 1u);
+            for (int k8 = 0; k8 < kTcK / 8; k8++) {  // K slices of 8: two K groups of the block
+                const uint32_t o = (uint32_t)k8 * 2 * 2048;
+                tc_mma(d, tc_desc(wh + o), tc_desc(xh + o), k8 > 0 ? 1u : 0u);
+                tc_mma(d, tc_desc(wh + o), tc_desc(xl + o), 1u);
+                tc_mma(d, tc_desc(wl + o), tc_desc(xh + o), 1u);
+                tc_mma(d, tc_desc(wl + o), tc_desc(xl + o), 1u);
             }
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                              smem_u32(&empty[s]))
                          : "memory");
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                             smem_u32(&ready[q]))
+                         : "memory");
             issued_mma = i + 1;
         }
-        // the accumulator is complete when everything issued so far has finished
-        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(&done))
-                     : "memory");
     }
     __syncwarp();
-    // ---------------- epilogue: warp w holds rows 32w..32w+31 (TMEM lanes) ----------------
-    const bool got = tc_wait(&done, 0);
-    if (!got) abort_flag = 1;
+    if (warp >= 2) {
+        // ---------------- drain: every chunk's product added in f32 (round to nearest) ----------------
+        // warp w reads TMEM lanes 32 (w % 4) .. : its weight rows
+        const int quarter = warp & 3, row = quarter * 32 + lane, n = rt * kTcRows + row;
+        float acc[kTcTok];
+#pragma unroll
+        for (int c = 0; c < kTcTok; c++) acc[c] = 0.f;
+        bool ok = true;
+        for (int i = 0; i < nloc; i++) {
+            const int q = i & 1;
+            if (!tc_wait(&ready[q], (uint32_t)(i >> 1) & 1u)) ok = false;
+            if (__any_sync(JDG_FULL, !ok || *(volatile int *)&abort_flag)) {  // leave as a whole warp
+                ok = false;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(q * kTcTok);
+#pragma unroll
+            for (int c0 = 0; c0 < kTcTok; c0 += 32) {
+                float v[32];
+                tc_ld8_nw(base + (uint32_t)c0, v);
+                tc_ld8_nw(base + (uint32_t)c0 + 8, v + 8);
+                tc_ld8_nw(base + (uint32_t)c0 + 16, v + 16);
+                tc_ld8_nw(base + (uint32_t)c0 + 24, v + 24);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                for (int j = 0; j < 32; j++) acc[c0 + j] = __fadd_rn(acc[c0 + j], v[j]);
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&freed[q]);
+        }
+        if (!ok) abort_flag = 1;
+        if (ok && nloc > 0) {
+            if (a.ksplit == 1) {
+#pragma unroll
+                for (int c = 0; c < kTcTok; c++)
+                    if (c < ntok) tc_store(a, seg, tt * kTcTok + c, n, acc[c], lane);
+            } else {
+                const size_t tile = ((size_t)seg * gridDim.y + tt) * gridDim.x + rt;
+                float *pp = a.part + (tile * a.ksplit + ks) * (size_t)kTcTok * kTcRows;
+#pragma unroll
+                for (int c = 0; c < kTcTok; c++)
+                    if (c < ntok) pp[(size_t)c * kTcRows + row] = acc[c];
+            }
+        }
+    }
     __syncthreads();
-    const bool ok = !abort_flag && nloc > 0;
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const int row = warp * 32 + lane, n = rt * kTcRows + row;
-    const uint32_t tbase = tmem + ((uint32_t)(warp * 32) << 16);
-    if (ok && a.ksplit == 1) {
-        for (int c0 = 0; c0 < kTcTok; c0 += 8) {
-            if (c0 >= ntok) break;  // uniform over the warp
-            float v[8];
-            qm_ld8_tc(tbase + (uint32_t)c0, v);
-#pragma unroll
-            for (int j = 0; j < 8; j++)
-                if (c0 + j < ntok) tc_store(a, seg, tt * kTcTok + c0 + j, n, v[j], lane);
-        }
-    } else if (ok) {
+    if (a.ksplit > 1 && !abort_flag && nloc > 0) {
+        // the last CTA of this tile adds the partials in split order
         const size_t tile = ((size_t)seg * gridDim.y + tt) * gridDim.x + rt;
-        float *pp = a.part + (tile * a.ksplit + ks) * (size_t)kTcTok * kTcRows;
-        for (int c0 = 0; c0 < kTcTok; c0 += 8) {
-            if (c0 >= ntok) break;
-            float v[8];
-            qm_ld8_tc(tbase + (uint32_t)c0, v);
-#pragma unroll
-            for (int j = 0; j < 8; j++)
-                if (c0 + j < ntok) pp[(size_t)(c0 + j) * kTcRows + row] = v[j];
-        }
-        __threadfence();
-        __syncthreads();
         if (tid == 0) {
+            __threadfence();
             const unsigned tk = atomicAdd(a.tickets + tile, 1u);
             s_last = tk == (unsigned)a.ksplit - 1;
             if (s_last) {
@@ -283,11 +338,12 @@ static __global__ __launch_bounds__(128) void k_tc32_gemm(TcArgs a) {
             }
         }
         __syncthreads();
-        if (s_last) {
+        if (s_last && warp >= 2) {
+            const int row = (warp & 3) * 32 + lane, n = rt * kTcRows + row;
             const float *p0 = a.part + tile * a.ksplit * (size_t)kTcTok * kTcRows;
             for (int t = 0; t < ntok; t++) {
                 float acc = 0.f;
-                for (int z = 0; z < a.ksplit; z++) acc += __ldcg(p0 + ((size_t)z * kTcTok + t) * kTcRows + row);
+                for (int z = 0; z < a.ksplit; z++) acc = __fadd_rn(acc, __ldcg(p0 + ((size_t)z * kTcTok + t) * kTcRows + row));
                 tc_store(a, seg, tt * kTcTok + t, n, acc, lane);
             }
         }
@@ -304,7 +360,7 @@ static __global__ __launch_bounds__(128) void k_tc32_gemm(TcArgs a) {
     __syncthreads();
     if (warp == 0) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTok));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kTcTok));
     }
 }
 

@@ -8,7 +8,7 @@
  *       or seeded synthetic weights; the prompt's bytes are the reference's byte tokens
  *       (ids 0..255, janusdoe.c:228); chat() samples at temperature 0.8, top-k 40.
  *   m --host model.gguf [--ask TEXT] [--rope-neox | --rope-norm] [--lora FILE]
- *               [--lora-rank R] [--gen N]
+ *               [--lora-rank R] [--gen N] [--learn FILE]
  *       host mode (janusdoe.c:3762-3795): gguf_host_load, BOS + whole-word tokenisation
  *       (jd_host_tokenize), greedy generation with the LoRA parliament, stop at EOS.
  *   --print-ids prints the prompt's and the generated token ids after the text.
@@ -32,7 +32,22 @@ static void usage(void) {
     printf("  --lora FILE     LoRA parliament sidecar for --host (default: drawn from --seed)\n");
     printf("  --gen N         tokens to generate (default 64)\n");
     printf("  --temp T --topk K   own-model sampling (default 0.8 and 40, as chat())\n");
+    printf("  --learn FILE    --host: Hebbian LoRA pass over the file's tokens (lr 0.01) before generating\n");
     printf("  --print-ids     also print the prompt and generated token ids\n");
+}
+
+/* the whole file as a NUL-terminated string (NULL on failure) */
+static char *read_text(const char *path) {
+    FILE *f = fopen(path, "rb");
+    if (!f) return NULL;
+    fseek(f, 0, SEEK_END);
+    long n = ftell(f);
+    fseek(f, 0, SEEK_SET);
+    char *t = n >= 0 ? malloc((size_t)n + 1) : NULL;
+    if (t && fread(t, 1, (size_t)n, f) != (size_t)n) { free(t); t = NULL; }
+    if (t) t[n] = 0;
+    fclose(f);
+    return t;
 }
 
 static void print_ids(const char *what, const int *ids, int n) {
@@ -50,7 +65,7 @@ int main(int argc, char **argv) {
     int depth = 0, gen = 64, topk = 40, rope_override = -1, vocab = 0, lora_rank = 16, show_ids = 0;
     uint64_t seed = 0;
     float temp = 0.8f;
-    const char *gguf = NULL, *host = NULL, *ask = "The capital of France is", *lora = NULL;
+    const char *gguf = NULL, *host = NULL, *ask = "The capital of France is", *lora = NULL, *learn = NULL;
     for (int i = 1; i < argc; i++) {
         if (!strcmp(argv[i], "--depth") && i + 1 < argc) depth = atoi(argv[++i]);
         else if (!strcmp(argv[i], "--gguf") && i + 1 < argc) gguf = argv[++i];
@@ -59,6 +74,7 @@ int main(int argc, char **argv) {
         else if (!strcmp(argv[i], "--host") && i + 1 < argc) host = argv[++i];
         else if (!strcmp(argv[i], "--ask") && i + 1 < argc) ask = argv[++i];
         else if (!strcmp(argv[i], "--lora") && i + 1 < argc) lora = argv[++i];
+        else if (!strcmp(argv[i], "--learn") && i + 1 < argc) learn = argv[++i];
         else if (!strcmp(argv[i], "--lora-rank") && i + 1 < argc) lora_rank = atoi(argv[++i]);
         else if (!strcmp(argv[i], "--gen") && i + 1 < argc) gen = atoi(argv[++i]);
         else if (!strcmp(argv[i], "--temp") && i + 1 < argc) temp = (float)atof(argv[++i]);
@@ -81,13 +97,26 @@ int main(int argc, char **argv) {
         if (rc != JD_OK) return fail(ctx, "LoRA parliament", rc);
         printf("[m] host %s: arch=%s rope=%s dim=%d layers=%d heads=%d/%d vocab=%d\n", host, hm.arch,
                hm.rope_norm ? "NORM" : "NEOX", hm.dim, hm.n_layers, hm.n_heads, hm.n_kv_heads, hm.vocab);
-        const int max_seq = 256;
+        const int max_seq = 512;
         int toks[256], nt = 0;
         if (hm.bos >= 0 && hm.bos < hm.vocab) toks[nt++] = hm.bos;
         if (hm.vocab_tokens) nt += jd_host_tokenize(&hm, ask, toks + nt, 200);
         if (nt == 0) toks[nt++] = 1;
         if (gen > max_seq - nt) gen = max_seq - nt;
         if ((rc = jdg_host_upload(ctx, &hm, 1, max_seq, &eng)) != JD_OK) return fail(ctx, "upload", rc);
+        if (learn) {  /* janusdoe.c:3776-3788: tokens of the file (at most 512), one learning pass */
+            char *text = read_text(learn);
+            if (text && hm.vocab_tokens) {
+                int lt[512], nl = jd_host_tokenize(&hm, text, lt, 512), deaths = 0, offset = 0;
+                uint64_t rng = 42; /* the reference's RNG state after loading */
+                if ((rc = jdg_host_learn(eng, lt, nl, 0.01f, &rng, &offset, &deaths)) != JD_OK)
+                    return fail(ctx, "learn", rc);
+                printf("[learn] %s: %d tokens | quarantined %d\n", learn, nl, deaths);
+            } else {
+                printf("[learn] cannot read %s or host has no vocab\n", learn);
+            }
+            free(text);  /* the EMA carries into the generation, as in the reference */
+        }
         if ((rc = jdg_set_prompt(eng, 1, toks, nt, &nt, NULL)) != JD_OK) return fail(ctx, "prompt", rc);
         if ((rc = jdg_run(eng, 1, nt - 1 + gen)) != JD_OK) return fail(ctx, "decode", rc);
         int *out = malloc(sizeof(int) * gen);

@@ -120,6 +120,8 @@ def lib():
         "jdg_set_prompt": [C.c_void_p, C.c_int, I32P, C.c_int, I32P, U64P],
         "jdg_run": [C.c_void_p, C.c_int, C.c_int],
         "jdg_prefill": [C.c_void_p, C.c_int],
+        "jdg_host_learn": [C.c_void_p, I32P, C.c_int, C.c_float, U64P, I32P, I32P],
+        "jdg_host_get_expert": [C.c_void_p, C.c_int, C.c_int, F32P, F32P, I32P],
         "jdg_get_prefill_trace": [C.c_void_p, C.c_int, C.POINTER(JdgTrace)],
         "jdg_get_state": [C.c_void_p, C.c_int, I32P, I32P],
         "jdg_get_history": [C.c_void_p, C.c_int, C.c_int, I32P],
@@ -347,6 +349,22 @@ class Engine:
         ms = C.c_float(0)
         lib().jdg_last_run_ms(self.h, C.byref(ms))
         return ms.value
+
+    def host_learn(self, toks, lr, rng, offset):
+        """Hebbian --learn pass over toks; returns (deaths, rng state, notorch offset)."""
+        t = np.ascontiguousarray(toks, np.int32)
+        st = np.array([rng], np.uint64)
+        off = np.array([offset], np.int32)
+        dead = np.zeros(1, np.int32)
+        self._ck(lib().jdg_host_learn(self.h, _p(t, I32P), t.size, lr, _p(st, U64P), _p(off, I32P), _p(dead, I32P)))
+        return int(dead[0]), int(st[0]), int(off[0])
+
+    def expert(self, l, x, dim, rank):
+        A = np.zeros((dim, rank), np.float32)
+        B = np.zeros((rank, dim), np.float32)
+        al = np.zeros(1, np.int32)
+        self._ck(lib().jdg_host_get_expert(self.h, l, x, _p(A, F32P), _p(B, F32P), _p(al, I32P)))
+        return A, B, int(al[0])
 
     def prefill(self, B):
         """Batched prompt prefill of slots 0..B-1 (after set_prompt); returns device ms."""

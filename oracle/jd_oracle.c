@@ -724,8 +724,10 @@ void jdo_host_free(jdo_host *h) {
 
 int jdo_host_state_alloc(const jdo_host *h, jdo_host_state *s, int max_seq) {
     size_t n = (size_t)h->n_layers * max_seq * h->n_kv_heads * h->head_dim;
+    memset(s, 0, sizeof(*s));
     s->max_seq = max_seq; s->kc = calloc(n, 4); s->vc = calloc(n, 4);
-    if (!s->kc || !s->vc) return -1;
+    s->host_x = calloc(h->dim, 4); s->host_dy = calloc(h->dim, 4);
+    if (!s->kc || !s->vc || !s->host_x || !s->host_dy) return -1;
     jdo_host_state_reset(h, s);
     return 0;
 }
@@ -734,7 +736,9 @@ void jdo_host_state_reset(const jdo_host *h, jdo_host_state *s) {
     memset(s->kc, 0, n * 4); memset(s->vc, 0, n * 4);
     for (int l = 0; l < JDO_MAX_LAYERS; l++) s->consensus[l] = h->consensus0[l];
 }
-void jdo_host_state_free(jdo_host_state *s) { free(s->kc); free(s->vc); memset(s, 0, sizeof(*s)); }
+void jdo_host_state_free(jdo_host_state *s) {
+    free(s->kc); free(s->vc); free(s->host_x); free(s->host_dy); memset(s, 0, sizeof(*s));
+}
 
 /* janusdoe.c:3054-3087 host_parliament_elect */
 int jdo_host_elect(const jdo_host *h, int l, float *cons_io, const float *xn, int D, int *selected, float *weights, jdo_elect *tr) {
@@ -849,6 +853,10 @@ void jdo_host_forward(const jdo_host *h, jdo_host_state *s, int token, int pos, 
             for (int i = 0; i < HH; i++) gate[i] = gate[i] / (1.0f + expf(-gate[i])) * up[i];
             jdo_mv(fo, h->layers[l].down, h->layers[l].down_dt, gate, D, HH);
             for (int i = 0; i < D; i++) x[i] += fo[i] * h->layer_focus[l];
+            /* janusdoe.c:3274-3278: the learning target dy, the FFN output RMS-normalised */
+            double sd = 0; for (int i = 0; i < D; i++) sd += (double)fo[i] * fo[i];
+            float inv = 1.0f / (sqrtf((float)(sd / D)) + 1e-8f);
+            for (int i = 0; i < D; i++) s->host_dy[i] = fo[i] * inv;
         }
         {
             int sel[JDO_MAX_EXPERTS]; float w[JDO_MAX_EXPERTS];
@@ -861,6 +869,7 @@ void jdo_host_forward(const jdo_host *h, jdo_host_state *s, int token, int pos, 
                 memset(t, 0, (size_t)(R > 0 ? R : 1) * 4);
                 for (int r = 0; r < R; r++) { float sacc = 0; for (int j = 0; j < D; j++) sacc += Bm[r * D + j] * xn[j]; t[r] = sacc; }
                 for (int i = 0; i < D; i++) { float sacc = 0; for (int r = 0; r < R; r++) sacc += A[i * R + r] * t[r]; x[i] += wt * sacc; }
+                s->tokens_seen[l][e]++;   /* janusdoe.c:3300 */
             }
         }
     }
@@ -868,6 +877,89 @@ void jdo_host_forward(const jdo_host *h, jdo_host_state *s, int token, int pos, 
     ss = 1.0f / sqrtf(ss / D + h->rms_eps);
     if (h->output_norm) for (int i = 0; i < D; i++) x[i] = x[i] * ss * h->output_norm[i];
     else for (int i = 0; i < D; i++) x[i] *= ss;
+    {   /* janusdoe.c:3311-3315: the learning target x, the final hidden RMS-normalised */
+        double sx = 0; for (int i = 0; i < D; i++) sx += (double)x[i] * x[i];
+        float inv = 1.0f / (sqrtf((float)(sx / D)) + 1e-8f);
+        for (int i = 0; i < D; i++) s->host_x[i] = x[i] * inv;
+    }
     jdo_mv(logits, h->output, h->output_dt, x, h->vocab, D);
     free(x); free(t); free(xn); free(q); free(k); free(v); free(ao_in); free(ao); free(fn); free(gate); free(up); free(fo); free(att);
+}
+
+/* ============================ Hebbian --learn =========================== */
+/* janusdoe.c:3091-3096 host_prophecy_debt */
+static float jdo_prophecy_debt(const float *lg, int chosen, int n) {
+    if (n <= 0 || chosen < 0 || chosen >= n) return 0.0f;
+    float mx = lg[0]; for (int i = 1; i < n; i++) if (lg[i] > mx) mx = lg[i];
+    float diff = mx - lg[chosen];
+    return diff > 0.0f ? diff / (diff + 1.0f) : 0.0f;
+}
+#define JDO_NOTORCH_RANK 4
+/* janusdoe.c:3102-3132 host_notorch_step with the global RNG and offset made explicit */
+static void jdo_notorch_step(float *A, float *B, int D, int rank, const float *x, const float *dy, float signal,
+                             float lr_base, uint64_t *rng, int *offset) {
+    if (fabsf(signal) < 1e-8f) return;
+    if (signal > 2.0f) signal = 2.0f;
+    if (signal < -2.0f) signal = -2.0f;
+    float lr = lr_base * signal;
+    int nr = JDO_NOTORCH_RANK; if (nr > rank) nr = rank;
+    int base = *offset % rank;
+    float u[JDO_NOTORCH_RANK];
+    for (int j = 0; j < nr; j++) {
+        int r = (base + j) % rank;
+        float sacc = 0; for (int i = 0; i < D; i++) sacc += B[r * D + i] * dy[i];
+        sacc += jdo_rand_normal(rng) * 0.01f;
+        if (sacc > 1.0f) sacc = 1.0f;
+        if (sacc < -1.0f) sacc = -1.0f;
+        u[j] = sacc;
+    }
+    for (int j = 0; j < nr; j++) {
+        int r = (base + j) % rank; float ur = u[j];
+        for (int i = 0; i < D; i++) { float *a = &A[i * rank + r]; *a += lr * ur * (x[i] - ur * (*a)); }
+        for (int i = 0; i < D; i++) { float *b = &B[r * D + i]; *b += lr * ur * (dy[i] - ur * (*b)); }
+    }
+    *offset = (base + nr) % rank;
+    int n = D * rank; const float cap = 0.05f;
+    double sa = 0, sb = 0; for (int i = 0; i < n; i++) { sa += (double)A[i] * A[i]; sb += (double)B[i] * B[i]; }
+    float ra = (float)sqrt(sa / n), rb = (float)sqrt(sb / n);
+    if (ra > cap) { float f = cap / ra; for (int i = 0; i < n; i++) A[i] *= f; }
+    if (rb > cap) { float f = cap / rb; for (int i = 0; i < n; i++) B[i] *= f; }
+}
+/* janusdoe.c:3136-3144 host_lora_poisoned */
+static int jdo_lora_poisoned(const float *A, const float *B, int D, int rank) {
+    int n = D * rank; double s2 = 0; float mx = 0;
+    for (int i = 0; i < n; i++) { float a = A[i]; if (!isfinite(a)) return 1; float ab = fabsf(a); if (ab > mx) mx = ab; s2 += (double)a * a; }
+    for (int i = 0; i < n; i++) { float b = B[i]; if (!isfinite(b)) return 1; float ab = fabsf(b); if (ab > mx) mx = ab; s2 += (double)b * b; }
+    if (mx > 8.0f) return 1;
+    if (sqrt(s2 / (2.0 * n)) > 5.0) return 1;
+    return 0;
+}
+/* janusdoe.c:3420-3447 host_learn_run: fresh caches, the EMA state carried on */
+int jdo_host_learn_run(jdo_host *h, jdo_host_state *s, const int *toks, int nt, float lr, uint64_t *rng,
+                       int *notorch_offset) {
+    size_t n = (size_t)h->n_layers * s->max_seq * h->n_kv_heads * h->head_dim;
+    memset(s->kc, 0, n * 4); memset(s->vc, 0, n * 4);
+    float *lg = malloc((size_t)h->vocab * 4);
+    if (!lg) return 0;
+    memset(s->tokens_seen, 0, sizeof(s->tokens_seen));
+    int deaths = 0;
+    for (int t = 0; t + 1 < nt && t < s->max_seq - 1; t++) {
+        jdo_host_forward(h, s, toks[t], t, lg, NULL);
+        int nxt = toks[t + 1];
+        float signal = 0.0f;
+        if (nxt >= 0 && nxt < h->vocab) {
+            float pd = jdo_prophecy_debt(lg, nxt, h->vocab);
+            signal = pd > 0.3f ? -pd : (1.0f - pd) * 0.1f;
+        }
+        for (int l = 0; l < h->n_layers && l < JDO_MAX_LAYERS; l++)
+            for (int e = 0; e < JDO_MAX_EXPERTS; e++) {
+                if (!h->alive[l][e] || s->tokens_seen[l][e] == 0 || !h->A[l][e] || !h->B[l][e]) continue;
+                jdo_notorch_step(h->A[l][e], h->B[l][e], h->dim, h->lora_rank, s->host_x, s->host_dy, signal, lr,
+                                 rng, notorch_offset);
+                if (jdo_lora_poisoned(h->A[l][e], h->B[l][e], h->dim, h->lora_rank)) { h->alive[l][e] = 0; deaths++; }
+                s->tokens_seen[l][e] = 0;
+            }
+    }
+    free(lg);
+    return deaths;
 }

@@ -118,6 +118,8 @@ typedef struct {
     int max_seq;
     float *kc, *vc;                         /* [L][max_seq][kd] */
     float consensus[JDO_MAX_LAYERS];
+    float *host_x, *host_dy;                /* learning captures of the last forward (janusdoe.c:3274, 3311) */
+    int tokens_seen[JDO_MAX_LAYERS][JDO_MAX_EXPERTS];
 } jdo_host_state;
 
 int  jdo_rope_norm_for_arch(const char *arch);                              /* janusdoe.c:3153-3156 */
@@ -131,6 +133,12 @@ int  jdo_host_elect(const jdo_host *h, int l, float *consensus, const float *xn,
                     int *selected, float *weights, jdo_elect *trace);      /* janusdoe.c:3054-3087 */
 void jdo_host_forward(const jdo_host *h, jdo_host_state *s, int token, int pos,
                       float *logits, jdo_elect *trace);                     /* janusdoe.c:3160-3322 */
+/* Hebbian adaptation pass over a token stream (janusdoe.c:3416-3447): per token a forward
+ * from position 0 of fresh caches, the prophecy-debt signal of the next token, a notorch
+ * step on every expert elected in that token, quarantine.  The reference's global RNG state
+ * and notorch offset are explicit here (in/out).  Returns the experts killed. */
+int  jdo_host_learn_run(jdo_host *h, jdo_host_state *s, const int *toks, int nt, float lr,
+                        uint64_t *rng, int *notorch_offset);
 
 #ifdef __cplusplus
 }

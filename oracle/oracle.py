@@ -73,7 +73,8 @@ class JdoHost(C.Structure):
 
 
 class JdoHostState(C.Structure):
-    _fields_ = [("max_seq", C.c_int), ("kc", F32P), ("vc", F32P), ("consensus", C.c_float * MAXL)]
+    _fields_ = [("max_seq", C.c_int), ("kc", F32P), ("vc", F32P), ("consensus", C.c_float * MAXL),
+                ("host_x", F32P), ("host_dy", F32P), ("tokens_seen", (C.c_int * MAXE) * MAXL)]
 
 
 def trace_to_arrays(tr, L):
@@ -135,6 +136,8 @@ class Oracle:
                                        C.POINTER(JdoElect)]
         L.jdo_host_elect.argtypes = [C.POINTER(JdoHost), C.c_int, C.POINTER(C.c_float), F32P, C.c_int, I32P, F32P,
                                      C.POINTER(JdoElect)]
+        L.jdo_host_learn_run.argtypes = [C.POINTER(JdoHost), C.POINTER(JdoHostState), I32P, C.c_int, C.c_float,
+                                         C.POINTER(C.c_uint64), I32P]
 
     # ---- helpers
     def splitmix64(self, x):
@@ -269,6 +272,21 @@ class HostModel:
     def ema(self):
         return np.array(self.s.consensus[: self.h.n_layers], np.float32)
 
+    def learn(self, toks, lr, rng, offset):
+        """host_learn_run over toks; returns (deaths, rng, offset)."""
+        t = np.ascontiguousarray(toks, np.int32)
+        st, off = C.c_uint64(rng), C.c_int(offset)
+        d = self.lib.jdo_host_learn_run(C.byref(self.h), C.byref(self.s), iptr(t), t.size, lr, C.byref(st),
+                                        C.byref(off))
+        return d, st.value, off.value
+
+    def expert(self, l, e):
+        """(A [D][R], B [R][D], alive) of expert slot e in layer l."""
+        D, R = self.h.dim, self.h.lora_rank
+        A = np.ctypeslib.as_array(self.h.A[l][e], (D, R)).copy() if self.h.A[l][e] else None
+        B = np.ctypeslib.as_array(self.h.B[l][e], (R, D)).copy() if self.h.B[l][e] else None
+        return A, B, int(self.h.alive[l][e])
+
     def close(self):
         if self.h.map:
             self.lib.jdo_host_state_free(C.byref(self.s))
@@ -308,6 +326,8 @@ class Reference:
         L.jdr_host_reset_seq.argtypes = [C.c_int]
         L.jdr_host_forward.argtypes = [C.c_int, C.c_int, F32P, F32P]
         L.jdr_host_tokenize.argtypes = [C.c_char_p, I32P, C.c_int]
+        L.jdr_host_learn.argtypes = [I32P, C.c_int, C.c_int, C.c_float, C.POINTER(C.c_uint64), I32P]
+        L.jdr_host_expert.argtypes = [C.c_int, C.c_int, F32P, F32P]
         L.jdr_host_decode_print.argtypes = [C.c_int, C.c_char_p, C.c_int]
         self.depth = 0
         self.V = 0
@@ -353,6 +373,19 @@ class Reference:
         self.lib.jdr_host_dims(iptr(d))
         self.hdims = d
         self.hL, self.hV = int(d[0]), int(d[6])
+
+    def host_learn(self, toks, max_seq, lr, rng, offset):
+        t = np.ascontiguousarray(toks, np.int32)
+        st, off = C.c_uint64(rng), C.c_int(offset)
+        d = self.lib.jdr_host_learn(iptr(t), t.size, max_seq, lr, C.byref(st), C.byref(off))
+        return d, st.value, off.value
+
+    def host_expert(self, l, e):
+        D, R = int(self.hdims[1]), int(self.lib.jdr_lora_rank())
+        A = np.zeros((D, R), np.float32)
+        B = np.zeros((R, D), np.float32)
+        alive = self.lib.jdr_host_expert(l, e, fptr(A), fptr(B))
+        return A, B, int(alive)
 
     def host_tokenize(self, text, max_ids=256):
         out = np.zeros(max(1, max_ids), np.int32)

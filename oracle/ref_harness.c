@@ -193,6 +193,23 @@ JDR_API int jdr_host_forward(int token, int pos, float *logits, float *ema) {
     if (ema) for (int l = 0; l < g_h.host_n_layers && l < LORA_MAX_LAYERS; l++) ema[l] = g_h.consensus[l];
     return 0;
 }
+/* host_learn_run (janusdoe.c:3420) with the global RNG state and notorch offset set from /
+ * returned to the caller; caches of max_seq positions */
+JDR_API int jdr_host_learn(const int *toks, int nt, int max_seq, float lr, uint64_t *rng, int *offset) {
+    rng_state = *rng;
+    host_notorch_offset = *offset;
+    int d = host_learn_run(&g_h, toks, nt, max_seq, lr);
+    *rng = rng_state;
+    *offset = host_notorch_offset;
+    return d;
+}
+/* expert (l, e)'s LoRA factors A [D][R], B [R][D] and its alive flag */
+JDR_API int jdr_host_expert(int l, int e, float *A, float *B) {
+    HostExpert *ex = &g_h.experts[l][e];
+    if (ex->A && A) memcpy(A, ex->A, (size_t)g_h.host_dim * LORA_RANK * 4);
+    if (ex->B && B) memcpy(B, ex->B, (size_t)g_h.host_dim * LORA_RANK * 4);
+    return ex->alive;
+}
 /* host_tokenize on the loaded vocabulary (janusdoe.c:3334) */
 JDR_API int jdr_host_tokenize(const char *text, int *out, int max) { return host_tokenize(&g_h, text, out, max); }
 /* host_decode_print (janusdoe.c:3348) captured from stdout into buf (NUL-terminated) */

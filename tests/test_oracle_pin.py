@@ -118,3 +118,34 @@ def test_loaders_reject_truncated(orc, jd, tmp_path):
             HostModel(orc, bad, 16)
         with pytest.raises(jd.JdError):
             jd.HostModel(bad)
+
+
+def test_host_learn_matches_reference(jd, orc, tmp_path):
+    """The oracle's Hebbian --learn pass (notorch steps on the elected experts, prophecy-debt
+    signal, RMS cap, quarantine; janusdoe.c:3091-3147, 3416-3447) equals the reference's
+    host_learn_run bit for bit: every expert's A and B, alive flags, RNG state and offset."""
+    from oracle.oracle import HostModel as OHost, Reference
+    path = str(tmp_path / "learn.gguf")
+    jd.write_synthetic_gguf(path, "llama", 2, 256, 512, 4, 2, 500, 1e4, 1e-5, 8, 9, 0.02)
+    ref = Reference("")
+    ref.host_load(path)
+    ref.lib.jdr_host_lora_seed(5, 4, 0.01, 1.0 / 16)
+    om = OHost(orc, path, 16, -1, 64)
+    om.lora_seed(5, 4, 0.01, 1.0 / 16)
+    try:
+        toks = np.random.default_rng(3).integers(0, 500, 24).astype(np.int32)
+        for lr, rounds in ((0.05, 2), (3.0, 1)):
+            for _ in range(rounds):
+                got = om.learn(toks, lr, 42, 1)
+                exp = ref.host_learn(toks, 64, lr, 42, 1)
+                assert got == exp, (got, exp)
+                for l in range(2):
+                    for e in range(16):
+                        a1, b1, al1 = om.expert(l, e)
+                        a2, b2, al2 = ref.host_expert(l, e)
+                        assert al1 == al2, (l, e)
+                        if a1 is not None:
+                            assert np.array_equal(a1, a2) and np.array_equal(b1, b2), (l, e)
+    finally:
+        om.close()
+        ref.lib.jdr_host_free()

@@ -7,7 +7,7 @@ Workloads are the synthetic configs: depth-4 (dim 256, 4 experts, vocab 2256), d
 import numpy as np
 import pytest
 
-from _util import LOGIT_TOL, compare_trace, greedy_near_tie, logit_err
+from _util import LOGIT_TOL, compare_trace, compare_trace_ties, greedy_near_tie, logit_err
 from oracle.oracle import OwnModel
 
 pytestmark = pytest.mark.gpu
@@ -249,12 +249,17 @@ def test_batched_prefill_matches_token_by_token(jd, orc, gpu_ctx, P):
         tok, p = eng.state(1)
         assert int(p[0]) == P - 1 and int(tok[0]) == int(prompt[-1])
         tr = eng.prefill_trace(P - 1)
-        ties = 0
+        ties = []
         for t in range(P - 1):
-            bad = compare_trace(tr, traces[t], 12, b=t)
+            bad, tie = compare_trace_ties(tr, traces[t], 12, b=t)
             assert not bad, (t, bad[:3])
+            if tie:             # a reference near-tie: the residual streams part here
+                ties.append((t, tie))
+                break
+        print("prefill P=%d: near-ties %s" % (P, ties))
         eng.run(1, G)   # the last prompt token, then greedy tokens
-        assert list(eng.history(1, G)[0]) == exp
+        if not ties:
+            assert list(eng.history(1, G)[0]) == exp
     finally:
         eng.close()
         om.close()
