@@ -465,8 +465,6 @@ static int tc_build(jdg_engine *e, const jd_model *m) {
     e->tc_xt_bytes = (size_t)kMaxE * tt * (kmax / kTcK) * 2 * kTcBlk;
     DALLOC(e->tc_xt, e->tc_xt_bytes);
     DALLOC(e->tc_part, (size_t)64 << 20);
-    DALLOC(e->tc_tickets, 16384 * 4);
-    CK(cudaMemsetAsync(e->tc_tickets, 0, 16384 * 4, e->st));
     CK(cudaFuncSetAttribute(k_tc32_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));
     CK(cudaStreamSynchronize(e->st));
     e->tc_ok = 1;
@@ -488,15 +486,20 @@ static void launch_tc(jdg_engine *e, const uint8_t *const *wt, int nseg, const f
     int ks = 1;
     const int tiles = rtiles * ttiles * nseg;
     if (nseg == 1)
-        while (ks < kTcMaxSplit && tiles * (ks + 1) <= 160 && nkc / (ks + 1) >= 2) ks++;
+        while (ks < kTcMaxSplit && tiles * (ks + 1) <= 148 && nkc / (ks + 1) >= 2) ks++;
     const int per = (nkc + ks - 1) / ks;
     ks = (nkc + per - 1) / per;
     TcArgs a = {};
     a.wt = wt; a.xt = e->tc_xt; a.cnt = cnt; a.M = M; a.n_rows = n_rows; a.nkc = nkc; a.ttiles = ttiles;
     a.C = C; a.ldc = ldc; a.c_seg = c_seg; a.epi = epi; a.alpha = alpha; a.ksplit = ks; a.part = e->tc_part;
-    a.tickets = e->tc_tickets; a.err = e->err;
+    a.err = e->err;
     k_tc32_gemm<<<dim3(rtiles, ttiles, nseg * ks), kTcThreads, kTcSmem, e->st>>>(a);
     e->launches += 2;
+    if (ks > 1) {
+        const long items = (long)nseg * ttiles * rtiles * kTcTok * (kTcRows / 4);
+        k_tc_reduce<<<(int)std::min<long>((items + 255) / 256, 148 * 8), 256, 0, e->st>>>(a, rtiles, nseg);
+        e->launches++;
+    }
 }
 
 static int pick_bm(int B) { return B <= 16 ? 16 : B <= 32 ? 32 : 64; }

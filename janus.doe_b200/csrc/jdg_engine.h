@@ -98,7 +98,6 @@ struct jdg_engine {
     uint8_t *tc_xt = nullptr;            // activation blocks, sized for 16 segments
     size_t tc_xt_bytes = 0;
     float *tc_part = nullptr;            // split-K partials
-    unsigned *tc_tickets = nullptr;
     // prompt prefill buffers (own model, allocated at the first jdg_prefill; rows = tokens)
     float *pf_x = nullptr, *pf_xb = nullptr, *pf_qkv = nullptr, *pf_att = nullptr, *pf_part = nullptr;
     float *pf_hbuf = nullptr, *pf_ybuf = nullptr, *pf_selw = nullptr, *pf_votes = nullptr, *pf_cs = nullptr;

@@ -400,9 +400,25 @@ struct AttnArgs {
     float scale, bias, clamp, inv_clamp;
     float *part;  // [B][H][nchunk][HD+2]
 };
+// Per warp: the 16 key and 16 value rows of its positions (t = warp + 4i) are loaded as
+// vectors before any use, so 32 row loads per warp are in flight at once.
+template <int E>
+struct AttnVec;
+template <>
+struct AttnVec<2> {
+    using T = float2;
+    __device__ static void get(const T &v, float (&o)[2]) { o[0] = v.x; o[1] = v.y; }
+};
+template <>
+struct AttnVec<4> {
+    using T = float4;
+    __device__ static void get(const T &v, float (&o)[4]) { o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w; }
+};
 template <int HD>
 static __global__ __launch_bounds__(128) void k_attn_partial(AttnArgs a) {
     constexpr int E = HD / 32;  // dims per lane
+    constexpr int TW = kAttnChunk / 4;  // positions per warp
+    using V = AttnVec<E>;
     const int c = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int p = a.pos[b], t0 = c * kAttnChunk;
     if (t0 > p) return;
@@ -411,21 +427,33 @@ static __global__ __launch_bounds__(128) void k_attn_partial(AttnArgs a) {
     __shared__ __align__(16) float q_s[kMaxHG][HD];
     __shared__ float s_s[kMaxHG][kAttnChunk];
     __shared__ __align__(16) float o_s[4][kMaxHG][HD];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float *kbase = a.kc + (size_t)b * a.bstride + (size_t)t0 * kd + (size_t)g * HD + lane * E;
+    const float *vbase = a.vc + (size_t)b * a.bstride + (size_t)t0 * kd + (size_t)g * HD + lane * E;
+    typename V::T kv[TW], vv[TW];
+#pragma unroll
+    for (int i = 0; i < TW; i++) {
+        const int t = warp + 4 * i;
+        if (t < nt) kv[i] = *reinterpret_cast<const typename V::T *>(kbase + (size_t)t * kd);
+    }
+#pragma unroll
+    for (int i = 0; i < TW; i++) {
+        const int t = warp + 4 * i;
+        if (t < nt) vv[i] = *reinterpret_cast<const typename V::T *>(vbase + (size_t)t * kd);
+    }
     const float *qrow = a.qkv + (size_t)b * a.ld + (size_t)g * hg * HD;
     for (int i = threadIdx.x; i < hg * HD; i += blockDim.x) q_s[i / HD][i % HD] = qrow[i];
     __syncthreads();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const float *kbase = a.kc + (size_t)b * a.bstride + (size_t)t0 * kd + (size_t)g * HD;
-    const float *vbase = a.vc + (size_t)b * a.bstride + (size_t)t0 * kd + (size_t)g * HD;
-    for (int t = warp; t < nt; t += 4) {
-        const float *kr = kbase + (size_t)t * kd + lane * E;
-        float kv[E];
 #pragma unroll
-        for (int e = 0; e < E; e++) kv[e] = kr[e];
+    for (int i = 0; i < TW; i++) {
+        const int t = warp + 4 * i;
+        if (t >= nt) break;
+        float k[E];
+        V::get(kv[i], k);
         for (int j = 0; j < hg; j++) {
             float d = 0.f;
 #pragma unroll
-            for (int e = 0; e < E; e++) d = fmaf(q_s[j][lane * E + e], kv[e], d);
+            for (int e = 0; e < E; e++) d = fmaf(q_s[j][lane * E + e], k[e], d);
             d = warp_sum(d);
             if (lane == 0) {
                 float s = __fmul_rn(d, a.scale);
@@ -459,17 +487,18 @@ static __global__ __launch_bounds__(128) void k_attn_partial(AttnArgs a) {
     for (int j = 0; j < kMaxHG; j++)
 #pragma unroll
         for (int e = 0; e < E; e++) o[j][e] = 0.f;
-    for (int t = warp; t < nt; t += 4) {
-        const float *vr = vbase + (size_t)t * kd + lane * E;
-        float vv[E];
 #pragma unroll
-        for (int e = 0; e < E; e++) vv[e] = vr[e];
+    for (int i = 0; i < TW; i++) {
+        const int t = warp + 4 * i;
+        if (t >= nt) break;
+        float v[E];
+        V::get(vv[i], v);
 #pragma unroll
         for (int j = 0; j < kMaxHG; j++) {
             if (j < hg) {
                 float pj = s_s[j][t];
 #pragma unroll
-                for (int e = 0; e < E; e++) o[j][e] = fmaf(pj, vv[e], o[j][e]);
+                for (int e = 0; e < E; e++) o[j][e] = fmaf(pj, v[e], o[j][e]);
             }
         }
     }
@@ -492,7 +521,6 @@ static __global__ __launch_bounds__(128) void k_attn_partial(AttnArgs a) {
     }
 }
 
-// merge chunk partials: o = sum_c o_c e^{m_c-M} / sum_c l_c e^{m_c-M}; grid (H, B), block HD
 static __global__ void k_attn_combine(const float *__restrict__ part, const int *__restrict__ pos, int H, int HD, int nchunk,
                                float *__restrict__ out, int ldo) {
     const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
@@ -798,25 +826,41 @@ static __global__ void k_add_scaled(float *x, const float *y, float s, int n) {
 // ------------------------------------------------------------------------------------
 // Bucket (sequence, election slot) pairs by expert, in ascending sequence order.
 // grid 1, block 512 (warp e = expert slot).  idx[e*B + j] = b; pairrow[b*16+ki] = e*B + j.
+// The elections of up to 512 sequences are first staged in shared memory (one byte per
+// slot, 0xFF past kcnt), so every warp scans them without global-memory round trips.
 static __global__ __launch_bounds__(512) void k_route(const int *__restrict__ kcnt, const int *__restrict__ sel, int B,
                                                int *__restrict__ cnt, int *__restrict__ idx, int *__restrict__ pairrow,
                                                unsigned long long *stats) {
+    static_assert(kMaxE == 16, "one 16-byte row of slots per sequence");
+    __shared__ __align__(16) uint8_t sel_s[512][kMaxE];
     const int e = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int n = 0;
-    for (int b0 = 0; b0 < B; b0 += 32) {
-        int b = b0 + lane, ki = -1;
-        if (b < B) {
-            int k = kcnt[b];
-            for (int i = 0; i < k; i++)
-                if (sel[b * kMaxE + i] == e) ki = i;
+    for (int base = 0; base < B; base += 512) {
+        const int nb = min(512, B - base);
+        __syncthreads();
+        for (int i = threadIdx.x; i < nb * kMaxE; i += 512) {
+            const int b = i / kMaxE, s = i % kMaxE;
+            sel_s[b][s] = s < kcnt[base + b] ? (uint8_t)sel[(size_t)(base + b) * kMaxE + s] : (uint8_t)0xFF;
         }
-        unsigned m = __ballot_sync(JDG_FULL, ki >= 0);
-        if (ki >= 0) {
-            int j = n + __popc(m & ((1u << lane) - 1));
-            idx[e * B + j] = b;
-            pairrow[b * kMaxE + ki] = e * B + j;
+        __syncthreads();
+        for (int b0 = 0; b0 < nb; b0 += 32) {
+            const int bl = b0 + lane;
+            int ki = -1;
+            if (bl < nb) {
+                const uint4 w = *reinterpret_cast<const uint4 *>(sel_s[bl]);
+                const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int i = 0; i < kMaxE; i++)
+                    if (((words[i >> 2] >> (8 * (i & 3))) & 0xFFu) == (uint32_t)e) ki = i;
+            }
+            const unsigned m = __ballot_sync(JDG_FULL, ki >= 0);
+            if (ki >= 0) {
+                const int j = n + __popc(m & ((1u << lane) - 1)), b = base + bl;
+                idx[e * B + j] = b;
+                pairrow[b * kMaxE + ki] = e * B + j;
+            }
+            n += __popc(m);
         }
-        n += __popc(m);
     }
     if (lane == 0) {
         cnt[e] = n;

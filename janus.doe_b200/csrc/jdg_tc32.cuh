@@ -14,13 +14,13 @@
 // core matrix (row group g < 16, K group c < 8) of 8 rows x 4 elements (16 bytes a row) sits
 // at byte (c * 16 + g) * 128 — 16 KB per block and part.  Weights are laid out once at upload
 // ([row tile][K chunk][hi | lo]); activations by a prep kernel before each product
-// ([segment][token tile][K chunk][hi | lo], rows past the segment's count zero).  So a stage
+// ([segment][token tile][K chunk][hi | lo], rows past the segment's count left as they are).  So a stage
 // is four 1-D bulk copies (cp.async.bulk, no tensor maps), and every byte is read once.
 //
-// CTA (192 threads) = one 128-row x 128-token output tile over a K range (split-K CTAs of a
-// tile add their partials in split order in the last CTA, by ticket): thread 0 streams
-// stages into a 3-deep ring; thread 32 issues the 16 MMAs (M128 N128 K8) of each 32-wide
-// chunk into one of two accumulator regions and commits the stage back; warps 2-5 drain each
+// CTA (192 threads) = one 128-row x 128-token output tile over a K range (split-K CTAs write
+// partials that k_tc_reduce adds in split order): thread 0 streams stages into a 3-deep ring;
+// thread 32 issues the 16 MMAs (M128 K8, N = the tile's token count rounded up to 32) of each
+// 32-wide chunk into one of four accumulator regions and commits the stage back; warps 2-5 drain each
 // chunk's region into f32 registers with round-to-nearest adds (the tensor core's own
 // accumulation then spans only one chunk, 128 products) and apply the epilogue.  Every wait is bounded by wall time; on a timeout the CTA flags
 // JDG_ERR_TIMEOUT, waits (bounded) for what it issued, frees its tensor memory and returns.
@@ -39,10 +39,11 @@ constexpr int kTcStageBytes = 4 * kTcBlk;      // W hi, W lo, X hi, X lo
 constexpr int kTcSmem = 1024 + kTcStages * kTcStageBytes;
 constexpr int kTcMaxSplit = 8;
 constexpr int kTcThreads = 192;                // warp 0 copies, warp 1 MMAs, warps 2-5 drain
+constexpr int kTcRegions = 4;                  // accumulator regions of 128 TMEM columns
 // kind::tf32 instruction descriptor: D f32 (bits 4-5 = 1), A and B TF32 (bits 7-9, 10-12 = 2),
-// both K-major, N = 128 (bits 17-22 = N/8), M = 128 (bits 24-28 = M/16)
-constexpr uint32_t kTcIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(kTcTok >> 3) << 17) |
-                              ((uint32_t)(kTcRows >> 4) << 24);
+// both K-major, M = 128 (bits 24-28 = M/16); N (bits 17-22 = N/8) is set per tile
+constexpr uint32_t kTcIdescM = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(kTcRows >> 4) << 24);
+__host__ __device__ __forceinline__ uint32_t tc_idesc(int n) { return kTcIdescM | ((uint32_t)(n >> 3) << 17); }
 
 // byte offset of element (row r, k) inside a 128 x 32 block
 __host__ __device__ __forceinline__ uint32_t tc_off(int r, int k) {
@@ -75,7 +76,8 @@ static __global__ void k_tc_wprep(const float *__restrict__ W, int N, int K, uin
 }
 
 // Activation blocks: segment s, token j of the segment is row idx[s*ldi + j] of X (idx null:
-// row j, segment 0), j < cnt[s] (cnt null: M); tokens past the count are zeros.
+// row j, segment 0), j < cnt[s] (cnt null: M).  Rows past the count are not written: they
+// only reach output columns (tokens) that are never stored.
 // out: [seg][token tile < ttiles][K chunk][hi | lo][16 KB]
 struct TcPrep {
     const float *X;
@@ -96,11 +98,9 @@ static __global__ void k_tc_xprep(TcPrep p) {
         const long rem = i % per_seg;
         const int j = (int)(rem / (p.K / 4)), k4 = (int)(rem % (p.K / 4)) * 4;
         const int n = p.cnt ? p.cnt[s] : p.M;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (j < n) {
-            const int row = p.idx ? p.idx[(size_t)s * p.ldi + j] : j;
-            v = *reinterpret_cast<const float4 *>(p.X + (size_t)s * p.x_seg + (size_t)row * p.ldx + k4);
-        }
+        if (j >= n) continue;
+        const int row = p.idx ? p.idx[(size_t)s * p.ldi + j] : j;
+        const float4 v = *reinterpret_cast<const float4 *>(p.X + (size_t)s * p.x_seg + (size_t)row * p.ldx + k4);
         float4 h, l;
         tc_split(v.x, h.x, l.x);
         tc_split(v.y, h.y, l.y);
@@ -124,8 +124,7 @@ struct TcArgs {
     int epi;                   // EPI_STORE, EPI_ADD (C += alpha * Y), EPI_SWIGLU (C[t][n/2] = silu(Y[2i]) * Y[2i+1])
     float alpha;
     int ksplit;
-    float *part;               // [tiles][ksplit][128 tokens][128 rows]
-    unsigned *tickets;         // one per tile (returned to zero by the last CTA)
+    float *part;               // [tiles][ksplit][128 tokens][128 rows], tile = (seg * ttiles + tt) * rtiles + rt
     int *err;
 };
 
@@ -134,11 +133,11 @@ __device__ __forceinline__ uint64_t tc_desc(uint32_t saddr) {
     return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((2048u >> 4) & 0x3FFF) << 16) |
            ((uint64_t)((128u >> 4) & 0x3FFF) << 32) | (1ull << 46);
 }
-__device__ __forceinline__ void tc_mma(uint32_t dtmem, uint64_t da, uint64_t db, uint32_t acc) {
+__device__ __forceinline__ void tc_mma(uint32_t dtmem, uint64_t da, uint64_t db, uint32_t acc, uint32_t idesc) {
     asm volatile(
         "{ .reg .pred p; setp.ne.b32 p, %3, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %4, p; }" ::"r"(dtmem),
-        "l"(da), "l"(db), "r"(acc), "r"(kTcIdesc));
+        "l"(da), "l"(db), "r"(acc), "r"(idesc));
 }
 __device__ __forceinline__ unsigned long long tc_now() {
     unsigned long long t;
@@ -194,9 +193,9 @@ __device__ __forceinline__ void tc_store(const TcArgs &a, int seg, int t, int n,
 static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
     extern __shared__ __align__(1024) uint8_t tc_sm[];
     uint8_t *stages = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tc_sm) + 1023) & ~(uintptr_t)1023);
-    __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], ready[2], freed[2];
+    __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], ready[kTcRegions], freed[kTcRegions];
     __shared__ uint32_t tmem_slot;
-    __shared__ int abort_flag, s_last;
+    __shared__ int abort_flag;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rt = blockIdx.x, tt = blockIdx.y, seg = blockIdx.z / a.ksplit, ks = blockIdx.z % a.ksplit;
     const int n_tok_seg = a.cnt ? a.cnt[seg] : a.M;
@@ -210,7 +209,7 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        for (int q = 0; q < 2; q++) {
+        for (int q = 0; q < kTcRegions; q++) {
             mbar_init(&ready[q], 1);
             mbar_init(&freed[q], 4);  // the four drain warps
         }
@@ -219,7 +218,7 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
-                     "r"(2 * kTcTok));
+                     "r"(kTcRegions * kTcTok));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -246,11 +245,14 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
             issued_ld = i + 1;
         }
     } else if (tid == 32) {
-        // ---------------- MMA issuer: chunk i into accumulator region i % 2 ----------------
+        // ---------------- MMA issuer: chunk i into accumulator region i % kTcRegions ----------------
+        // token columns past ntok are not computed beyond the next multiple of 32; the drain
+        // reads whole groups of 32 columns and stores only those below ntok
+        const uint32_t idesc = tc_idesc(min(kTcTok, (ntok + 31) & ~31));
         for (int i = 0; i < nloc; i++) {
-            const int s = i % kTcStages, q = i & 1;
+            const int s = i % kTcStages, q = i % kTcRegions;
             bool ok = tc_wait(&full[s], (uint32_t)(i / kTcStages) & 1u);
-            if (ok && i >= 2) ok = tc_wait(&freed[q], (uint32_t)((i >> 1) - 1) & 1u);
+            if (ok && i >= kTcRegions) ok = tc_wait(&freed[q], (uint32_t)((i / kTcRegions) - 1) & 1u);
             if (!ok || *(volatile int *)&abort_flag) {
                 abort_flag = 1;
                 break;
@@ -262,10 +264,10 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
 #pragma unroll
             for (int k8 = 0; k8 < kTcK / 8; k8++) {  // K slices of 8: two K groups of the block
                 const uint32_t o = (uint32_t)k8 * 2 * 2048;
-                tc_mma(d, tc_desc(wh + o), tc_desc(xh + o), k8 > 0 ? 1u : 0u);
-                tc_mma(d, tc_desc(wh + o), tc_desc(xl + o), 1u);
-                tc_mma(d, tc_desc(wl + o), tc_desc(xh + o), 1u);
-                tc_mma(d, tc_desc(wl + o), tc_desc(xl + o), 1u);
+                tc_mma(d, tc_desc(wh + o), tc_desc(xh + o), k8 > 0 ? 1u : 0u, idesc);
+                tc_mma(d, tc_desc(wh + o), tc_desc(xl + o), 1u, idesc);
+                tc_mma(d, tc_desc(wl + o), tc_desc(xh + o), 1u, idesc);
+                tc_mma(d, tc_desc(wl + o), tc_desc(xl + o), 1u, idesc);
             }
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                              smem_u32(&empty[s]))
@@ -286,8 +288,8 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
         for (int c = 0; c < kTcTok; c++) acc[c] = 0.f;
         bool ok = true;
         for (int i = 0; i < nloc; i++) {
-            const int q = i & 1;
-            if (!tc_wait(&ready[q], (uint32_t)(i >> 1) & 1u)) ok = false;
+            const int q = i % kTcRegions;
+            if (!tc_wait(&ready[q], (uint32_t)(i / kTcRegions) & 1u)) ok = false;
             if (__any_sync(JDG_FULL, !ok || *(volatile int *)&abort_flag)) {  // leave as a whole warp
                 ok = false;
                 break;
@@ -296,6 +298,7 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
             const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(q * kTcTok);
 #pragma unroll
             for (int c0 = 0; c0 < kTcTok; c0 += 32) {
+                if (c0 >= ntok) break;  // columns past the tile's tokens hold zeros (uniform)
                 float v[32];
                 tc_ld8_nw(base + (uint32_t)c0, v);
                 tc_ld8_nw(base + (uint32_t)c0 + 8, v + 8);
@@ -325,29 +328,6 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
         }
     }
     __syncthreads();
-    if (a.ksplit > 1 && !abort_flag && nloc > 0) {
-        // the last CTA of this tile adds the partials in split order
-        const size_t tile = ((size_t)seg * gridDim.y + tt) * gridDim.x + rt;
-        if (tid == 0) {
-            __threadfence();
-            const unsigned tk = atomicAdd(a.tickets + tile, 1u);
-            s_last = tk == (unsigned)a.ksplit - 1;
-            if (s_last) {
-                __threadfence();
-                a.tickets[tile] = 0;
-            }
-        }
-        __syncthreads();
-        if (s_last && warp >= 2) {
-            const int row = (warp & 3) * 32 + lane, n = rt * kTcRows + row;
-            const float *p0 = a.part + tile * a.ksplit * (size_t)kTcTok * kTcRows;
-            for (int t = 0; t < ntok; t++) {
-                float acc = 0.f;
-                for (int z = 0; z < a.ksplit; z++) acc = __fadd_rn(acc, __ldcg(p0 + ((size_t)z * kTcTok + t) * kTcRows + row));
-                tc_store(a, seg, tt * kTcTok + t, n, acc, lane);
-            }
-        }
-    }
     if (abort_flag) {
         if (tid == 0) atomicOr(a.err, JDG_ERR_TIMEOUT);
         // let the issued copies and MMAs land before the memory goes away
@@ -360,7 +340,46 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
     __syncthreads();
     if (warp == 0) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kTcTok));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcRegions * kTcTok));
+    }
+}
+
+// Split-K sum: out[t][n] = sum over z = 0..ksplit-1 (in that order) of the partials, then the
+// epilogue.  One thread per (tile, token, 4 consecutive rows), grid-stride.
+static __global__ __launch_bounds__(256) void k_tc_reduce(TcArgs a, int rtiles, int nseg) {
+    const long total = (long)nseg * a.ttiles * rtiles * kTcTok * (kTcRows / 4);
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const int r4 = (int)(i % (kTcRows / 4)) * 4;
+        const int c = (int)((i / (kTcRows / 4)) % kTcTok);
+        const long tile = i / ((long)(kTcRows / 4) * kTcTok);
+        const int rt = (int)(tile % rtiles), tt = (int)((tile / rtiles) % a.ttiles), seg = (int)(tile / ((long)rtiles * a.ttiles));
+        const int n_tok_seg = a.cnt ? a.cnt[seg] : a.M;
+        if (!a.wt[seg] || c >= n_tok_seg - tt * kTcTok) continue;
+        const int n = rt * kTcRows + r4;
+        if (n >= a.n_rows) continue;
+        const float *p = a.part + (size_t)tile * a.ksplit * kTcTok * kTcRows + (size_t)c * kTcRows + r4;
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int z = 0; z < a.ksplit; z++) {
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(p + (size_t)z * kTcTok * kTcRows));
+            s.x = __fadd_rn(s.x, v.x);
+            s.y = __fadd_rn(s.y, v.y);
+            s.z = __fadd_rn(s.z, v.z);
+            s.w = __fadd_rn(s.w, v.w);
+        }
+        float *out = a.C + (size_t)seg * a.c_seg + (size_t)(tt * kTcTok + c) * a.ldc;
+        const float v[4] = {s.x, s.y, s.z, s.w};
+        if (a.epi == EPI_SWIGLU) {
+#pragma unroll
+            for (int j = 0; j < 4; j += 2)
+                if (n + j + 1 < a.n_rows) out[(n + j) >> 1] = __fmul_rn(silu_ref(v[j]), v[j + 1]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                if (n + j >= a.n_rows) break;
+                if (a.epi == EPI_ADD) out[n + j] = __fadd_rn(out[n + j], __fmul_rn(v[j], a.alpha));
+                else out[n + j] = v[j];
+            }
+        }
     }
 }
 
