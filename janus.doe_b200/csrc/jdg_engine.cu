@@ -239,7 +239,7 @@ int jdg_own_upload_impl(jdg_engine *e, const jd_model *m, int max_batch) {
     e->qkvd = e->qd + 2 * e->kd;
     e->eps = c.norm_eps;
     e->clamp = c.attn_clamp;
-    e->nchunk = (e->max_seq + kAttnChunk - 1) / kAttnChunk;
+    if (jdg_attn_setup(e) != JD_OK) return JD_ECUDA;
     const int D = e->D, H = e->hidden, L = e->L, V = e->V;
     // weight arena
     size_t bytes = al256((size_t)V * D * 4) * 2 + al256(D * 4);
@@ -553,11 +553,40 @@ static void launch_attention(jdg_engine *e, int l, int B, float scale, float bia
     a.clamp = e->clamp;
     a.inv_clamp = e->clamp > 0 ? 1.0f / e->clamp : 0.f;
     a.part = e->part;
-    dim3 grid(e->nchunk, e->KVH, B);
-    if (e->HD == 64) k_attn_partial<64><<<grid, 128, 0, e->st>>>(a);
-    else k_attn_partial<128><<<grid, 128, 0, e->st>>>(a);
-    k_attn_combine<<<dim3(e->Hh, B), e->HD, 0, e->st>>>(e->part, e->pos, e->Hh, e->HD, e->nchunk, e->att, e->qd);
+    int chunk = kAttnChunk;
+    if (e->attn_rows) {
+        chunk = kAttnRowsChunk;
+        dim3 grid((e->max_seq + chunk - 1) / chunk, B);
+        const size_t sm = attn_rows_smem(e->Hh, e->HD, e->kd);
+        if (e->HD == 64) k_attn_rows<64><<<grid, e->Hh * 32, sm, e->st>>>(a);
+        else k_attn_rows<128><<<grid, e->Hh * 32, sm, e->st>>>(a);
+    } else {
+        dim3 grid((e->max_seq + chunk - 1) / chunk, e->KVH, B);
+        if (e->HD == 64) k_attn_partial<64><<<grid, 128, 0, e->st>>>(a);
+        else k_attn_partial<128><<<grid, 128, 0, e->st>>>(a);
+    }
+    k_attn_combine<<<dim3(e->Hh, B), e->HD, 0, e->st>>>(e->part, e->pos, e->Hh, e->HD, e->nchunk, chunk, e->att,
+                                                      e->qd);
     e->launches += 2;
+}
+
+// Pick the attention kernel for this engine's shapes (at upload, outside any capture):
+// k_attn_rows when a chunk's key and value rows fit shared memory and the heads fit one CTA.
+int jdg_attn_setup(jdg_engine *e) {
+    const size_t sm = attn_rows_smem(e->Hh, e->HD, e->kd);
+    e->attn_rows = (e->HD == 64 || e->HD == 128) && e->Hh <= 32 && e->Hh % e->KVH == 0 && sm <= 160 * 1024;
+    if (e->attn_rows) {
+        cudaError_t r = e->HD == 64
+                            ? cudaFuncSetAttribute(k_attn_rows<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)
+                            : cudaFuncSetAttribute(k_attn_rows<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        if (r != cudaSuccess) {
+            jdg_set_err(e->ctx, "attention smem attribute: %s", cudaGetErrorString(r));
+            return JD_ECUDA;
+        }
+    }
+    // partial buffers are laid out for the smaller chunk
+    e->nchunk = (e->max_seq + kAttnRowsChunk - 1) / kAttnRowsChunk;
+    return JD_OK;
 }
 
 void jdg_launch_rope(jdg_engine *e, int l, int B) {

@@ -43,6 +43,7 @@ struct jdg_engine {
     // shapes
     int B_max = 0, L = 0, D = 0, Hh = 0, KVH = 0, HD = 0, hidden = 0, V = 0, max_seq = 0;
     int qd = 0, kd = 0, qkvd = 0, nchunk = 0, kmax = 1;
+    int attn_rows = 0;                   // 1: k_attn_rows (32-position chunks), 0: k_attn_partial
     int ldl = 0;  // logits row stride (the rank's vocab slice under tensor parallelism)
     float eps = 1e-5f, clamp = 0.f;
     int rope_norm = 0;
@@ -122,6 +123,7 @@ int jdg_alloc_state(jdg_engine *e);
 int jdg_own_upload_impl(jdg_engine *e, const jd_model *m, int max_batch);
 void jdg_launch_rope(jdg_engine *e, int l, int B);
 void jdg_launch_attention(jdg_engine *e, int l, int B, float scale, float bias);
+int jdg_attn_setup(jdg_engine *e);
 void jdg_launch_pick(jdg_engine *e, int B);
 void jdg_launch_pick_tp(jdg_engine *e, int B, const float *v, const int *ix, int world);
 int jdg_engine_create(jdg_ctx *ctx, int kind, jdg_engine **out);

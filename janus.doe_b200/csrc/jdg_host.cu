@@ -355,7 +355,7 @@ static int host_upload_impl(jdg_engine *e, const jd_host_model *h, int max_batch
     e->eps = h->rms_eps;
     e->clamp = 0.f;
     e->rope_norm = h->rope_norm;
-    e->nchunk = (max_seq + kAttnChunk - 1) / kAttnChunk;
+    if (jdg_attn_setup(e) != JD_OK) return JD_ECUDA;
     e->lora_rank = h->lora_rank;
     e->lora_alpha = h->lora_alpha;
     const int R = h->lora_rank;

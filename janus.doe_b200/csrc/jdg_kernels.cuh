@@ -3,12 +3,14 @@
 // RoPE + KV append, split-K decode attention, the parliament election, routing, expert
 // combine, and next-token selection.  Every kernel cites the reference lines it replaces.
 #pragma once
+#include "jdg_async.cuh"
 #include "jdg_common.cuh"
 
 namespace jdg {
 
 constexpr int kMaxE = 16;
-constexpr int kAttnChunk = 64;  // positions per attention CTA
+constexpr int kAttnChunk = 64;  // positions per attention CTA (k_attn_partial)
+constexpr int kAttnRowsChunk = 32;  // positions per attention CTA (k_attn_rows)
 constexpr int kMaxHG = 8;       // query heads per KV head supported by the attention kernel
 
 // ------------------------------------------------------------------------------------
@@ -521,10 +523,89 @@ static __global__ __launch_bounds__(128) void k_attn_partial(AttnArgs a) {
     }
 }
 
+// Decode attention, one CTA per (chunk of 32 positions, row) over every head: the chunk's
+// key and value rows (all KV heads, contiguous in the cache) are copied to shared memory with
+// 16-byte cp.async (rows padded by 4 floats so that lanes reading different rows hit
+// different banks), then warp h scores its query head against position t = lane (one
+// sequential fmaf chain over the head dimension), takes the chunk's max and sum in the warp,
+// and lane d accumulates sum_t p_t v_t[d] in position order.  Same (o, max, sum) partials as
+// k_attn_partial.  Block = H * 32 threads; dynamic shared memory attn_rows_smem().
+__host__ __device__ inline size_t attn_rows_smem(int H, int HD, int kd) {
+    return ((size_t)2 * kAttnRowsChunk * (kd + 4) + (size_t)H * HD + (size_t)H * kAttnRowsChunk) * 4;
+}
+template <int HD>
+static __global__ __launch_bounds__(1024) void k_attn_rows(AttnArgs a) {
+    constexpr int E = HD / 32;
+    extern __shared__ __align__(16) float ar_sm[];
+    const int c = blockIdx.x, b = blockIdx.y;
+    const int p = a.pos[b], t0 = c * kAttnRowsChunk;
+    if (t0 > p) return;
+    const int nt = min(kAttnRowsChunk, p + 1 - t0);
+    const int kd = a.KVH * HD, ks = kd + 4;
+    float *k_s = ar_sm, *v_s = k_s + (size_t)kAttnRowsChunk * ks, *q_s = v_s + (size_t)kAttnRowsChunk * ks;
+    float *p_s = q_s + a.H * HD;
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    {
+        const float *ksrc = a.kc + (size_t)b * a.bstride + (size_t)t0 * kd;
+        const float *vsrc = a.vc + (size_t)b * a.bstride + (size_t)t0 * kd;
+        const int q4 = kd / 4, n4 = nt * q4;
+        for (int i = tid; i < n4; i += nthr) {
+            const int t = i / q4, d = (i % q4) * 4;
+            const uint32_t dk = smem_u32(k_s + t * ks + d), dv = smem_u32(v_s + t * ks + d);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dk), "l"(ksrc + (size_t)t * kd + d) : "memory");
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dv), "l"(vsrc + (size_t)t * kd + d) : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        const float *qrow = a.qkv + (size_t)b * a.ld;
+        for (int i = tid; i < a.H * HD; i += nthr) q_s[i] = qrow[i];
+        asm volatile("cp.async.wait_all;" ::: "memory");
+    }
+    __syncthreads();
+    const int h = tid >> 5, lane = tid & 31, g = h / a.hg;
+    float s = -INFINITY;
+    if (lane < nt) {
+        const float *kr = k_s + lane * ks + g * HD, *qh = q_s + h * HD;
+        float d = 0.f;
+#pragma unroll
+        for (int i = 0; i < HD; i += 4) {
+            const float4 kv = *reinterpret_cast<const float4 *>(kr + i);
+            const float4 qv = *reinterpret_cast<const float4 *>(qh + i);
+            d = fmaf(qv.x, kv.x, d);
+            d = fmaf(qv.y, kv.y, d);
+            d = fmaf(qv.z, kv.z, d);
+            d = fmaf(qv.w, kv.w, d);
+        }
+        s = __fmul_rn(d, a.scale);
+        if (a.bias != 1.0f) s = __fmul_rn(s, a.bias);
+        if (a.clamp > 0.f) s = __fmul_rn(a.clamp, tanhf(__fmul_rn(s, a.inv_clamp)));
+    }
+    const float m = warp_max(s);
+    const float ex = lane < nt ? expf(s - m) : 0.f;
+    const float l = warp_sum(ex);
+    p_s[h * kAttnRowsChunk + lane] = ex;
+    __syncwarp();
+    float o[E];
+#pragma unroll
+    for (int e = 0; e < E; e++) o[e] = 0.f;
+    const float *vcol = v_s + g * HD + lane * E;
+    for (int t = 0; t < nt; t++) {
+        const float pt = p_s[h * kAttnRowsChunk + t];
+#pragma unroll
+        for (int e = 0; e < E; e++) o[e] = fmaf(pt, vcol[(size_t)t * ks + e], o[e]);
+    }
+    float *dst = a.part + (((size_t)b * a.H + h) * a.nchunk + c) * (HD + 2);
+#pragma unroll
+    for (int e = 0; e < E; e++) dst[lane * E + e] = o[e];
+    if (lane == 0) {
+        dst[HD] = m;
+        dst[HD + 1] = l;
+    }
+}
+
 static __global__ void k_attn_combine(const float *__restrict__ part, const int *__restrict__ pos, int H, int HD, int nchunk,
-                               float *__restrict__ out, int ldo) {
+                               int chunk, float *__restrict__ out, int ldo) {
     const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
-    const int nc = pos[b] / kAttnChunk + 1;
+    const int nc = pos[b] / chunk + 1;
     const float *pp = part + ((size_t)b * H + h) * nchunk * (HD + 2);
     float M = -INFINITY;
     for (int c = 0; c < nc; c++) M = fmaxf(M, pp[c * (HD + 2) + HD]);
