@@ -17,10 +17,10 @@
 // ([segment][token tile][K chunk][hi | lo], rows past the segment's count left as they are).  So a stage
 // is four 1-D bulk copies (cp.async.bulk, no tensor maps), and every byte is read once.
 //
-// CTA (192 threads) = one 128-row x 128-token output tile over a K range (split-K CTAs write
+// CTA (320 threads) = one 128-row x 128-token output tile over a K range (split-K CTAs write
 // partials that k_tc_reduce adds in split order): thread 0 streams stages into a 3-deep ring;
 // thread 32 issues the 16 MMAs (M128 K8, N = the tile's token count rounded up to 32) of each
-// 32-wide chunk into one of four accumulator regions and commits the stage back; warps 2-5 drain each
+// 32-wide chunk into one of four accumulator regions and commits the stage back; warps 2-9 drain each
 // chunk's region into f32 registers with round-to-nearest adds (the tensor core's own
 // accumulation then spans only one chunk, 128 products) and apply the epilogue.  Every wait is bounded by wall time; on a timeout the CTA flags
 // JDG_ERR_TIMEOUT, waits (bounded) for what it issued, frees its tensor memory and returns.
@@ -38,7 +38,8 @@ constexpr int kTcStages = 3;
 constexpr int kTcStageBytes = 4 * kTcBlk;      // W hi, W lo, X hi, X lo
 constexpr int kTcSmem = 1024 + kTcStages * kTcStageBytes;
 constexpr int kTcMaxSplit = 8;
-constexpr int kTcThreads = 192;                // warp 0 copies, warp 1 MMAs, warps 2-5 drain
+constexpr int kTcThreads = 320;                // warp 0 copies, warp 1 MMAs, warps 2-9 drain
+constexpr int kTcDrainCols = 64;               // token columns per drain warp (two warps per TMEM lane quarter)
 constexpr int kTcRegions = 4;                  // accumulator regions of 128 TMEM columns
 // kind::tf32 instruction descriptor: D f32 (bits 4-5 = 1), A and B TF32 (bits 7-9, 10-12 = 2),
 // both K-major, M = 128 (bits 24-28 = M/16); N (bits 17-22 = N/8) is set per tile
@@ -211,7 +212,7 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
         }
         for (int q = 0; q < kTcRegions; q++) {
             mbar_init(&ready[q], 1);
-            mbar_init(&freed[q], 4);  // the four drain warps
+            mbar_init(&freed[q], 8);  // the eight drain warps
         }
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -281,11 +282,13 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
     __syncwarp();
     if (warp >= 2) {
         // ---------------- drain: every chunk's product added in f32 (round to nearest) ----------------
-        // warp w reads TMEM lanes 32 (w % 4) .. : its weight rows
+        // warp w reads TMEM lanes 32 (w % 4) .. (its weight rows), token columns
+        // col0 .. col0 + 63: all eight 8-column loads in flight before one wait
         const int quarter = warp & 3, row = quarter * 32 + lane, n = rt * kTcRows + row;
-        float acc[kTcTok];
+        const int col0 = ((warp - 2) >> 2) * kTcDrainCols, ncol = min(kTcDrainCols, ntok - col0);
+        float acc[kTcDrainCols];
 #pragma unroll
-        for (int c = 0; c < kTcTok; c++) acc[c] = 0.f;
+        for (int c = 0; c < kTcDrainCols; c++) acc[c] = 0.f;
         bool ok = true;
         for (int i = 0; i < nloc; i++) {
             const int q = i % kTcRegions;
@@ -295,18 +298,21 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
                 break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(q * kTcTok);
+            const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(q * kTcTok + col0);
+            if (ncol > 32) {  // uniform per warp; columns past ntok (up to the MMA's N) are not stored
+                float v[64];
 #pragma unroll
-            for (int c0 = 0; c0 < kTcTok; c0 += 32) {
-                if (c0 >= ntok) break;  // columns past the tile's tokens hold zeros (uniform)
-                float v[32];
-                tc_ld8_nw(base + (uint32_t)c0, v);
-                tc_ld8_nw(base + (uint32_t)c0 + 8, v + 8);
-                tc_ld8_nw(base + (uint32_t)c0 + 16, v + 16);
-                tc_ld8_nw(base + (uint32_t)c0 + 24, v + 24);
+                for (int j = 0; j < 64; j += 8) tc_ld8_nw(base + (uint32_t)j, v + j);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-                for (int j = 0; j < 32; j++) acc[c0 + j] = __fadd_rn(acc[c0 + j], v[j]);
+                for (int j = 0; j < 64; j++) acc[j] = __fadd_rn(acc[j], v[j]);
+            } else if (ncol > 0) {
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; j += 8) tc_ld8_nw(base + (uint32_t)j, v + j);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                for (int j = 0; j < 32; j++) acc[j] = __fadd_rn(acc[j], v[j]);
             }
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
@@ -316,14 +322,14 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
         if (ok && nloc > 0) {
             if (a.ksplit == 1) {
 #pragma unroll
-                for (int c = 0; c < kTcTok; c++)
-                    if (c < ntok) tc_store(a, seg, tt * kTcTok + c, n, acc[c], lane);
+                for (int c = 0; c < kTcDrainCols; c++)
+                    if (c < ncol) tc_store(a, seg, tt * kTcTok + col0 + c, n, acc[c], lane);
             } else {
                 const size_t tile = ((size_t)seg * gridDim.y + tt) * gridDim.x + rt;
                 float *pp = a.part + (tile * a.ksplit + ks) * (size_t)kTcTok * kTcRows;
 #pragma unroll
-                for (int c = 0; c < kTcTok; c++)
-                    if (c < ntok) pp[(size_t)c * kTcRows + row] = acc[c];
+                for (int c = 0; c < kTcDrainCols; c++)
+                    if (c < ncol) pp[(size_t)(col0 + c) * kTcRows + row] = acc[c];
             }
         }
     }
