@@ -388,10 +388,10 @@ int jdg_own_upload_impl(jdg_engine *e, const jd_model *m, int max_batch) {
     }
     e->b1_ok = D % 128 == 0 && H % 128 == 0 && D / 128 <= 8 && H / 128 <= 12 && e->qd == D && D <= 1024 &&
                (e->HD == 64 || e->HD == 128) && D / 4 + 64 <= 1024 && e->max_seq <= 1024;
-    DALLOC(e->hbuf, (size_t)B * kMaxE * H * 4);
+    DALLOC(e->hbuf, (size_t)B * kMaxE * 2 * H * 4);  // batched tensor-core step: [slot][B][2H]
     DALLOC(e->ybuf, (size_t)B * kMaxE * D * 4);
     CK(cudaMemset(e->ybuf, 0, (size_t)B * kMaxE * D * 4));
-    CK(cudaMemset(e->hbuf, 0, (size_t)B * kMaxE * H * 4));
+    CK(cudaMemset(e->hbuf, 0, (size_t)B * kMaxE * 2 * H * 4));
     DALLOC(e->logits, (size_t)B * V * 4);
     // KV cache [B][L][S][kd]
     e->kv_bstride = (long)L * e->max_seq * e->kd;
@@ -429,6 +429,11 @@ static int tc_build(jdg_engine *e, const jd_model *m) {
     const char *g = getenv("JDG_SIMT_GEMM");
     if ((g && g[0] == '1') || e->D % kTcK || e->hidden % kTcK || e->qd % kTcK) return JD_OK;
     const int D = e->D, H = e->hidden, L = e->L;
+    {  // the activation prep indexes segments x token tiles x 128 x K/4 in 32 bits
+        const uint64_t rows = (uint64_t)std::max(e->B_max, e->max_seq) + kTcTok;
+        const uint64_t kq = (uint64_t)std::max(std::max(D, H), e->qd) / 4;
+        if ((uint64_t)kMaxE * rows * kq >= (1ull << 32)) return JD_OK;
+    }
     std::vector<const float *> gu_h((size_t)L * kMaxE), dn_h((size_t)L * kMaxE);
     CK(cudaMemcpy(gu_h.data(), e->gu_tab, gu_h.size() * sizeof(void *), cudaMemcpyDeviceToHost));
     CK(cudaMemcpy(dn_h.data(), e->dn_tab, dn_h.size() * sizeof(void *), cudaMemcpyDeviceToHost));
@@ -475,11 +480,11 @@ static int tc_build(jdg_engine *e, const jd_model *m) {
 // when idx is given, counts cnt[s] or M), W as per-segment block tables `wt` (n_rows x K).
 static void launch_tc(jdg_engine *e, const uint8_t *const *wt, int nseg, const float *X, long x_seg, int ldx,
                       const int *idx, int ldi, const int *cnt, int M, int max_rows, int n_rows, int K, float *C,
-                      int ldc, long c_seg, int epi, float alpha) {
+                      int ldc, long c_seg, int epi, float alpha, int x_glu = 0) {
     const int ttiles = (max_rows + kTcTok - 1) / kTcTok, nkc = K / kTcK;
     TcPrep p = {};
     p.X = X; p.x_seg = x_seg; p.ldx = ldx; p.K = K; p.idx = idx; p.ldi = ldi; p.cnt = cnt; p.M = M;
-    p.nseg = nseg; p.ttiles = ttiles; p.out = e->tc_xt;
+    p.nseg = nseg; p.ttiles = ttiles; p.glu = x_glu; p.out = e->tc_xt;
     k_tc_xprep<<<1184, 256, 0, e->st>>>(p);
     const int rtiles = (n_rows + kTcRows - 1) / kTcRows;
     // split K until about one CTA per SM (every split keeps at least one chunk)
@@ -493,6 +498,8 @@ static void launch_tc(jdg_engine *e, const uint8_t *const *wt, int nseg, const f
     a.wt = wt; a.xt = e->tc_xt; a.cnt = cnt; a.M = M; a.n_rows = n_rows; a.nkc = nkc; a.ttiles = ttiles;
     a.C = C; a.ldc = ldc; a.c_seg = c_seg; a.epi = epi; a.alpha = alpha; a.ksplit = ks; a.part = e->tc_part;
     a.err = e->err;
+    a.tl = e->timeline;  // debug wait profile: 0 q/k/v, 1 Wo, 2 gate/up, 3 down, 4 LM head
+    a.tl_type = nseg > 1 ? (x_glu ? 3 : 2) : epi == EPI_ADD ? 1 : n_rows == e->V ? 4 : 0;
     k_tc32_gemm<<<dim3(rtiles, ttiles, nseg * ks), kTcThreads, kTcSmem, e->st>>>(a);
     e->launches += 2;
     if (ks > 1) {
@@ -968,11 +975,13 @@ static void own_batch_layers(jdg_engine *e, int B, int prefill_slot) {
         } else {
             k_route<<<1, 512, 0, e->st>>>(e->kcnt, e->sel, B, e->rcnt, e->ridx, e->pairrow, e->stats);
             if (e->tc_ok) {
-                // segments = expert slots: gate/up of the routed rows of xb (gathered), then down
-                launch_tc(e, ly.tc_gu, kMaxE, e->xb, 0, D, e->ridx, B, e->rcnt, 0, B, 2 * H, D, e->hbuf, H,
-                          (long)B * H, EPI_SWIGLU, 1.f);
-                launch_tc(e, ly.tc_dn, kMaxE, e->hbuf, (long)B * H, H, nullptr, 0, e->rcnt, 0, B, D, H, e->ybuf, D,
-                          (long)B * D, EPI_STORE, 1.f);
+                // segments = expert slots: gate/up of the routed rows of xb (gathered) stored as
+                // interleaved (gate, up) rows [slot][B][2H]; down's activation prep applies
+                // silu(gate) * up while it splits the operand
+                launch_tc(e, ly.tc_gu, kMaxE, e->xb, 0, D, e->ridx, B, e->rcnt, 0, B, 2 * H, D, e->hbuf, 2 * H,
+                          (long)B * 2 * H, EPI_STORE, 1.f);
+                launch_tc(e, ly.tc_dn, kMaxE, e->hbuf, (long)B * 2 * H, 2 * H, nullptr, 0, e->rcnt, 0, B, D, H, e->ybuf,
+                          D, (long)B * D, EPI_STORE, 1.f, 1);
             } else {
                 SgemmArgs a = {};
                 a.A = e->xb; a.lda = D; a.idx = e->ridx; a.ldi = B; a.cnt = e->rcnt; a.Wtab = gu; a.N = 2 * H; a.K = D;
@@ -1157,7 +1166,7 @@ static int pf_alloc(jdg_engine *e) {
     DALLOC(e->pf_qkv, P * e->qkvd * 4);
     DALLOC(e->pf_att, P * e->qd * 4);
     DALLOC(e->pf_part, P * e->Hh * e->nchunk * (e->HD + 2) * 4);
-    DALLOC(e->pf_hbuf, (size_t)kMaxE * P * H * 4);
+    DALLOC(e->pf_hbuf, (size_t)kMaxE * P * 2 * H * 4);
     DALLOC(e->pf_ybuf, (size_t)kMaxE * P * D * 4);
     DALLOC(e->pf_kcnt, P * 4);
     DALLOC(e->pf_sel, P * kMaxE * 4);
@@ -1175,7 +1184,7 @@ static int pf_alloc(jdg_engine *e) {
     std::vector<int> iota(P);
     for (size_t i = 0; i < P; i++) iota[i] = (int)i;
     CK(cudaMemcpy(e->pf_pos, iota.data(), P * 4, cudaMemcpyHostToDevice));
-    CK(cudaMemset(e->pf_hbuf, 0, (size_t)kMaxE * P * H * 4));
+    CK(cudaMemset(e->pf_hbuf, 0, (size_t)kMaxE * P * 2 * H * 4));
     CK(cudaMemset(e->pf_ybuf, 0, (size_t)kMaxE * P * D * 4));
     return JD_OK;
 }

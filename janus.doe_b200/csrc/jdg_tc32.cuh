@@ -88,20 +88,30 @@ struct TcPrep {
     int ldi;
     const int *cnt;
     int M, nseg, ttiles;
+    int glu;  // 1: X rows hold interleaved (gate, up) pairs, 2K floats; the product reads silu(gate) * up
     uint8_t *out;
 };
 static __global__ void k_tc_xprep(TcPrep p) {
     const int nkc = p.K / kTcK;
-    const long per_seg = (long)p.ttiles * kTcTok * (p.K / 4);
-    const long total = per_seg * p.nseg;
-    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-        const int s = (int)(i / per_seg);
-        const long rem = i % per_seg;
-        const int j = (int)(rem / (p.K / 4)), k4 = (int)(rem % (p.K / 4)) * 4;
+    // 32-bit index arithmetic: the engine uses this path only when 16 segments x (rows + 128)
+    // x K/4 stays below 2^32
+    const unsigned kq = (unsigned)p.K / 4, per_seg = (unsigned)p.ttiles * kTcTok * kq;
+    const unsigned total = per_seg * (unsigned)p.nseg;
+    for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const unsigned s = i / per_seg, rem = i - s * per_seg;
+        const int j = (int)(rem / kq), k4 = (int)(rem - (unsigned)j * kq) * 4;
         const int n = p.cnt ? p.cnt[s] : p.M;
         if (j >= n) continue;
         const int row = p.idx ? p.idx[(size_t)s * p.ldi + j] : j;
-        const float4 v = *reinterpret_cast<const float4 *>(p.X + (size_t)s * p.x_seg + (size_t)row * p.ldx + k4);
+        float4 v;
+        if (p.glu) {  // janusdoe.c:925: silu(gate) * up, in f32
+            const float *xr = p.X + (size_t)s * p.x_seg + (size_t)row * p.ldx + 2 * k4;
+            const float4 a = *reinterpret_cast<const float4 *>(xr), b = *reinterpret_cast<const float4 *>(xr + 4);
+            v = make_float4(__fmul_rn(silu_ref(a.x), a.y), __fmul_rn(silu_ref(a.z), a.w), __fmul_rn(silu_ref(b.x), b.y),
+                            __fmul_rn(silu_ref(b.z), b.w));
+        } else {
+            v = *reinterpret_cast<const float4 *>(p.X + (size_t)s * p.x_seg + (size_t)row * p.ldx + k4);
+        }
         float4 h, l;
         tc_split(v.x, h.x, l.x);
         tc_split(v.y, h.y, l.y);
@@ -127,6 +137,8 @@ struct TcArgs {
     int ksplit;
     float *part;               // [tiles][ksplit][128 tokens][128 rows], tile = (seg * ttiles + tt) * rtiles + rt
     int *err;
+    unsigned long long *tl;    // optional wait profile (engine debug timeline), null when off
+    int tl_type;               // product kind: its eight counters are timeline slots 400 + 8 * tl_type
 };
 
 __device__ __forceinline__ uint64_t tc_desc(uint32_t saddr) {
@@ -203,6 +215,9 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
     const int ntok = min(kTcTok, n_tok_seg - tt * kTcTok);
     const uint8_t *wt = a.wt[seg];
     if (ntok <= 0 || !wt) return;  // whole CTA, before any barrier or allocation
+    const bool prof = a.tl != nullptr;
+    long long pw = 0, pw2 = 0;
+    const long long t_begin = prof ? clock64() : 0;
     const int per = (a.nkc + a.ksplit - 1) / a.ksplit, kc0 = ks * per, kc1 = min(a.nkc, kc0 + per);
     const int nloc = max(0, kc1 - kc0);
     if (tid == 0) {
@@ -226,6 +241,13 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_slot;
+    // debug wait profile (clock64 cycles): [1] CTA, [2] copy waits, [3] MMA operand waits,
+    // [4] MMA region waits, [5] drain waits (warp 2), [6] drain epilogue, [7] set-up
+    if (prof && tid == 0) {
+        unsigned long long *c = a.tl + 3 * (400 + 8 * a.tl_type) + 2;
+        atomicAdd(c, 1ull);
+        atomicAdd(c + 3 * 7, (unsigned long long)(clock64() - t_begin));
+    }
     const uint8_t *wbase = wt + ((size_t)rt * a.nkc) * 2 * kTcBlk;
     const uint8_t *xbase = a.xt + (((size_t)seg * a.ttiles + tt) * a.nkc) * 2 * kTcBlk;
     int issued_ld = 0, issued_mma = 0;
@@ -233,10 +255,12 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
         // ---------------- producer: four 16 KB bulk copies per chunk ----------------
         for (int i = 0; i < nloc; i++) {
             const int s = i % kTcStages;
+            const long long w0 = prof ? clock64() : 0;
             if (i >= kTcStages && !tc_wait(&empty[s], (uint32_t)((i / kTcStages) - 1) & 1u)) {
                 abort_flag = 1;
                 break;
             }
+            if (prof) pw += clock64() - w0;
             if (*(volatile int *)&abort_flag) break;
             uint8_t *st = stages + (size_t)s * kTcStageBytes;
             const int kc = kc0 + i;
@@ -252,8 +276,14 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
         const uint32_t idesc = tc_idesc(min(kTcTok, (ntok + 31) & ~31));
         for (int i = 0; i < nloc; i++) {
             const int s = i % kTcStages, q = i % kTcRegions;
+            const long long w0 = prof ? clock64() : 0;
             bool ok = tc_wait(&full[s], (uint32_t)(i / kTcStages) & 1u);
+            const long long w1 = prof ? clock64() : 0;
             if (ok && i >= kTcRegions) ok = tc_wait(&freed[q], (uint32_t)((i / kTcRegions) - 1) & 1u);
+            if (prof) {
+                pw += w1 - w0;
+                pw2 += clock64() - w1;
+            }
             if (!ok || *(volatile int *)&abort_flag) {
                 abort_flag = 1;
                 break;
@@ -292,7 +322,9 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
         bool ok = true;
         for (int i = 0; i < nloc; i++) {
             const int q = i % kTcRegions;
+            const long long w0 = prof ? clock64() : 0;
             if (!tc_wait(&ready[q], (uint32_t)(i / kTcRegions) & 1u)) ok = false;
+            if (prof) pw += clock64() - w0;
             if (__any_sync(JDG_FULL, !ok || *(volatile int *)&abort_flag)) {  // leave as a whole warp
                 ok = false;
                 break;
@@ -319,18 +351,59 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
             if (lane == 0) mbar_arrive(&freed[q]);
         }
         if (!ok) abort_flag = 1;
-        if (ok && nloc > 0) {
-            if (a.ksplit == 1) {
+        const long long e0 = prof ? clock64() : 0;
+        // Epilogue.  The tile goes through shared memory (the stage ring is idle once every
+        // chunk's product has been drained) as [token][row] and leaves by bulk copies, one row
+        // of the output per token; a residual add, or rows/strides that are not 16-byte
+        // multiples, take per-thread stores instead.
+        const int nr = min(kTcRows, a.n_rows - rt * kTcRows);
+        const bool al16 = a.ldc % 4 == 0 && a.c_seg % 4 == 0 && (reinterpret_cast<uintptr_t>(a.C) & 15) == 0;
+        const bool bulk = a.ksplit > 1 || (a.epi == EPI_STORE && al16 && nr % 4 == 0) ||
+                          (a.epi == EPI_SWIGLU && al16 && nr % 8 == 0);
+        if (!bulk) {
+            if (ok && nloc > 0) {
 #pragma unroll
                 for (int c = 0; c < kTcDrainCols; c++)
                     if (c < ncol) tc_store(a, seg, tt * kTcTok + col0 + c, n, acc[c], lane);
-            } else {
-                const size_t tile = ((size_t)seg * gridDim.y + tt) * gridDim.x + rt;
-                float *pp = a.part + (tile * a.ksplit + ks) * (size_t)kTcTok * kTcRows;
-#pragma unroll
-                for (int c = 0; c < kTcDrainCols; c++)
-                    if (c < ncol) pp[(size_t)(col0 + c) * kTcRows + row] = acc[c];
             }
+        } else {
+            float *tile = reinterpret_cast<float *>(stages);  // [128 tokens][128 rows]
+            if (ok && nloc > 0) {  // this warp saw every chunk land: no copy into the ring is in flight
+                if (a.ksplit == 1 && a.epi == EPI_SWIGLU) {
+#pragma unroll
+                    for (int c = 0; c < kTcDrainCols; c++)
+                        if (c < ncol) {  // uniform per warp
+                            const float other = __shfl_xor_sync(JDG_FULL, acc[c], 1);
+                            if ((lane & 1) == 0) tile[(col0 + c) * kTcRows + (row >> 1)] = __fmul_rn(silu_ref(acc[c]), other);
+                        }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < kTcDrainCols; c++)
+                        if (c < ncol) tile[(col0 + c) * kTcRows + row] = acc[c];
+                }
+            }
+            fence_proxy_async_smem();
+            asm volatile("bar.sync 1, %0;" ::"r"(kTcThreads - 64) : "memory");  // the eight drain warps
+            if (lane == 0 && nloc > 0 && !*(volatile int *)&abort_flag) {
+                if (a.ksplit > 1) {
+                    if (warp == 2) {
+                        const size_t t = ((size_t)seg * gridDim.y + tt) * gridDim.x + rt;
+                        bulk_s2g(a.part + (t * a.ksplit + ks) * (size_t)kTcTok * kTcRows, tile,
+                                 (uint32_t)ntok * kTcRows * 4);
+                    }
+                } else {
+                    const bool glu = a.epi == EPI_SWIGLU;
+                    float *cb = a.C + (size_t)seg * a.c_seg + (size_t)rt * (glu ? kTcRows / 2 : kTcRows);
+                    for (int c = warp - 2; c < ntok; c += 8)
+                        bulk_s2g(cb + (size_t)(tt * kTcTok + c) * a.ldc, tile + c * kTcRows, (uint32_t)(glu ? nr * 2 : nr * 4));
+                }
+                bulk_s2g_drain();
+            }
+        }
+        if (prof && warp == 2 && lane == 0) {
+            unsigned long long *c = a.tl + 3 * (400 + 8 * a.tl_type) + 2;
+            atomicAdd(c + 3 * 5, (unsigned long long)pw);
+            atomicAdd(c + 3 * 6, (unsigned long long)(clock64() - e0));
         }
     }
     __syncthreads();
@@ -342,8 +415,17 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
                 tc_wait(&full[i % kTcStages], (uint32_t)(i / kTcStages) & 1u);
         if (tid == 32 && issued_mma > 0) tc_wait(&empty[(issued_mma - 1) % kTcStages], (uint32_t)((issued_mma - 1) / kTcStages) & 1u);
     }
+    if (prof && (tid == 0 || tid == 32)) {
+        unsigned long long *c = a.tl + 3 * (400 + 8 * a.tl_type) + 2;
+        if (tid == 0) atomicAdd(c + 3 * 2, (unsigned long long)pw);
+        if (tid == 32) {
+            atomicAdd(c + 3 * 3, (unsigned long long)pw);
+            atomicAdd(c + 3 * 4, (unsigned long long)pw2);
+        }
+    }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
+    if (prof && tid == 0) atomicAdd(a.tl + 3 * (400 + 8 * a.tl_type) + 2 + 3, (unsigned long long)(clock64() - t_begin));
     if (warp == 0) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcRegions * kTcTok));
