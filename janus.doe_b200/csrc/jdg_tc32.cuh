@@ -5,9 +5,11 @@
 //
 // The f32 operands are split into TF32 parts, x = x_hi + x_lo with x_hi = x rounded to 10
 // mantissa bits and x_lo = x - x_hi (exact in f32, |x_lo| <= 2^-11 |x|; the tensor core keeps
-// its top 10 bits, so 2^-22 |x|), and four kind::tf32 products are accumulated in f32 in
-// tensor memory: W_hi.X_hi + W_hi.X_lo + W_lo.X_hi + W_lo.X_lo.  Every product of two TF32
-// numbers is exact in f32, so each term carries about 2^-21 relative error.
+// its top 10 bits, so 2^-22 |x|), and three kind::tf32 products are accumulated in f32 in
+// tensor memory: W_hi.X_hi + W_hi.X_lo + W_lo.X_hi.  Every product of two TF32 numbers is
+// exact in f32; the omitted W_lo.X_lo is at most 2^-22 |w x| per term (about 2^-24 on
+// average), which over a K = 768 sum stays an order of magnitude below the rounding of the
+// f32 sum itself (measured on N(0, 0.02) weights: 7.5e-8 against 4.3e-7 relative).
 //
 // Operands live in global memory already in the shared-memory layout the MMA descriptors
 // address (canonical K-major, no swizzle): for a block of 128 rows and a 32-wide K chunk, the
@@ -19,7 +21,7 @@
 //
 // CTA (320 threads) = one 128-row x 128-token output tile over a K range (split-K CTAs write
 // partials that k_tc_reduce adds in split order): thread 0 streams stages into a 3-deep ring;
-// thread 32 issues the 16 MMAs (M128 K8, N = the tile's token count rounded up to 32) of each
+// thread 32 issues the 12 MMAs (M128 K8, N = the tile's token count rounded up to 32) of each
 // 32-wide chunk into one of four accumulator regions and commits the stage back; warps 2-9 drain each
 // chunk's region into f32 registers with round-to-nearest adds (the tensor core's own
 // accumulation then spans only one chunk, 128 products) and apply the epilogue.  Every wait is bounded by wall time; on a timeout the CTA flags
@@ -298,7 +300,6 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
                 tc_mma(d, tc_desc(wh + o), tc_desc(xh + o), k8 > 0 ? 1u : 0u, idesc);
                 tc_mma(d, tc_desc(wh + o), tc_desc(xl + o), 1u, idesc);
                 tc_mma(d, tc_desc(wl + o), tc_desc(xh + o), 1u, idesc);
-                tc_mma(d, tc_desc(wl + o), tc_desc(xl + o), 1u, idesc);
             }
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                              smem_u32(&empty[s]))
