@@ -480,12 +480,15 @@ static int tc_build(jdg_engine *e, const jd_model *m) {
 // when idx is given, counts cnt[s] or M), W as per-segment block tables `wt` (n_rows x K).
 static void launch_tc(jdg_engine *e, const uint8_t *const *wt, int nseg, const float *X, long x_seg, int ldx,
                       const int *idx, int ldi, const int *cnt, int M, int max_rows, int n_rows, int K, float *C,
-                      int ldc, long c_seg, int epi, float alpha, int x_glu = 0) {
+                      int ldc, long c_seg, int epi, float alpha, int x_glu = 0, int x_ready = 0) {
     const int ttiles = (max_rows + kTcTok - 1) / kTcTok, nkc = K / kTcK;
     TcPrep p = {};
     p.X = X; p.x_seg = x_seg; p.ldx = ldx; p.K = K; p.idx = idx; p.ldi = ldi; p.cnt = cnt; p.M = M;
     p.nseg = nseg; p.ttiles = ttiles; p.glu = x_glu; p.out = e->tc_xt;
-    k_tc_xprep<<<1184, 256, 0, e->st>>>(p);
+    if (!x_ready) {  // else the producing kernel wrote the blocks (k_tc_norm_prep, k_tc_combine_prep)
+        k_tc_xprep<<<1184, 256, 0, e->st>>>(p);
+        e->launches++;
+    }
     const int rtiles = (n_rows + kTcRows - 1) / kTcRows;
     // split K until about one CTA per SM (every split keeps at least one chunk)
     int ks = 1;
@@ -501,7 +504,7 @@ static void launch_tc(jdg_engine *e, const uint8_t *const *wt, int nseg, const f
     a.tl = e->timeline;  // debug wait profile: 0 q/k/v, 1 Wo, 2 gate/up, 3 down, 4 LM head
     a.tl_type = nseg > 1 ? (x_glu ? 3 : 2) : epi == EPI_ADD ? 1 : n_rows == e->V ? 4 : 0;
     k_tc32_gemm<<<dim3(rtiles, ttiles, nseg * ks), kTcThreads, kTcSmem, e->st>>>(a);
-    e->launches += 2;
+    e->launches++;
     if (ks > 1) {
         const long items = (long)nseg * ttiles * rtiles * kTcTok * (kTcRows / 4);
         k_tc_reduce<<<(int)std::min<long>((items + 255) / 256, 148 * 8), 256, 0, e->st>>>(a, rtiles, nseg);
@@ -542,7 +545,8 @@ static void launch_gemv1(jdg_engine *e, int epi, const float *W, int N, int K, c
     e->launches++;
 }
 
-static void launch_attention(jdg_engine *e, int l, int B, float scale, float bias) {
+// tc_prep: the merge writes the Wo product's activation blocks instead of att
+static void launch_attention(jdg_engine *e, int l, int B, float scale, float bias, bool tc_prep = false) {
     AttnArgs a = {};
     a.qkv = e->qkv;
     a.ld = e->qkvd;
@@ -572,8 +576,12 @@ static void launch_attention(jdg_engine *e, int l, int B, float scale, float bia
         if (e->HD == 64) k_attn_partial<64><<<grid, 128, 0, e->st>>>(a);
         else k_attn_partial<128><<<grid, 128, 0, e->st>>>(a);
     }
-    k_attn_combine<<<dim3(e->Hh, B), e->HD, 0, e->st>>>(e->part, e->pos, e->Hh, e->HD, e->nchunk, chunk, e->att,
-                                                      e->qd);
+    if (tc_prep)
+        k_tc_combine_prep<<<dim3(e->Hh, B), e->HD, (size_t)2 * e->nchunk * 4, e->st>>>(e->part, e->pos, e->Hh, e->HD,
+                                                                                e->nchunk, chunk, e->tc_xt);
+    else
+        k_attn_combine<<<dim3(e->Hh, B), e->HD, (size_t)2 * e->nchunk * 4, e->st>>>(e->part, e->pos, e->Hh, e->HD,
+                                                                             e->nchunk, chunk, e->att, e->qd);
     e->launches += 2;
 }
 
@@ -899,11 +907,14 @@ static void enqueue_own_step(jdg_engine *e, int B) {
     if (B == 1) {
         launch_gemv1(e, EPI_STORE, e->output, V, D, e->x, e->output_norm, 1, e->logits);
     } else {
-        k_rmsnorm<<<B, 256, 0, e->st>>>(e->x, e->output_norm, e->xb, D, e->eps);
-        e->launches++;
-        if (e->tc_ok) {
-            launch_tc(e, e->tc_out_tab, 1, e->xb, 0, D, nullptr, 0, nullptr, B, B, V, D, e->logits, V, 0, EPI_STORE, 1.f);
+        if (e->tc_ok) {  // final norm straight into the LM head's activation blocks
+            k_tc_norm_prep<<<B, 256, 0, e->st>>>(e->x, e->output_norm, D, e->eps, e->tc_xt);
+            e->launches++;
+            launch_tc(e, e->tc_out_tab, 1, e->xb, 0, D, nullptr, 0, nullptr, B, B, V, D, e->logits, V, 0, EPI_STORE, 1.f,
+                      0, 1);
         } else {
+            k_rmsnorm<<<B, 256, 0, e->st>>>(e->x, e->output_norm, e->xb, D, e->eps);
+            e->launches++;
             SgemmArgs a = {};
             a.A = e->xb; a.lda = D; a.M = B; a.W = e->output; a.N = V; a.K = D; a.C = e->logits; a.ldc = V;
             launch_sgemm<EPI_STORE>(e, a, B, 1);
@@ -925,23 +936,26 @@ static void own_batch_layers(jdg_engine *e, int B, int prefill_slot) {
         if (B == 1) {
             launch_gemv1(e, EPI_STORE, ly.wqkv, e->qkvd, D, e->x, ly.attn_norm, 1, e->qkv);
         } else {
-            k_rmsnorm<<<B, 256, 0, e->st>>>(e->x, ly.attn_norm, e->xb, D, e->eps);
-            e->launches++;
-            if (e->tc_ok) {
+            if (e->tc_ok) {  // attention norm straight into the q/k/v product's activation blocks
+                k_tc_norm_prep<<<B, 256, 0, e->st>>>(e->x, ly.attn_norm, D, e->eps, e->tc_xt);
+                e->launches++;
                 launch_tc(e, ly.tc_wqkv_tab, 1, e->xb, 0, D, nullptr, 0, nullptr, B, B, e->qkvd, D, e->qkv, e->qkvd, 0,
-                          EPI_STORE, 1.f);
+                          EPI_STORE, 1.f, 0, 1);
             } else {
+                k_rmsnorm<<<B, 256, 0, e->st>>>(e->x, ly.attn_norm, e->xb, D, e->eps);
+                e->launches++;
                 SgemmArgs a = {};
                 a.A = e->xb; a.lda = D; a.M = B; a.W = ly.wqkv; a.N = e->qkvd; a.K = D; a.C = e->qkv; a.ldc = e->qkvd;
                 launch_sgemm<EPI_STORE>(e, a, B, 1);
             }
         }
         jdg_launch_rope(e, l, B);
-        launch_attention(e, l, B, scale, 1.0f);
+        launch_attention(e, l, B, scale, 1.0f, B > 1 && e->tc_ok);
         if (B == 1) {
             launch_gemv1(e, EPI_ADD, ly.wo, D, qd, e->att, nullptr, 0, e->x);
-        } else if (e->tc_ok) {
-            launch_tc(e, ly.tc_wo_tab, 1, e->att, 0, qd, nullptr, 0, nullptr, B, B, D, qd, e->x, D, 0, EPI_ADD, 1.f);
+        } else if (e->tc_ok) {  // the attention merge wrote the activation blocks
+            launch_tc(e, ly.tc_wo_tab, 1, e->att, 0, qd, nullptr, 0, nullptr, B, B, D, qd, e->x, D, 0, EPI_ADD, 1.f, 0,
+                      1);
         } else {
             SgemmArgs a = {};
             a.A = e->att; a.lda = qd; a.M = B; a.W = ly.wo; a.N = D; a.K = qd; a.C = e->x; a.ldc = D;

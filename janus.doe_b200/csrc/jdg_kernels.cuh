@@ -29,12 +29,9 @@ static __global__ void k_embed(const float *__restrict__ emb, int V, int D, cons
 }
 
 // out[b] = x[b] * (1/sqrtf(sum(x^2)/D + eps)) * w   (janusdoe.c:504, 3181-3186); w may be null
-static __global__ void k_rmsnorm(const float *__restrict__ x, const float *__restrict__ w, float *__restrict__ out, int D,
-                          float eps) {
-    __shared__ float red[32];
-    int b = blockIdx.x;
-    const float *xr = x + (size_t)b * D;
-    // elements tid, tid + blockDim, ... in order, eight loads in flight
+// 1 / sqrt(mean(x^2) + eps) of one row, the whole block taking part (janusdoe.c:504): thread
+// t sums elements t, t + blockDim, ... in order with eight loads in flight, then block_sum.
+__device__ __forceinline__ float rms_inv(const float *__restrict__ xr, int D, float eps, float *red) {
     float ss = 0.f;
     for (int base = 0; base < D; base += blockDim.x * 8) {
         float v[8];
@@ -48,7 +45,14 @@ static __global__ void k_rmsnorm(const float *__restrict__ x, const float *__res
             if (base + threadIdx.x + blockDim.x * m < D) ss = fmaf(v[m], v[m], ss);
     }
     ss = block_sum(ss, red);
-    float inv = 1.0f / sqrtf(ss / (float)D + eps);
+    return 1.0f / sqrtf(ss / (float)D + eps);
+}
+static __global__ void k_rmsnorm(const float *__restrict__ x, const float *__restrict__ w, float *__restrict__ out, int D,
+                          float eps) {
+    __shared__ float red[32];
+    int b = blockIdx.x;
+    const float *xr = x + (size_t)b * D;
+    const float inv = rms_inv(xr, D, eps, red);
     float *o = out + (size_t)b * D;
     for (int i = threadIdx.x; i < D; i += blockDim.x) {
         float v = __fmul_rn(xr[i], inv);
@@ -402,25 +406,9 @@ struct AttnArgs {
     float scale, bias, clamp, inv_clamp;
     float *part;  // [B][H][nchunk][HD+2]
 };
-// Per warp: the 16 key and 16 value rows of its positions (t = warp + 4i) are loaded as
-// vectors before any use, so 32 row loads per warp are in flight at once.
-template <int E>
-struct AttnVec;
-template <>
-struct AttnVec<2> {
-    using T = float2;
-    __device__ static void get(const T &v, float (&o)[2]) { o[0] = v.x; o[1] = v.y; }
-};
-template <>
-struct AttnVec<4> {
-    using T = float4;
-    __device__ static void get(const T &v, float (&o)[4]) { o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w; }
-};
 template <int HD>
 static __global__ __launch_bounds__(128) void k_attn_partial(AttnArgs a) {
     constexpr int E = HD / 32;  // dims per lane
-    constexpr int TW = kAttnChunk / 4;  // positions per warp
-    using V = AttnVec<E>;
     const int c = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int p = a.pos[b], t0 = c * kAttnChunk;
     if (t0 > p) return;
@@ -429,33 +417,21 @@ static __global__ __launch_bounds__(128) void k_attn_partial(AttnArgs a) {
     __shared__ __align__(16) float q_s[kMaxHG][HD];
     __shared__ float s_s[kMaxHG][kAttnChunk];
     __shared__ __align__(16) float o_s[4][kMaxHG][HD];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const float *kbase = a.kc + (size_t)b * a.bstride + (size_t)t0 * kd + (size_t)g * HD + lane * E;
-    const float *vbase = a.vc + (size_t)b * a.bstride + (size_t)t0 * kd + (size_t)g * HD + lane * E;
-    typename V::T kv[TW], vv[TW];
-#pragma unroll
-    for (int i = 0; i < TW; i++) {
-        const int t = warp + 4 * i;
-        if (t < nt) kv[i] = *reinterpret_cast<const typename V::T *>(kbase + (size_t)t * kd);
-    }
-#pragma unroll
-    for (int i = 0; i < TW; i++) {
-        const int t = warp + 4 * i;
-        if (t < nt) vv[i] = *reinterpret_cast<const typename V::T *>(vbase + (size_t)t * kd);
-    }
     const float *qrow = a.qkv + (size_t)b * a.ld + (size_t)g * hg * HD;
     for (int i = threadIdx.x; i < hg * HD; i += blockDim.x) q_s[i / HD][i % HD] = qrow[i];
     __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float *kbase = a.kc + (size_t)b * a.bstride + (size_t)t0 * kd + (size_t)g * HD;
+    const float *vbase = a.vc + (size_t)b * a.bstride + (size_t)t0 * kd + (size_t)g * HD;
+    for (int t = warp; t < nt; t += 4) {
+        const float *kr = kbase + (size_t)t * kd + lane * E;
+        float kv[E];
 #pragma unroll
-    for (int i = 0; i < TW; i++) {
-        const int t = warp + 4 * i;
-        if (t >= nt) break;
-        float k[E];
-        V::get(kv[i], k);
+        for (int e = 0; e < E; e++) kv[e] = kr[e];
         for (int j = 0; j < hg; j++) {
             float d = 0.f;
 #pragma unroll
-            for (int e = 0; e < E; e++) d = fmaf(q_s[j][lane * E + e], k[e], d);
+            for (int e = 0; e < E; e++) d = fmaf(q_s[j][lane * E + e], kv[e], d);
             d = warp_sum(d);
             if (lane == 0) {
                 float s = __fmul_rn(d, a.scale);
@@ -489,18 +465,17 @@ static __global__ __launch_bounds__(128) void k_attn_partial(AttnArgs a) {
     for (int j = 0; j < kMaxHG; j++)
 #pragma unroll
         for (int e = 0; e < E; e++) o[j][e] = 0.f;
+    for (int t = warp; t < nt; t += 4) {
+        const float *vr = vbase + (size_t)t * kd + lane * E;
+        float vv[E];
 #pragma unroll
-    for (int i = 0; i < TW; i++) {
-        const int t = warp + 4 * i;
-        if (t >= nt) break;
-        float v[E];
-        V::get(vv[i], v);
+        for (int e = 0; e < E; e++) vv[e] = vr[e];
 #pragma unroll
         for (int j = 0; j < kMaxHG; j++) {
             if (j < hg) {
                 float pj = s_s[j][t];
 #pragma unroll
-                for (int e = 0; e < E; e++) o[j][e] = fmaf(pj, v[e], o[j][e]);
+                for (int e = 0; e < E; e++) o[j][e] = fmaf(pj, vv[e], o[j][e]);
             }
         }
     }
@@ -523,6 +498,7 @@ static __global__ __launch_bounds__(128) void k_attn_partial(AttnArgs a) {
     }
 }
 
+// merge chunk partials: o = sum_c o_c e^{m_c-M} / sum_c l_c e^{m_c-M}; grid (H, B), block HD
 // Decode attention, one CTA per (chunk of 32 positions, row) over every head: the chunk's
 // key and value rows (all KV heads, contiguous in the cache) are copied to shared memory with
 // 16-byte cp.async (rows padded by 4 floats so that lanes reading different rows hit
@@ -602,20 +578,34 @@ static __global__ __launch_bounds__(1024) void k_attn_rows(AttnArgs a) {
     }
 }
 
+// Merge of the chunk partials of one (row, head): o[d] = sum_c o_c[d] f_c / sum_c l_c f_c with
+// f_c = e^{m_c - M}, in chunk order.  The chunks' (m, l) pairs are staged in shared memory
+// (ml: 2 * nc floats) by the whole block first, so no load waits on another.
+__device__ __forceinline__ float attn_merge(const float *__restrict__ pp, int nc, int HD, int d, float *ml) {
+    for (int c = threadIdx.x; c < nc; c += blockDim.x) {
+        ml[2 * c] = pp[(size_t)c * (HD + 2) + HD];
+        ml[2 * c + 1] = pp[(size_t)c * (HD + 2) + HD + 1];
+    }
+    __syncthreads();
+    float M = -INFINITY;
+    for (int c = 0; c < nc; c++) M = fmaxf(M, ml[2 * c]);
+    float S = 0.f, o = 0.f;
+#pragma unroll 8
+    for (int c = 0; c < nc; c++) {
+        const float f = expf(ml[2 * c] - M);
+        S = fmaf(ml[2 * c + 1], f, S);
+        o = fmaf(pp[(size_t)c * (HD + 2) + d], f, o);
+    }
+    return o / S;
+}
+// grid (H, rows), block HD, dynamic shared memory 2 * nchunk floats
 static __global__ void k_attn_combine(const float *__restrict__ part, const int *__restrict__ pos, int H, int HD, int nchunk,
                                int chunk, float *__restrict__ out, int ldo) {
+    extern __shared__ float ac_ml[];
     const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
     const int nc = pos[b] / chunk + 1;
-    const float *pp = part + ((size_t)b * H + h) * nchunk * (HD + 2);
-    float M = -INFINITY;
-    for (int c = 0; c < nc; c++) M = fmaxf(M, pp[c * (HD + 2) + HD]);
-    float S = 0.f, o = 0.f;
-    for (int c = 0; c < nc; c++) {
-        float f = expf(pp[c * (HD + 2) + HD] - M);
-        S = fmaf(pp[c * (HD + 2) + HD + 1], f, S);
-        o = fmaf(pp[c * (HD + 2) + d], f, o);
-    }
-    if (d < HD) out[(size_t)b * ldo + h * HD + d] = o / S;
+    const float o = attn_merge(part + ((size_t)b * H + h) * nchunk * (HD + 2), nc, HD, d, ac_ml);
+    out[(size_t)b * ldo + h * HD + d] = o;
 }
 
 // ------------------------------------------------------------------------------------
@@ -950,13 +940,26 @@ static __global__ __launch_bounds__(512) void k_route(const int *__restrict__ kc
 }
 
 // x[b] += sum_ki w[b][ki] * y[pairrow(b,ki)] in election order (janusdoe.c:927-929)
+// (the sequence's weights and rows are staged in shared memory, then every expert output of a
+// column is loaded before the sum)
 static __global__ void k_combine(const int *__restrict__ kcnt, const float *__restrict__ selw, const int *__restrict__ pairrow,
                           const float *__restrict__ y, int D, float *__restrict__ x) {
+    __shared__ float w_s[kMaxE];
+    __shared__ int row_s[kMaxE];
     const int b = blockIdx.x, k = kcnt[b];
+    if (threadIdx.x < kMaxE) {
+        w_s[threadIdx.x] = threadIdx.x < k ? selw[b * kMaxE + threadIdx.x] : 0.f;
+        row_s[threadIdx.x] = threadIdx.x < k ? pairrow[b * kMaxE + threadIdx.x] : 0;
+    }
+    __syncthreads();
     for (int r = threadIdx.x; r < D; r += blockDim.x) {
+        float yv[kMaxE];
+#pragma unroll
+        for (int ki = 0; ki < kMaxE; ki++) yv[ki] = ki < k ? y[(size_t)row_s[ki] * D + r] : 0.f;
         float eo = 0.f;
-        for (int ki = 0; ki < k; ki++)
-            eo = __fadd_rn(eo, __fmul_rn(selw[b * kMaxE + ki], y[(size_t)pairrow[b * kMaxE + ki] * D + r]));
+#pragma unroll
+        for (int ki = 0; ki < kMaxE; ki++)
+            if (ki < k) eo = __fadd_rn(eo, __fmul_rn(w_s[ki], yv[ki]));
         x[(size_t)b * D + r] = __fadd_rn(x[(size_t)b * D + r], eo);
     }
 }

@@ -126,6 +126,50 @@ static __global__ void k_tc_xprep(TcPrep p) {
     }
 }
 
+// Activation blocks written by the kernel that produces the activations (no separate prep):
+// one f32 value v of row j, column k of a single-segment operand with ttiles token tiles.
+__device__ __forceinline__ void tc_put(uint8_t *__restrict__ out, int nkc, int j, int k, float v) {
+    float hi, lo;
+    tc_split(v, hi, lo);
+    uint8_t *blk = out + ((size_t)(j / kTcTok) * nkc + k / kTcK) * 2 * kTcBlk;
+    *reinterpret_cast<float *>(blk + tc_off(j % kTcTok, k % kTcK)) = hi;
+    *reinterpret_cast<float *>(blk + kTcBlk + tc_off(j % kTcTok, k % kTcK)) = lo;
+}
+
+// RMS norm of row b (janusdoe.c:504, the arithmetic of k_rmsnorm) written straight into the
+// activation blocks of the next product.  grid = rows, block 256.
+static __global__ void k_tc_norm_prep(const float *__restrict__ x, const float *__restrict__ w, int D, float eps,
+                                      uint8_t *__restrict__ out) {
+    __shared__ float red[32];
+    const int b = blockIdx.x, nkc = D / kTcK;
+    const float *xr = x + (size_t)b * D;
+    const float inv = rms_inv(xr, D, eps, red);
+    for (int k4 = threadIdx.x * 4; k4 < D; k4 += blockDim.x * 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(xr + k4), g = *reinterpret_cast<const float4 *>(w + k4);
+        float4 y = make_float4(__fmul_rn(__fmul_rn(v.x, inv), g.x), __fmul_rn(__fmul_rn(v.y, inv), g.y),
+                               __fmul_rn(__fmul_rn(v.z, inv), g.z), __fmul_rn(__fmul_rn(v.w, inv), g.w));
+        float4 h, l;
+        tc_split(y.x, h.x, l.x);
+        tc_split(y.y, h.y, l.y);
+        tc_split(y.z, h.z, l.z);
+        tc_split(y.w, h.w, l.w);
+        uint8_t *blk = out + ((size_t)(b / kTcTok) * nkc + k4 / kTcK) * 2 * kTcBlk;
+        *reinterpret_cast<float4 *>(blk + tc_off(b % kTcTok, k4 % kTcK)) = h;
+        *reinterpret_cast<float4 *>(blk + kTcBlk + tc_off(b % kTcTok, k4 % kTcK)) = l;
+    }
+}
+
+// Attention merge (k_attn_combine's arithmetic) written into the activation blocks of the Wo
+// product: grid (H, rows), block HD, dynamic shared memory 2 * nchunk floats.
+static __global__ void k_tc_combine_prep(const float *__restrict__ part, const int *__restrict__ pos, int H, int HD,
+                                         int nchunk, int chunk, uint8_t *__restrict__ out) {
+    extern __shared__ float tcp_ml[];
+    const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    const int nc = pos[b] / chunk + 1;
+    const float o = attn_merge(part + ((size_t)b * H + h) * nchunk * (HD + 2), nc, HD, d, tcp_ml);
+    tc_put(out, H * HD / kTcK, b, h * HD + d, o);
+}
+
 struct TcArgs {
     const uint8_t *const *wt;  // per segment: weight blocks of W (n_rows x K); null = no work
     const uint8_t *xt;         // activation blocks [seg][ttiles][nkc][2][16 KB]
@@ -173,6 +217,26 @@ __device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity) {
     }
 }
 
+// The same wait for threads with nothing else to do (copy thread, drain warps): after one
+// test, mbarrier.try_wait suspends the thread in hardware until the phase completes or a
+// short time passes, so the waiters do not take issue slots from the MMA thread.
+__device__ __forceinline__ bool tc_wait_idle(uint64_t *bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile("{ .reg .pred p; mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                 : "=r"(done)
+                 : "r"(smem_u32(bar)), "r"(parity)
+                 : "memory");
+    if (done) return true;
+    const unsigned long long t0 = tc_now();
+    for (;;) {
+        asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                     : "=r"(done)
+                     : "r"(smem_u32(bar)), "r"(parity)
+                     : "memory");
+        if (done) return true;
+        if (tc_now() - t0 > 200ull * 1000 * 1000) return false;
+    }
+}
 // 8 consecutive f32 columns (tokens) of this warp's 32 TMEM lanes (rows), waited for
 __device__ __forceinline__ void tc_ld8(uint32_t taddr, float (&v)[8]) {
     uint32_t r[8];
@@ -258,7 +322,7 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
         for (int i = 0; i < nloc; i++) {
             const int s = i % kTcStages;
             const long long w0 = prof ? clock64() : 0;
-            if (i >= kTcStages && !tc_wait(&empty[s], (uint32_t)((i / kTcStages) - 1) & 1u)) {
+            if (i >= kTcStages && !tc_wait_idle(&empty[s], (uint32_t)((i / kTcStages) - 1) & 1u)) {
                 abort_flag = 1;
                 break;
             }
@@ -292,14 +356,17 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t st = smem_u32(stages + (size_t)s * kTcStageBytes);
-            const uint32_t wh = st, wl = st + kTcBlk, xh = st + 2 * kTcBlk, xl = st + 3 * kTcBlk;
+            // descriptors of the four parts; a K slice moves the start address (bits 0-13,
+            // 16-byte units) by two K groups of 2048 bytes
+            const uint64_t dwh = tc_desc(st), dwl = tc_desc(st + kTcBlk), dxh = tc_desc(st + 2 * kTcBlk),
+                           dxl = tc_desc(st + 3 * kTcBlk);
             const uint32_t d = tmem + (uint32_t)(q * kTcTok);
 #pragma unroll
             for (int k8 = 0; k8 < kTcK / 8; k8++) {  // K slices of 8: two K groups of the block
-                const uint32_t o = (uint32_t)k8 * 2 * 2048;
-                tc_mma(d, tc_desc(wh + o), tc_desc(xh + o), k8 > 0 ? 1u : 0u, idesc);
-                tc_mma(d, tc_desc(wh + o), tc_desc(xl + o), 1u, idesc);
-                tc_mma(d, tc_desc(wl + o), tc_desc(xh + o), 1u, idesc);
+                const uint64_t o = (uint64_t)(k8 * 2 * 2048 >> 4);
+                tc_mma(d, dwh + o, dxh + o, k8 > 0 ? 1u : 0u, idesc);
+                tc_mma(d, dwh + o, dxl + o, 1u, idesc);
+                tc_mma(d, dwl + o, dxh + o, 1u, idesc);
             }
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                              smem_u32(&empty[s]))
@@ -324,7 +391,7 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
         for (int i = 0; i < nloc; i++) {
             const int q = i % kTcRegions;
             const long long w0 = prof ? clock64() : 0;
-            if (!tc_wait(&ready[q], (uint32_t)(i / kTcRegions) & 1u)) ok = false;
+            if (!tc_wait_idle(&ready[q], (uint32_t)(i / kTcRegions) & 1u)) ok = false;
             if (prof) pw += clock64() - w0;
             if (__any_sync(JDG_FULL, !ok || *(volatile int *)&abort_flag)) {  // leave as a whole warp
                 ok = false;
