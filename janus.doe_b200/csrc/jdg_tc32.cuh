@@ -19,9 +19,9 @@
 // ([segment][token tile][K chunk][hi | lo], rows past the segment's count left as they are).  So a stage
 // is four 1-D bulk copies (cp.async.bulk, no tensor maps), and every byte is read once.
 //
-// CTA (320 threads) = one 128-row x 128-token output tile over a K range (split-K CTAs write
+// CTA (352 threads) = one 128-row x 128-token output tile over a K range (split-K CTAs write
 // partials that k_tc_reduce adds in split order): thread 0 streams stages into a 3-deep ring;
-// thread 32 issues the 12 MMAs (M128 K8, N = the tile's token count rounded up to 32) of each
+// threads 32 and 320 issue (alternate chunks) the 12 MMAs (M128 K8, N = the tile's token count rounded up to 32) of each
 // 32-wide chunk into one of four accumulator regions and commits the stage back; warps 2-9 drain each
 // chunk's region into f32 registers with round-to-nearest adds (the tensor core's own
 // accumulation then spans only one chunk, 128 products) and apply the epilogue.  Every wait is bounded by wall time; on a timeout the CTA flags
@@ -40,7 +40,7 @@ constexpr int kTcStages = 3;
 constexpr int kTcStageBytes = 4 * kTcBlk;      // W hi, W lo, X hi, X lo
 constexpr int kTcSmem = 1024 + kTcStages * kTcStageBytes;
 constexpr int kTcMaxSplit = 8;
-constexpr int kTcThreads = 320;                // warp 0 copies, warp 1 MMAs, warps 2-9 drain
+constexpr int kTcThreads = 352;                // warp 0 copies, warps 1 and 10 MMAs, warps 2-9 drain
 constexpr int kTcDrainCols = 64;               // token columns per drain warp (two warps per TMEM lane quarter)
 constexpr int kTcRegions = 4;                  // accumulator regions of 128 TMEM columns
 // kind::tf32 instruction descriptor: D f32 (bits 4-5 = 1), A and B TF32 (bits 7-9, 10-12 = 2),
@@ -275,6 +275,7 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
     __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], ready[kTcRegions], freed[kTcRegions];
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag;
+    __shared__ int seen[2];  // chunks of each parity whose operands their MMA issuer has seen land
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rt = blockIdx.x, tt = blockIdx.y, seg = blockIdx.z / a.ksplit, ks = blockIdx.z % a.ksplit;
     const int n_tok_seg = a.cnt ? a.cnt[seg] : a.M;
@@ -296,6 +297,7 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
             mbar_init(&freed[q], 8);  // the eight drain warps
         }
         abort_flag = 0;
+        seen[0] = seen[1] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
@@ -335,15 +337,33 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
             bulk_g2s(st + 2 * kTcBlk, xbase + (size_t)kc * 2 * kTcBlk, 2 * kTcBlk, &full[s]);
             issued_ld = i + 1;
         }
-    } else if (tid == 32) {
-        // ---------------- MMA issuer: chunk i into accumulator region i % kTcRegions ----------------
+    } else if (tid == 32 || tid == kTcThreads - 32) {
+        // ---------------- MMA issuers: chunk i into accumulator region i % kTcRegions ----------------
+        // thread 32 issues the even chunks, the first thread of warp 10 the odd ones (each
+        // commit tracks the issuing thread's own MMAs; different chunks use different stages
+        // and regions), so one chunk's issue overlaps the other's waits
         // token columns past ntok are not computed beyond the next multiple of 32; the drain
         // reads whole groups of 32 columns and stores only those below ntok
         const uint32_t idesc = tc_idesc(min(kTcTok, (ntok + 31) & ~31));
-        for (int i = 0; i < nloc; i++) {
+        const int par = tid == 32 ? 0 : 1;
+        for (int i = par; i < nloc; i += 2) {
             const int s = i % kTcStages, q = i % kTcRegions;
             const long long w0 = prof ? clock64() : 0;
-            bool ok = tc_wait(&full[s], (uint32_t)(i / kTcStages) & 1u);
+            bool ok = true;
+            if (i >= kTcStages) {
+                // stage s last held chunk i - 3, the other issuer's: its phase of full[s] must
+                // have completed before this parity test means chunk i (a phase-parity wait
+                // cannot tell phase n from phase n - 2)
+                const int o = (i - kTcStages) & 1, need = (i - kTcStages - o) / 2 + 1;
+                const unsigned long long t0 = tc_now();
+                while (*(volatile int *)&seen[o] < need)
+                    if (tc_now() - t0 > 200ull * 1000 * 1000) {
+                        ok = false;
+                        break;
+                    }
+            }
+            ok = ok && tc_wait(&full[s], (uint32_t)(i / kTcStages) & 1u);
+            if (ok) *(volatile int *)&seen[par] = (i - par) / 2 + 1;
             const long long w1 = prof ? clock64() : 0;
             if (ok && i >= kTcRegions) ok = tc_wait(&freed[q], (uint32_t)((i / kTcRegions) - 1) & 1u);
             if (prof) {
@@ -378,7 +398,7 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
         }
     }
     __syncwarp();
-    if (warp >= 2) {
+    if (warp >= 2 && warp < 10) {
         // ---------------- drain: every chunk's product added in f32 (round to nearest) ----------------
         // warp w reads TMEM lanes 32 (w % 4) .. (its weight rows), token columns
         // col0 .. col0 + 63: all eight 8-column loads in flight before one wait
@@ -451,7 +471,7 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
                 }
             }
             fence_proxy_async_smem();
-            asm volatile("bar.sync 1, %0;" ::"r"(kTcThreads - 64) : "memory");  // the eight drain warps
+            asm volatile("bar.sync 1, 256;" ::: "memory");  // the eight drain warps
             if (lane == 0 && nloc > 0 && !*(volatile int *)&abort_flag) {
                 if (a.ksplit > 1) {
                     if (warp == 2) {
@@ -481,12 +501,12 @@ static __global__ __launch_bounds__(kTcThreads, 1) void k_tc32_gemm(TcArgs a) {
         if (tid == 0)
             for (int i = max(0, issued_ld - kTcStages); i < issued_ld; i++)
                 tc_wait(&full[i % kTcStages], (uint32_t)(i / kTcStages) & 1u);
-        if (tid == 32 && issued_mma > 0) tc_wait(&empty[(issued_mma - 1) % kTcStages], (uint32_t)((issued_mma - 1) / kTcStages) & 1u);
+        if ((tid == 32 || tid == kTcThreads - 32) && issued_mma > 0) tc_wait(&empty[(issued_mma - 1) % kTcStages], (uint32_t)((issued_mma - 1) / kTcStages) & 1u);
     }
-    if (prof && (tid == 0 || tid == 32)) {
+    if (prof && (tid == 0 || tid == 32 || tid == kTcThreads - 32)) {
         unsigned long long *c = a.tl + 3 * (400 + 8 * a.tl_type) + 2;
         if (tid == 0) atomicAdd(c + 3 * 2, (unsigned long long)pw);
-        if (tid == 32) {
+        if (tid != 0) {
             atomicAdd(c + 3 * 3, (unsigned long long)pw);
             atomicAdd(c + 3 * 4, (unsigned long long)pw2);
         }
