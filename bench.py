@@ -91,15 +91,46 @@ def dram_traffic(workload, alg_bytes_per_step):
 
 
 class Clocks:
-    """nvidia-smi sampler for the timed region (SM clock and throttle reasons)."""
+    """SM clock and throttle reasons sampled during the timed region: NVML polled every 2 ms
+    from a thread (so even a region of a few milliseconds gets samples), nvidia-smi at 200 ms
+    when NVML is not importable."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, gpu_index):
-        self.idx, self.rows, self.proc = gpu_index, [], None
+        self.idx, self.rows, self.proc, self.nv = gpu_index, [], None, None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(gpu_index)
+            self.bits = [pynvml.nvmlClocksEventReasonHwSlowdown, pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                         pynvml.nvmlClocksEventReasonSwThermalSlowdown, pynvml.nvmlClocksEventReasonSwPowerCap]
+        except Exception:
+            self.nv = None
+
+    def _poll(self):
+        nv = self.nv
+        while not self.done:
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM),
+                                     nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)))
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def start(self):
+        if self.nv is not None:
+            self.samples, self.done = [], False
+            self.th = threading.Thread(target=self._poll, daemon=True)
+            self.th.start()
+            t0 = time.time()
+            while not self.samples and time.time() - t0 < 2.0:  # the first sample precedes the region
+                time.sleep(0.001)
+            self.n0 = len(self.samples)
+            return
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), "--query-gpu=" + self.Q,
                                           "--format=csv,noheader,nounits", "-lms", "200"],
@@ -114,6 +145,18 @@ class Clocks:
             self.rows.append([x.strip() for x in line.split(",")])
 
     def stop(self):
+        if self.nv is not None:
+            self.done = True
+            self.th.join(timeout=1.0)
+            inside = self.samples[self.n0:] or self.samples[-1:]
+            sm = [float(c) for c, _ in inside]
+            reasons = sorted({self.NAMES[i] for _, r in inside for i, b in enumerate(self.bits) if r & b})
+            try:
+                mx = float(self.nv.nvmlDeviceGetMaxClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+            except Exception:
+                mx = None
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                    "samples": len(sm), "source": "nvml, 2 ms"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         time.sleep(0.25)
@@ -124,10 +167,9 @@ class Clocks:
             self.proc.kill()
         sm = [float(r[1]) for r in self.rows if len(r) >= 8 and r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in self.rows if len(r) >= 8 and r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows if len(r) >= 8 for i in range(4) if r[4 + i] == "Active"})
+        reasons = sorted({self.NAMES[i] for r in self.rows if len(r) >= 8 for i in range(4) if r[4 + i] == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(sm)}
+                "reasons": reasons, "samples": len(sm), "source": "nvidia-smi, 200 ms"}
 
 
 def dist_setup():
