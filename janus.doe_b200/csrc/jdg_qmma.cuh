@@ -215,13 +215,23 @@ __device__ __forceinline__ void qm_epilogue(const QmArgs &a, const float (&acc)[
             const float other = __shfl_xor_sync(JDG_FULL, acc[t], 1);
             if (!(lane & 1) && t < a.M && n + 1 < a.w.rows) a.C[(size_t)t * a.ldc + n / 2] = __fmul_rn(silu_ref(acc[t]), other);
         }
+    } else if (n < a.w.rows && a.epi == EPI_ADD) {
+        // eight tokens' C values loaded before any store (a load after a store to another
+        // token's row could not be moved ahead of it: one L2 round trip per token)
+#pragma unroll
+        for (int t0 = 0; t0 < kQmTok; t0 += 8) {
+            float c[8];
+#pragma unroll
+            for (int t = 0; t < 8; t++) c[t] = t0 + t < a.M ? a.C[(size_t)(t0 + t) * a.ldc + n] : 0.f;
+#pragma unroll
+            for (int t = 0; t < 8; t++)
+                if (t0 + t < a.M) a.C[(size_t)(t0 + t) * a.ldc + n] = __fadd_rn(c[t], __fmul_rn(acc[t0 + t], a.alpha));
+        }
     } else if (n < a.w.rows) {
 #pragma unroll
         for (int t = 0; t < kQmTok; t++) {
             if (t >= a.M) break;
-            float *cp = a.C + (size_t)t * a.ldc + n;
-            if (a.epi == EPI_ADD) *cp = __fadd_rn(*cp, __fmul_rn(acc[t], a.alpha));
-            else *cp = acc[t];
+            a.C[(size_t)t * a.ldc + n] = acc[t];
         }
     }
 }
