@@ -766,10 +766,19 @@ static __global__ __launch_bounds__(128) void k_b1_ffn2(B1Args a) {
     if (!last_cta(a.tickets + 64 + rb, k)) return;
     if (threadIdx.x < 4) {
         const int rr = rb * 4 + threadIdx.x;
-        if (rr < a.D) {
+        if (rr < a.D) {  // every operand loaded before the ordered sum
+            const float xo = a.x[rr];
+            float wv[kMaxE], yv[kMaxE];
+#pragma unroll
+            for (int q = 0; q < kMaxE; q++) {
+                wv[q] = q < k ? __ldcg(a.selw + q) : 0.f;
+                yv[q] = q < k ? __ldcg(a.ybuf + (size_t)q * a.D + rr) : 0.f;
+            }
             float eo = 0.f;
-            for (int q = 0; q < k; q++) eo = __fadd_rn(eo, __fmul_rn(__ldcg(a.selw + q), __ldcg(a.ybuf + (size_t)q * a.D + rr)));
-            a.x[rr] = __fadd_rn(a.x[rr], eo);
+#pragma unroll
+            for (int q = 0; q < kMaxE; q++)
+                if (q < k) eo = __fadd_rn(eo, __fmul_rn(wv[q], yv[q]));
+            a.x[rr] = __fadd_rn(xo, eo);
         }
     }
     if (threadIdx.x == 0) a.tickets[64 + rb] = 0;
