@@ -236,6 +236,29 @@ __device__ __forceinline__ void qm_epilogue(const QmArgs &a, const float (&acc)[
     }
 }
 
+// The same for tokens t0 .. t0 + 7 only (the split-K sum, where each warp owns eight tokens).
+__device__ __forceinline__ void qm_epilogue8(const QmArgs &a, const float (&acc)[8], int t0, int n, int lane) {
+    if (a.epi == EPI_SWIGLU) {
+#pragma unroll
+        for (int t = 0; t < 8; t++) {
+            const float other = __shfl_xor_sync(JDG_FULL, acc[t], 1);
+            if (!(lane & 1) && t0 + t < a.M && n + 1 < a.w.rows)
+                a.C[(size_t)(t0 + t) * a.ldc + n / 2] = __fmul_rn(silu_ref(acc[t]), other);
+        }
+    } else if (n < a.w.rows && a.epi == EPI_ADD) {
+        float c[8];
+#pragma unroll
+        for (int t = 0; t < 8; t++) c[t] = t0 + t < a.M ? a.C[(size_t)(t0 + t) * a.ldc + n] : 0.f;
+#pragma unroll
+        for (int t = 0; t < 8; t++)
+            if (t0 + t < a.M) a.C[(size_t)(t0 + t) * a.ldc + n] = __fadd_rn(c[t], __fmul_rn(acc[t], a.alpha));
+    } else if (n < a.w.rows) {
+#pragma unroll
+        for (int t = 0; t < 8; t++)
+            if (t0 + t < a.M) a.C[(size_t)(t0 + t) * a.ldc + n] = acc[t];
+    }
+}
+
 // grid (rows/128, ksplit), block kQmThreads, dynamic smem kQmSmem.  tm_codes: 2-D map over
 // the code bytes [rows][cols/2], box 128 bytes x 128 rows, 128-byte swizzle; tm_hdr: 2-D map
 // over the headers [rows][cols/256 * 16], box 16 bytes x 128 rows.  Rows past the end read
@@ -496,25 +519,29 @@ static __global__ __launch_bounds__(kQmThreads, 1) void k_qm_q4k(QmArgs a, const
             }
         }
         __syncthreads();
-        if (s_last && warp > kQmTmaWarp) {
-            const int row = (warp & 3) * 32 + lane, n = n0 + row;
-            float acc[kQmTok];
+        if (s_last && warp < 16) {
+            // sixteen warps: TMEM-row quarter warp % 4, tokens 8 (warp / 4) .. + 7; four
+            // splits' loads in flight at once, added in split order
+            const int row = (warp & 3) * 32 + lane, n = n0 + row, t0 = 8 * (warp >> 2);
+            float acc[8];
 #pragma unroll
-            for (int t = 0; t < kQmTok; t++) acc[t] = 0.f;
-            // split by split, half the tokens' loads in flight at once
-            for (int z = 0; z < ks; z++)
+            for (int t = 0; t < 8; t++) acc[t] = 0.f;
+            for (int z0 = 0; z0 < ks; z0 += 4) {
+                float v[4][8];
 #pragma unroll
-                for (int hf = 0; hf < 2; hf++) {
-                    float v[16];
+                for (int zz = 0; zz < 4; zz++)
 #pragma unroll
-                    for (int t = 0; t < 16; t++)
-                        v[t] = (16 * hf + t < a.M && n < a.w.rows)
-                                   ? __ldcg(a.part + ((size_t)z * kQmTok + 16 * hf + t) * a.w.rows + n)
-                                   : 0.f;
+                    for (int t = 0; t < 8; t++)
+                        v[zz][t] = (z0 + zz < ks && t0 + t < a.M && n < a.w.rows)
+                                       ? __ldcg(a.part + ((size_t)(z0 + zz) * kQmTok + t0 + t) * a.w.rows + n)
+                                       : 0.f;
 #pragma unroll
-                    for (int t = 0; t < 16; t++) acc[16 * hf + t] += v[t];
-                }
-            qm_epilogue(a, acc, n, lane);
+                for (int zz = 0; zz < 4; zz++)
+                    if (z0 + zz < ks)
+#pragma unroll
+                        for (int t = 0; t < 8; t++) acc[t] += v[zz][t];
+            }
+            qm_epilogue8(a, acc, t0, n, lane);
         }
     }
     if (*abort_flag) {
