@@ -445,12 +445,17 @@ static __global__ __launch_bounds__(128) void k_hb1_wo(HB1Args a) {
         for (int c = 0; c < MAXCH; c++) fm[h][c] = f[c] / S;
     }
     __syncthreads();
-#pragma unroll 4
+#pragma unroll 2
     for (int i = threadIdx.x; i < a.qd; i += 128) {
         const int h = i / HD, d = i % HD;
         const float *pp = a.part + (size_t)h * ncs * (HD + 2) + d;
+        float ov[MAXCH];  // every chunk's value loaded before the ordered sum
+#pragma unroll
+        for (int c = 0; c < MAXCH; c++) ov[c] = c < nc ? __ldcg(pp + (size_t)c * (HD + 2)) : 0.f;
         float o = 0.f;
-        for (int c = 0; c < nc; c++) o = fmaf(__ldcg(pp + (size_t)c * (HD + 2)), fm[h][c], o);
+#pragma unroll
+        for (int c = 0; c < MAXCH; c++)
+            if (c < nc) o = fmaf(ov[c], fm[h][c], o);
         hsm[xsw<DT>(i >> 2) * 4 + (i & 3)] = o;
     }
     __syncthreads();
