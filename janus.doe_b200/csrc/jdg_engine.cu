@@ -158,6 +158,7 @@ int jdg_alloc_state(jdg_engine *e) {
     }
     e->pin_pos = e->pin_tok + B;
     e->pin_next = e->pin_pos + B;
+    e->pin_err = e->pin_next + B;  // in the 64 spare bytes
     DALLOC(e->tickets, 1024 * 4);
     CK(cudaMemsetAsync(e->tickets, 0, 1024 * 4, e->st));
     CK(cudaMemsetAsync(e->tok, 0, B * 4, e->st));
@@ -1073,8 +1074,14 @@ int jdg_host_drop_graphs(jdg_engine *e) {
 
 static int check_err(jdg_engine *e) {
     int h = 0;
-    CK(cudaMemcpyAsync(&h, e->err, 4, cudaMemcpyDeviceToHost, e->st));
-    CK(cudaStreamSynchronize(e->st));
+    if (e->pin_err) {  // a pinned destination keeps the copy asynchronous (no staging)
+        CK(cudaMemcpyAsync(e->pin_err, e->err, 4, cudaMemcpyDeviceToHost, e->st));
+        CK(cudaStreamSynchronize(e->st));
+        h = *e->pin_err;
+    } else {
+        CK(cudaMemcpyAsync(&h, e->err, 4, cudaMemcpyDeviceToHost, e->st));
+        CK(cudaStreamSynchronize(e->st));
+    }
     if (h) {
         CK(cudaMemsetAsync(e->err, 0, 4, e->st));
         jdg_set_err(e->ctx, "device-side check failed (flags 0x%x: %s%s%s%s%s)", h, (h & JDG_ERR_TOKEN) ? "token " : "",

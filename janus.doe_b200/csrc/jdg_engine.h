@@ -84,6 +84,7 @@ struct jdg_engine {
     unsigned long long *stats = nullptr;
     unsigned long long *timeline = nullptr;  // optional per-kernel timeline (jdg_debug_timeline)  // [0] experts read, [1] KV positions read, [2] steps
     int *pin_tok = nullptr, *pin_pos = nullptr, *pin_next = nullptr;  // pinned staging for jdg_step
+    int *pin_err = nullptr;              // pinned copy of the device error word
     int *amax_i = nullptr;
     int b1_ok = 0;                // shapes fit the batch-1 PDL chain
     int force_generic = 0;        // JDG_GENERIC=1: use the generic kernels at batch 1

@@ -534,19 +534,19 @@ static __global__ __launch_bounds__(256) void k_tc_reduce(TcArgs a, int rtiles, 
         const int n = rt * kTcRows + r4;
         if (n >= a.n_rows) continue;
         const float *p = a.part + (size_t)tile * a.ksplit * kTcTok * kTcRows + (size_t)c * kTcRows + r4;
-        float4 v[kTcMaxSplit];  // every split's partial loaded before the ordered sum
+        float4 pz[kTcMaxSplit];  // every split's partial loaded before the ordered sum
 #pragma unroll
         for (int z = 0; z < kTcMaxSplit; z++)
-            v[z] = z < a.ksplit ? __ldcg(reinterpret_cast<const float4 *>(p + (size_t)z * kTcTok * kTcRows))
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
+            pz[z] = z < a.ksplit ? __ldcg(reinterpret_cast<const float4 *>(p + (size_t)z * kTcTok * kTcRows))
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
         float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int z = 0; z < kTcMaxSplit; z++)
             if (z < a.ksplit) {
-                s.x = __fadd_rn(s.x, v[z].x);
-                s.y = __fadd_rn(s.y, v[z].y);
-                s.z = __fadd_rn(s.z, v[z].z);
-                s.w = __fadd_rn(s.w, v[z].w);
+                s.x = __fadd_rn(s.x, pz[z].x);
+                s.y = __fadd_rn(s.y, pz[z].y);
+                s.z = __fadd_rn(s.z, pz[z].z);
+                s.w = __fadd_rn(s.w, pz[z].w);
             }
         float *out = a.C + (size_t)seg * a.c_seg + (size_t)(tt * kTcTok + c) * a.ldc;
         const float v[4] = {s.x, s.y, s.z, s.w};
