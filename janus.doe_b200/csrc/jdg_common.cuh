@@ -14,6 +14,16 @@ enum {
     JDG_ERR_TIMEOUT = 16,  // a bounded wait on an asynchronous copy ran out
 };
 
+// Split-K partial tiles of a single-segment tensor-core product that the consumer sums
+// itself (no separate reduce launch): tile (row tile tt, column tile rt) holds
+// [ks][128 tokens][128 columns] at tile = tt * rtiles + rt.  part null: none.
+constexpr int kSplitTile = 128;
+constexpr int kSplitMax = 8;  // split ways at most
+struct SplitPart {
+    const float *part;
+    int ks, rtiles;
+};
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(JDG_FULL, v, o);

@@ -481,7 +481,8 @@ static int tc_build(jdg_engine *e, const jd_model *m) {
 // when idx is given, counts cnt[s] or M), W as per-segment block tables `wt` (n_rows x K).
 static void launch_tc(jdg_engine *e, const uint8_t *const *wt, int nseg, const float *X, long x_seg, int ldx,
                       const int *idx, int ldi, const int *cnt, int M, int max_rows, int n_rows, int K, float *C,
-                      int ldc, long c_seg, int epi, float alpha, int x_glu = 0, int x_ready = 0) {
+                      int ldc, long c_seg, int epi, float alpha, int x_glu = 0, int x_ready = 0,
+                      SplitPart *fuse = nullptr) {
     const int ttiles = (max_rows + kTcTok - 1) / kTcTok, nkc = K / kTcK;
     TcPrep p = {};
     p.X = X; p.x_seg = x_seg; p.ldx = ldx; p.K = K; p.idx = idx; p.ldi = ldi; p.cnt = cnt; p.M = M;
@@ -506,7 +507,10 @@ static void launch_tc(jdg_engine *e, const uint8_t *const *wt, int nseg, const f
     a.tl_type = nseg > 1 ? (x_glu ? 3 : 2) : epi == EPI_ADD ? 1 : n_rows == e->V ? 4 : 0;
     k_tc32_gemm<<<dim3(rtiles, ttiles, nseg * ks), kTcThreads, kTcSmem, e->st>>>(a);
     e->launches++;
-    if (ks > 1) {
+    if (fuse) *fuse = SplitPart{nullptr, 1, rtiles};
+    if (ks > 1 && fuse && nseg == 1) {  // the consumer sums the partials (split_sum)
+        *fuse = SplitPart{e->tc_part, ks, rtiles};
+    } else if (ks > 1) {
         const long items = (long)nseg * ttiles * rtiles * kTcTok * (kTcRows / 4);
         k_tc_reduce<<<(int)std::min<long>((items + 255) / 256, 148 * 8), 256, 0, e->st>>>(a, rtiles, nseg);
         e->launches++;
@@ -605,7 +609,7 @@ int jdg_attn_setup(jdg_engine *e) {
     return JD_OK;
 }
 
-void jdg_launch_rope(jdg_engine *e, int l, int B) {
+void jdg_launch_rope(jdg_engine *e, int l, int B, SplitPart sp) {
     RopeArgs r = {};
     r.qkv = e->qkv;
     r.ld = e->qkvd;
@@ -621,6 +625,7 @@ void jdg_launch_rope(jdg_engine *e, int l, int B) {
     r.vc = e->vc + (size_t)l * e->max_seq * e->kd;
     r.bstride = e->kv_bstride;
     r.err = e->err;
+    r.sp = sp;
     k_rope_kv<<<B, 256, 0, e->st>>>(r);
     e->launches++;
 }
@@ -655,9 +660,11 @@ void jdg_launch_pick_tp(jdg_engine *e, int B, const float *v, const int *ix, int
 }
 
 void jdg_launch_elect(jdg_engine *e, int l, int B, const float *xin, const float *norm_w, const float *w_vote,
-                      const int *alive, float temperature, int host) {
+                      const int *alive, float temperature, int host, SplitPart sp) {
     ElectArgs a = {};
     a.x = xin;
+    a.sp = sp;
+    a.x_out = e->x;
     a.norm_w = norm_w;
     a.eps = e->eps;
     a.D = e->D;
@@ -934,6 +941,8 @@ static void own_batch_layers(jdg_engine *e, int B, int prefill_slot) {
     e->launches++;
     for (int l = 0; l < L; l++) {
         LayerDev &ly = e->layers[l];
+        // split-K partials of q/k/v and Wo summed by their consumers (rope, election)
+        SplitPart qsp{nullptr, 1, 1}, wsp{nullptr, 1, 1};
         if (B == 1) {
             launch_gemv1(e, EPI_STORE, ly.wqkv, e->qkvd, D, e->x, ly.attn_norm, 1, e->qkv);
         } else {
@@ -941,7 +950,7 @@ static void own_batch_layers(jdg_engine *e, int B, int prefill_slot) {
                 k_tc_norm_prep<<<B, 256, 0, e->st>>>(e->x, ly.attn_norm, D, e->eps, e->tc_xt);
                 e->launches++;
                 launch_tc(e, ly.tc_wqkv_tab, 1, e->xb, 0, D, nullptr, 0, nullptr, B, B, e->qkvd, D, e->qkv, e->qkvd, 0,
-                          EPI_STORE, 1.f, 0, 1);
+                          EPI_STORE, 1.f, 0, 1, &qsp);
             } else {
                 k_rmsnorm<<<B, 256, 0, e->st>>>(e->x, ly.attn_norm, e->xb, D, e->eps);
                 e->launches++;
@@ -950,20 +959,21 @@ static void own_batch_layers(jdg_engine *e, int B, int prefill_slot) {
                 launch_sgemm<EPI_STORE>(e, a, B, 1);
             }
         }
-        jdg_launch_rope(e, l, B);
+        jdg_launch_rope(e, l, B, qsp);
         launch_attention(e, l, B, scale, 1.0f, B > 1 && e->tc_ok);
         if (B == 1) {
             launch_gemv1(e, EPI_ADD, ly.wo, D, qd, e->att, nullptr, 0, e->x);
         } else if (e->tc_ok) {  // the attention merge wrote the activation blocks
             launch_tc(e, ly.tc_wo_tab, 1, e->att, 0, qd, nullptr, 0, nullptr, B, B, D, qd, e->x, D, 0, EPI_ADD, 1.f, 0,
-                      1);
+                      1, &wsp);
         } else {
             SgemmArgs a = {};
             a.A = e->att; a.lda = qd; a.M = B; a.W = ly.wo; a.N = D; a.K = qd; a.C = e->x; a.ldc = D;
             launch_sgemm<EPI_ADD>(e, a, B, 1);
         }
         if (prefill_slot < 0) {
-            jdg_launch_elect(e, l, B, e->x, ly.ffn_norm, ly.w_vote, e->alive_dev + (size_t)l * kMaxE, ly.temperature, 0);
+            jdg_launch_elect(e, l, B, e->x, ly.ffn_norm, ly.w_vote, e->alive_dev + (size_t)l * kMaxE, ly.temperature, 0,
+                             wsp);
         } else {
             ElectArgs a = {};
             a.x = e->x; a.norm_w = ly.ffn_norm; a.eps = e->eps; a.D = D; a.host = 0; a.w_vote = ly.w_vote;
@@ -972,6 +982,8 @@ static void own_batch_layers(jdg_engine *e, int B, int prefill_slot) {
             a.tr_sel = e->tr_sel; a.tr_w = e->tr_w; a.tr_ema = e->tr_ema;
             a.prefill = 1; a.pf_votes = e->pf_votes; a.pf_cs = e->pf_cs;
             a.pf_cons = e->consensus + (size_t)prefill_slot * L + l;
+            a.sp = wsp;
+            a.x_out = e->x;
             k_elect<<<B, 256, (size_t)D * 4, e->st>>>(a);
             k_elect_scan<<<1, 256, (size_t)B * 4, e->st>>>(a, B);
             e->launches += 2;

@@ -6,6 +6,7 @@
 #include <vector>
 
 #include "../../include/jdgpu.h"
+#include "jdg_common.cuh"
 
 struct LayerDev {
     float *attn_norm = nullptr, *ffn_norm = nullptr, *wqkv = nullptr, *wo = nullptr, *w_vote = nullptr;
@@ -122,14 +123,14 @@ void jdg_set_err(jdg_ctx *c, const char *fmt, ...);
 int jdg_ctx_device(jdg_ctx *c);
 int jdg_alloc_state(jdg_engine *e);
 int jdg_own_upload_impl(jdg_engine *e, const jd_model *m, int max_batch);
-void jdg_launch_rope(jdg_engine *e, int l, int B);
+void jdg_launch_rope(jdg_engine *e, int l, int B, SplitPart sp = SplitPart{nullptr, 1, 1});
 void jdg_launch_attention(jdg_engine *e, int l, int B, float scale, float bias);
 int jdg_attn_setup(jdg_engine *e);
 void jdg_launch_pick(jdg_engine *e, int B);
 void jdg_launch_pick_tp(jdg_engine *e, int B, const float *v, const int *ix, int world);
 int jdg_engine_create(jdg_ctx *ctx, int kind, jdg_engine **out);
 void jdg_launch_elect(jdg_engine *e, int l, int B, const float *xin, const float *norm_w, const float *w_vote,
-                      const int *alive, float temperature, int host);
+                      const int *alive, float temperature, int host, SplitPart sp = SplitPart{nullptr, 1, 1});
 // host-model half (jdg_host.cu)
 int jdg_enqueue_host_step(jdg_engine *e, int B);
 int jdg_host_set_attrs(jdg_engine *e);

@@ -347,6 +347,22 @@ static __global__ __launch_bounds__(256) void k_sgemm(SgemmArgs a) {
 // RoPE on q and k heads of the fused qkv row, then append k and v to the cache at pos.
 // Own model: NeoX-half pairs from the alloc_run cache (janusdoe.c:536, 864-873, 893-897).
 // Host: NORM (2i,2i+1) or NEOX pairs (janusdoe.c:3198-3224).
+// Element (token t, column n) of the product: the ks partials loaded first, then added in
+// split order from zero (the arithmetic of the reduce kernel).
+__device__ __forceinline__ float split_sum(const SplitPart &sp, int t, int n) {
+    constexpr int kMaxSplitSum = kSplitMax;
+    const size_t tile = (size_t)(t / kSplitTile) * sp.rtiles + n / kSplitTile;
+    const float *p = sp.part + (tile * sp.ks * kSplitTile + t % kSplitTile) * kSplitTile + n % kSplitTile;
+    float v[kMaxSplitSum];
+#pragma unroll
+    for (int z = 0; z < kMaxSplitSum; z++) v[z] = z < sp.ks ? __ldcg(p + (size_t)z * kSplitTile * kSplitTile) : 0.f;
+    float s = 0.f;
+#pragma unroll
+    for (int z = 0; z < kMaxSplitSum; z++)
+        if (z < sp.ks) s = __fadd_rn(s, v[z]);
+    return s;
+}
+
 struct RopeArgs {
     float *qkv;
     int ld;          // row stride of qkv
@@ -358,6 +374,7 @@ struct RopeArgs {
     float *kc, *vc;  // layer base; slot b at + b*bstride, position t at + t*kd
     long bstride;
     int *err;
+    SplitPart sp;  // when set, q/k/v are summed from the product's split-K partials here
 };
 static __global__ void k_rope_kv(RopeArgs a) {
     const int b = blockIdx.x, p = a.pos[b];
@@ -375,7 +392,15 @@ static __global__ void k_rope_kv(RopeArgs a) {
         int h = idx / half, i = idx - h * half;
         int i0 = a.pair_norm ? 2 * i : i, i1 = a.pair_norm ? 2 * i + 1 : i + half;
         float *v = row + (size_t)h * a.HD;  // q heads then k heads are contiguous
-        float x0 = v[i0], x1 = v[i1], c = ct[i], s = st[i];
+        float x0, x1;
+        if (a.sp.part) {
+            x0 = split_sum(a.sp, b, h * a.HD + i0);
+            x1 = split_sum(a.sp, b, h * a.HD + i1);
+        } else {
+            x0 = v[i0];
+            x1 = v[i1];
+        }
+        const float c = ct[i], s = st[i];
         float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
         float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
         if (h < a.H) {
@@ -388,7 +413,7 @@ static __global__ void k_rope_kv(RopeArgs a) {
         }
     }
     const float *vsrc = row + qd + kd;
-    for (int i = threadIdx.x; i < kd; i += blockDim.x) vdst[i] = vsrc[i];
+    for (int i = threadIdx.x; i < kd; i += blockDim.x) vdst[i] = a.sp.part ? split_sum(a.sp, b, qd + kd + i) : vsrc[i];
 }
 
 // ------------------------------------------------------------------------------------
@@ -637,6 +662,10 @@ struct ElectArgs {
     float *pf_votes;       // [B][16]
     float *pf_cs;          // [B]
     float *pf_cons;        // the sequence's EMA of this layer (in: before the prompt, out: after)
+    // own model only: when sp is set, the residual is x + (Wo product summed from its split-K
+    // partials), written back to x_out before the norm
+    SplitPart sp;
+    float *x_out;
 };
 
 // The selection half of parliament_elect (janusdoe.c:811-837) / host_parliament_elect
@@ -707,7 +736,37 @@ static __global__ __launch_bounds__(256) void k_elect(ElectArgs a) {
     __shared__ float votes[kMaxE];
     const int b = blockIdx.x, D = a.D;
     const float *xr = a.x + (size_t)b * D;
-    if (!a.host) {
+    if (!a.host && a.sp.part) {
+        // x + Wo.att from the split-K partials (the reduce kernel's sum and residual add),
+        // kept in xs; elements tid, tid + blockDim, ... in order, four at a time
+        float ss = 0.f;
+        for (int base = 0; base < D; base += blockDim.x * 4) {
+            float xo[4], pv[4];
+#pragma unroll
+            for (int m = 0; m < 4; m++) {
+                const int i = base + threadIdx.x + blockDim.x * m;
+                xo[m] = i < D ? xr[i] : 0.f;
+                pv[m] = i < D ? split_sum(a.sp, b, i) : 0.f;
+            }
+#pragma unroll
+            for (int m = 0; m < 4; m++) {
+                const int i = base + threadIdx.x + blockDim.x * m;
+                if (i < D) {
+                    const float xn = __fadd_rn(xo[m], pv[m]);
+                    a.x_out[(size_t)b * D + i] = xn;
+                    xs[i] = xn;
+                    ss = fmaf(xn, xn, ss);
+                }
+            }
+        }
+        ss = block_sum(ss, red);
+        const float inv = 1.0f / sqrtf(ss / (float)D + a.eps);
+        for (int i = threadIdx.x; i < D; i += blockDim.x) {
+            const float v = __fmul_rn(__fmul_rn(xs[i], inv), a.norm_w[i]);
+            xs[i] = v;
+            a.xb[(size_t)b * D + i] = v;
+        }
+    } else if (!a.host) {
         // elements tid, tid + blockDim, ... in order, eight loads in flight
         float ss = 0.f;
         for (int base = 0; base < D; base += blockDim.x * 8) {

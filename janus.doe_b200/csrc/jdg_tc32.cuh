@@ -42,6 +42,7 @@ constexpr int kTcSmem = 1024 + kTcStages * kTcStageBytes;
 constexpr int kTcMaxSplit = 8;
 constexpr int kTcThreads = 352;                // warp 0 copies, warps 1 and 10 MMAs, warps 2-9 drain
 constexpr int kTcDrainCols = 64;               // token columns per drain warp (two warps per TMEM lane quarter)
+static_assert(kTcTok == kSplitTile && kTcRows == kSplitTile && kTcMaxSplit <= kSplitMax, "split_sum reads the partial tiles");
 constexpr int kTcRegions = 4;                  // accumulator regions of 128 TMEM columns
 // kind::tf32 instruction descriptor: D f32 (bits 4-5 = 1), A and B TF32 (bits 7-9, 10-12 = 2),
 // both K-major, M = 128 (bits 24-28 = M/16); N (bits 17-22 = N/8) is set per tile
